@@ -1,0 +1,134 @@
+"""Pin the CPU oracle to the reference implementation's own outputs.
+
+The fixtures under ``tests/golden/`` were produced by running the unmodified
+reference (chenxingqiang/SSA) with ``tests/golden/make_golden.py``.  These
+tests need no GPU.
+"""
+
+import os
+
+import numpy as np
+import pytest
+
+from oracle import ssa_oracle as O
+
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def _load(name):
+    return np.load(os.path.join(GOLD, name))
+
+
+def test_stage1_codes_match_reference():
+    z = _load("stage1.npz")
+    n, h_q, h_kv, d, d_s, n_c, a, b, k = z["dims"]
+    q_route, k_route = O.route_vectors(z["q"], z["k"], z["w_qr"], z["w_kr"])
+    qs = O.code_scores(q_route, z["codebook"])
+    np.testing.assert_allclose(qs, z["q_code_scores"], atol=2e-6)
+    q_codes = O.stable_topk(qs, a)
+    k_codes = O.stable_topk(O.code_scores(k_route, z["codebook"]), b)
+    np.testing.assert_array_equal(q_codes, z["top_q_codes"])
+    np.testing.assert_array_equal(k_codes, z["k_code_assign"])
+
+
+def test_candidate_mask_matches_reference():
+    z = _load("stage1.npz")
+    n, h_q, h_kv, d, d_s, n_c, a, b, k = z["dims"]
+    ref = np.unpackbits(z["candidate_mask"])[: n * h_kv * n].reshape(n, h_kv, n).astype(bool)
+    mine = O.candidate_mask_dense(z["top_q_codes"], z["k_code_assign"])
+    np.testing.assert_array_equal(mine, ref)
+    # the inverted-index restatement gives the same sets, causal-filtered
+    lists = O.candidate_lists(z["top_q_codes"], z["k_code_assign"], n_c, causal=True)
+    causal = np.tril(np.ones((n, n), dtype=bool))
+    for h in range(h_kv):
+        ptr, keys = lists[h]
+        for i in range(n):
+            expect = np.nonzero(ref[i, h] & causal[i])[0]
+            np.testing.assert_array_equal(keys[ptr[i]:ptr[i + 1]], expect)
+
+
+def test_topk_matches_reference_on_well_defined_rows():
+    z = _load("stage1.npz")
+    n, h_q, h_kv, d, d_s, n_c, a, b, k = z["dims"]
+    mine = O.select_topk_index(z["q"], z["k"], z["top_q_codes"], z["k_code_assign"], n_c, k,
+                               causal=True)
+    wd = z["well_defined"]
+    assert wd.sum() > 100
+    np.testing.assert_array_equal(mine[wd], z["indices"][wd])
+    dense = O.select_topk_dense(z["q"], z["k"], z["top_q_codes"], z["k_code_assign"], k,
+                                causal=True, q_block=32)
+    np.testing.assert_array_equal(dense, mine)
+
+
+@pytest.mark.parametrize("scale_key,scale", [("out", None), ("out_scale", 2.5)])
+def test_stage3_single_kv_head_matches_reference(scale_key, scale):
+    z = _load("stage3_h1.npz")
+    out = O.sparse_attention(z["q"], z["k"], z["v"], z["indices"], scale=scale, causal=False)
+    np.testing.assert_allclose(out, z[scale_key], rtol=1e-5, atol=1e-5)
+
+
+def test_stage3_gqa_gather_bug_is_pinned():
+    """At h_kv = 2 the raw reference follows its flattened row mapping; the
+    oracle's corrected per-head gather differs from it."""
+    z = _load("stage3_h2.npz")
+    raw = O.sparse_attention_reference_gather(z["q"], z["k"], z["v"], z["indices"])
+    np.testing.assert_allclose(raw, z["out"], rtol=1e-5, atol=1e-5)
+    fixed = O.sparse_attention(z["q"], z["k"], z["v"], z["indices"], causal=False)
+    assert np.abs(fixed - z["out"]).max() > 1e-2
+
+
+def test_dense_matches_reference():
+    z = _load("dense.npz")
+    out = O.dense_attention(z["q"], z["k"], z["v"], causal=True)
+    np.testing.assert_allclose(out, z["out"], rtol=1e-5, atol=1e-5)
+
+
+def _module_weights(z):
+    return {kname[3:].replace("__", "."): z[kname] for kname in z.files if kname.startswith("sd_")}
+
+
+def test_module_rope_quirk_and_output_match_reference():
+    z = _load("module.npz")
+    hs, h_q, h_kv, d, n, d_s, n_c, b, a, k = z["dims"]
+    w = _module_weights(z)
+    x = z["x"][0].astype(np.float64)
+    q = (x @ w["q_proj.weight"].T.astype(np.float64)).reshape(n, h_q, d)
+    kk = (x @ w["k_proj.weight"].T.astype(np.float64)).reshape(n, h_kv, d)
+    np.testing.assert_allclose(O.rope_reference(q, z["freqs"][:n]), z["q_rope"], atol=2e-5)
+    np.testing.assert_allclose(O.rope_reference(kk, z["freqs"][:n]), z["k_rope"], atol=2e-5)
+    y, idx = O.module_forward(z["x"], w, h_q, h_kv, d, n_c, a, b, k, freqs=z["freqs"])
+    rows = z["well_defined_rows"]
+    assert rows.sum() > 40
+    np.testing.assert_array_equal(idx[0][rows], z["indices"][rows])
+    np.testing.assert_allclose(y[0][rows], z["y"][0][rows], rtol=1e-4, atol=1e-5)
+
+
+def test_k_equals_n_reproduces_dense_causal():
+    rng = np.random.default_rng(5)
+    n, h_q, h_kv, d = 64, 6, 2, 16
+    q = rng.standard_normal((n, h_q, d))
+    k = rng.standard_normal((n, h_kv, d))
+    v = rng.standard_normal((n, h_kv, d))
+    w_qr = rng.standard_normal((8, d))
+    w_kr = rng.standard_normal((8, d))
+    cb = rng.standard_normal((h_kv, 32, 8))
+    idx = O.route(q, k, w_qr, w_kr, cb, a=4, b=2, top_k=n, causal=True)
+    for h in range(h_kv):
+        for i in range(n):
+            assert sorted(idx[i, h].tolist()) == list(range(n))
+    out = O.sparse_attention(q, k, v, idx, causal=True)
+    np.testing.assert_allclose(out, O.dense_attention(q, k, v, causal=True), atol=1e-12)
+
+
+def test_zero_padding_when_k_exceeds_n():
+    rng = np.random.default_rng(6)
+    n, h_q, h_kv, d = 10, 4, 2, 8
+    q = rng.standard_normal((n, h_q, d))
+    k = rng.standard_normal((n, h_kv, d))
+    idx = O.route(q, k, rng.standard_normal((4, d)), rng.standard_normal((4, d)),
+                  rng.standard_normal((h_kv, 8, 4)), a=2, b=2, top_k=16, causal=True)
+    assert idx.shape == (n, h_kv, 16)
+    assert (idx[:, :, n:] == 0).all()
+    for h in range(h_kv):
+        for i in range(n):
+            assert sorted(idx[i, h, :n].tolist()) == list(range(n))
