@@ -1,0 +1,368 @@
+"""SSA forward benchmark on B200: tokens/s of one forward pass of the hot path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--n 32768]
+
+Workload (BASELINE config 3 at its quoted point): batch 1, n = 32768,
+h_q = 32, h_kv = 8, d = 128, d_s = 32, N_c = 4096, a = 16, b = 4, k = 256,
+causal, bf16, planted-cluster synthetic inputs (seeded).  One step = the
+whole forward: the router (routing projection, codebook scoring with top-a /
+top-b, inverted index, candidate re-score + top-k) and the sparse exact
+attention over the selected keys.
+
+* ``value``: whole-job tokens/s with inputs resident in HBM, timed on the
+  device (CUDA events, barrier + synchronize on both sides, max over ranks).
+  Inputs (q 268 MB + k 67 MB + v 67 MB) exceed the 126 MB L2; no flush.
+* ``e2e``: the same forward through the public drop-in API
+  (``CodebookRouter`` -> ``sparse_exact_attention``) from pinned HOST
+  buffers: host->device copies of q/k/v and the device->host copy of the
+  output are inside the timed region.
+* ``roofline``: the sparse-attention kernel (the largest share of the step),
+  algorithmic bytes per launch / its CUDA-event duration, against the measured
+  HBM copy bandwidth.
+* ``cpu_baseline``: the reference algorithm (CPU oracle port, O(n^2) dense
+  re-score as the reference computes it) on a bounded sample, rank 0 only.
+
+Multi-GPU (torchrun, one process per GPU): each rank runs its own
+independent sequence (batch x KV-head units need no exchange) -> weak scaling.
+``--impl reference`` times the reference's CPU algorithm (oracle port) on the
+host cores instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "SSA fwd tokens/s per GPU (n=32k, k=256, bf16) and % of HBM/tensor roofline"
+UNIT = "tokens/s"
+LAUNCHES_PER_STEP = 12   # route: cb-normalize, 2x projection, 2x code select, index (count, 3x scan, scatter), rescore; attn: 1
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--n", type=int, default=32768)
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu", action="store_true")
+    return p.parse_args()
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            pk = json.load(f)
+        return float(pk["hbm_gbs"]), float(pk["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.f = None
+
+    def start(self):
+        try:
+            self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.flush()
+        rows = []
+        with open(self.f.name) as fh:
+            for line in fh:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.f.name)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        under = sorted(sm)[len(sm) // 2:] if sm else []
+        return {"sm_mhz": statistics.median(under) if under else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's algorithm (oracle port), bounded sample
+# ---------------------------------------------------------------------------
+def cpu_sample(t_cpu, shape, rows=256):
+    """Times one KV head of the reference algorithm on the host: key codes for
+    all n keys, then query codes, the dense O(n) re-score per query (the
+    reference's full [rows, g, n] logits + candidate mask + top-k) and stage 3
+    for the last ``rows`` query rows.  Returns (tokens/s estimate, seconds, text)."""
+    import numpy as np
+    from oracle import ssa_oracle as O
+
+    q, k, v, w_qr, w_kr, cb = t_cpu
+    n, g = shape.n, shape.h_q // shape.h_kv
+    h = 0
+    i0 = n - rows
+    qh = q[i0:, h * g:(h + 1) * g]
+    kh = k[:, h:h + 1]
+    vh = v[:, h:h + 1]
+    t0 = time.perf_counter()
+    _, k_route = O.route_vectors(kh[:1].repeat(g, axis=1), kh, w_qr, w_kr, dtype=np.float32)
+    k_codes = O.stable_topk(O.code_scores(k_route, cb[h:h + 1], dtype=np.float32), shape.b)
+    t1 = time.perf_counter()
+    q_route, _ = O.route_vectors(qh, kh[:rows], w_qr, w_kr, dtype=np.float32)
+    q_codes = O.stable_topk(O.code_scores(q_route, cb[h:h + 1], dtype=np.float32), shape.a)
+    idx = O.select_topk_dense(qh, kh, q_codes, k_codes, shape.top_k, causal=True, dtype=np.float32,
+                              q_block=64, q_start=i0)
+    O.sparse_attention(qh, kh, vh, idx, causal=True, q_offset=i0, dtype=np.float32)
+    t2 = time.perf_counter()
+    per_head = (t1 - t0) + (t2 - t1) * (n / rows)
+    seconds = per_head * shape.h_kv
+    sample = (f"1 of {shape.h_kv} KV heads: key codes for all {n} keys + last {rows} queries "
+              f"(codes, dense re-score over {n} keys, top-{shape.top_k}, attention), fp32, "
+              f"extrapolated x{n // rows} rows x{shape.h_kv} heads")
+    return n / seconds, t2 - t0, sample
+
+
+def cpu_inputs(shape, seed):
+    import numpy as np
+    import torch
+    from ssa_b200 import workloads as W
+
+    t = W.make_inputs(shape, seed=seed, dtype=torch.bfloat16, device="cpu")
+    f = lambda x: x[0].float().numpy() if x.dim() == 4 else x.float().numpy()
+    return f(t["q"]), f(t["k"]), f(t["v"]), t["w_qr"].numpy(), t["w_kr"].numpy(), t["codebook"].numpy()
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return 0
+    import torch
+    from ssa_b200 import workloads as W
+
+    shape = W.Shape(**{**W.CONFIG3.asdict(), "n": args.n})
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    t_cpu = cpu_inputs(shape, args.seed)
+    vals, secs = [], []
+    for it in range(args.warmup + args.steps):
+        v, s, sample = cpu_sample(t_cpu, shape, rows=128)
+        if it >= args.warmup:
+            vals.append(v)
+            secs.append(s)
+    value = statistics.median(vals)
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * shape.n / value,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded planted-cluster config-3 inputs)",
+            "config": {"workload": "config3", **shape.asdict()},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": sample, "sample_seconds": statistics.median(secs)},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from ssa_b200 import _lib as L
+    from ssa_b200 import ops
+    from ssa_b200 import workloads as W
+    import ssa_b200 as ssa
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    shape = W.Shape(**{**W.CONFIG3.asdict(), "n": args.n})
+    t = W.make_inputs(shape, seed=args.seed + rank, dtype=torch.bfloat16, device=dev)
+    q, k, v = t["q"], t["k"], t["v"]
+    n, hq, hkv, d, kk = shape.n, shape.h_q, shape.h_kv, shape.d, shape.top_k
+    lib = L.lib()
+
+    # preallocated outputs + workspace; calls go straight through the C ABI
+    idx = torch.empty((1, n, hkv, kk), dtype=torch.int32, device=dev)
+    out = torch.empty_like(q)
+    w_qr, w_kr, cb = t["w_qr"].contiguous(), t["w_kr"].contiguous(), t["codebook"].contiguous()
+    rargs = ops.route_args(q, k, w_qr, w_kr, cb, shape.a, shape.b, kk, True, 1.0, 0, idx, False)
+    ws = ops.workspace(rargs, dev)
+    aargs = ops.attn_args(q, k, v, idx, out, math.sqrt(d), True, 0)
+    stream = torch.cuda.current_stream(dev)
+    sptr = stream.cuda_stream
+
+    def step(ev=None):
+        if ev is not None:
+            ev[0].record(stream)
+        L.check("ssa_route", lib.ssa_route(ctypes.byref(rargs), ws.data_ptr(), ws.numel(), sptr))
+        if ev is not None:
+            ev[1].record(stream)
+        L.check("ssa_sparse_attn", lib.ssa_sparse_attn(ctypes.byref(aargs), sptr))
+        if ev is not None:
+            ev[2].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    clocks = ClockSampler(local)
+    clocks.start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for s in range(args.steps):
+        step(evs[s])
+    t_end.record(stream)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    total_ms = t_start.elapsed_time(t_end)
+    route_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    attn_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    if world > 1:
+        tt = torch.tensor([total_ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        total_ms = float(tt.item())
+    ms_step = total_ms / args.steps
+    value = world * n / (ms_step / 1e3)
+
+    # roofline of the sparse-attention kernel (one launch per step)
+    hbm, tflops, peak_kind = load_peaks()
+    units = n * hkv
+    attn_bytes = units * kk * (2 * d * 2) + 2 * n * hq * d * 2 + units * kk * 4
+    achieved = attn_bytes / (attn_ms / 1e3) / 1e9
+    traffic = os.environ.get("SSA_ATTN_DRAM_BYTES")
+    roof = {"kernel": "sparse_attn_kernel", "bound": "hbm", "achieved": achieved, "peak": hbm,
+            "unit": "GB/s", "frac": achieved / hbm, "peak_kind": peak_kind,
+            "traffic": float(traffic) if traffic else None,
+            "algorithmic_bytes_per_launch": attn_bytes, "launch_ms": attn_ms,
+            "router_ms": route_ms}
+
+    # e2e through the public API from pinned host buffers
+    e2e = None
+    if not args.no_e2e:
+        os.environ.setdefault("SSA_CHECKED", "0")
+        router = ssa.CodebookRouter(head_dim=d, route_dim=shape.d_s, num_kv_heads=hkv,
+                                    num_codebook=shape.n_codes, codes_per_key=shape.b,
+                                    codes_per_query=shape.a, top_k=kk).to(dev)
+        with torch.no_grad():
+            router.W_qr.weight.copy_(w_qr)
+            router.W_kr.weight.copy_(w_kr)
+            router.codebook.copy_(cb)
+        hq_, hk_, hv_ = (x[0].cpu().pin_memory() for x in (q, k, v))
+        hout = torch.empty(hq_.shape, dtype=hq_.dtype).pin_memory()
+
+        def e2e_step():
+            dq = hq_.to(dev, non_blocking=True)
+            dk = hk_.to(dev, non_blocking=True)
+            dv = hv_.to(dev, non_blocking=True)
+            with torch.no_grad():
+                ind = router(dq, dk, causal=True)
+                o = ssa.sparse_exact_attention(dq, dk, dv, ind, is_causal=True)
+            hout.copy_(o, non_blocking=True)
+
+        for _ in range(max(3, args.warmup)):
+            e2e_step()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        e_ms = e0.elapsed_time(e1)
+        if world > 1:
+            tt = torch.tensor([e_ms], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            e_ms = float(tt.item())
+        e2e = {"value": world * n / (e_ms / args.steps / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": sum(x.numel() * x.element_size() for x in (hq_, hk_, hv_)),
+               "d2h_bytes_per_step": hout.numel() * hout.element_size(),
+               "ms_per_step": e_ms / args.steps, "api": "CodebookRouter.forward + sparse_exact_attention"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cores = os.cpu_count() or 1
+        torch.set_num_threads(cores)
+        cv, cs, sample = cpu_sample(cpu_inputs(shape, args.seed), shape, rows=128)
+        cpu = {"value": cv, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample,
+               "sample_seconds": cs}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (seeded: Q/K ~ N(0,1), 5% planted keys around 64 centroids, V ~ N(0,1))",
+                "config": {"workload": "config3 (op-level sweep at n=32768)", **shape.asdict(),
+                           "per_rank": "one independent sequence per GPU",
+                           "l2": "inputs 403 MB > 126 MB L2, no flush",
+                           "parallelism": f"batch-units x{world}"},
+                "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
+                "gpu_launches": LAUNCHES_PER_STEP * args.steps}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,169 @@
+/*
+ * ssa_b200.h -- C ABI of libssa_sm100a.so, the B200 (sm_100a) implementation
+ * of the SSA forward hot path: CodebookRouter (stages 1-2) and
+ * sparse_exact_attention (stage 3) of chenxingqiang/SSA.
+ *
+ * Conventions
+ *  - Every pointer in an args struct is a DEVICE pointer on the current CUDA
+ *    device; sizes are element counts; strides are in ELEMENTS and the last
+ *    (feature) dimension of every tensor must be contiguous.
+ *  - The library never allocates device memory.  Scratch space is passed in
+ *    as `workspace` (size from ssa_route_workspace_size()).
+ *  - Every kernel is launched on the given stream; calls are asynchronous.
+ *    Argument errors are reported synchronously through the return code.
+ *    Data-dependent errors found on the device (an index outside [0, n))
+ *    are OR-ed into the optional `status` word, which the caller reads after
+ *    synchronising (SSA_DEVICE_* bits).
+ *  - Inputs are never written.  Outputs are fully overwritten.
+ *
+ * Reference interfaces replaced (file:line in chenxingqiang/SSA):
+ *  - ssa_route             CodebookRouter.forward            ssa/router.py:73-149
+ *                          (+ _select_candidates / _build_candidate_mask,
+ *                             ssa/router.py:151-259)
+ *  - ssa_code_assign       CodebookRouter.get_code_assignment ssa/router.py:261-275
+ *  - ssa_sparse_attn       sparse_exact_attention            ssa/attention.py:12-115
+ *  - ssa_select_from_scores, ssa_build_index, ssa_select_candidates
+ *                          test hooks exposing the stage-1 selection
+ *                          (ssa/router.py:129-141), the code->key index and the
+ *                          candidate re-score/top-k (ssa/router.py:151-214)
+ *                          on caller-provided inputs, for bit-exact parity
+ *                          tests.  No reference counterpart of their own.
+ */
+#ifndef SSA_B200_H_
+#define SSA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  SSA_OK = 0,
+  SSA_ERR_INVALID_ARG = 1,   /* null pointer, negative size, bad stride      */
+  SSA_ERR_UNSUPPORTED = 2,   /* a size outside the supported envelope        */
+  SSA_ERR_WORKSPACE = 3,     /* workspace missing or too small               */
+  SSA_ERR_ALIGNMENT = 4,     /* pointer/stride not 16-byte aligned           */
+  SSA_ERR_CUDA = 5,          /* a CUDA launch failed                         */
+  SSA_ERR_DEVICE = 6         /* device error word non-zero (ssa_read_status) */
+} ssa_status;
+
+/* Bits OR-ed into a device status word. */
+#define SSA_DEVICE_INDEX_OOB 0x1 /* sparse_attn: an index < 0 or >= n was skipped */
+
+typedef enum { SSA_F32 = 0, SSA_BF16 = 1, SSA_F16 = 2 } ssa_dtype;
+typedef enum { SSA_I32 = 0, SSA_I64 = 1 } ssa_index_dtype;
+
+/* ------------------------------------------------------------------------ */
+/* Router (stages 1-2)                                                       */
+/* ------------------------------------------------------------------------ */
+typedef struct {
+  /* sizes */
+  int32_t batch;        /* independent sequences                              */
+  int32_t n;            /* keys per sequence (seq_len)                        */
+  int32_t n_q;          /* query rows per sequence (== n unless sharded)      */
+  int32_t q_offset;     /* sequence position of query row 0 (query shard)     */
+  int32_t h_q, h_kv;    /* h_q % h_kv == 0                                    */
+  int32_t d;            /* head_dim                                           */
+  int32_t d_s;          /* route_dim                                          */
+  int32_t n_codes;      /* num_codebook                                       */
+  int32_t a;            /* codes_per_query                                    */
+  int32_t b;            /* codes_per_key                                      */
+  int32_t top_k;        /* k                                                  */
+  int32_t causal;       /* 1: keys j <= q_offset + i only                     */
+  float temperature;    /* > 0; scores are divided by it (order-neutral)      */
+  ssa_dtype dtype;      /* dtype of q and k                                   */
+  ssa_dtype w_dtype;    /* dtype of w_qr, w_kr and codebook                   */
+  int32_t codebook_heads; /* 1 (shared [N_c,d_s]) or h_kv ([h_kv,N_c,d_s])    */
+  /* inputs */
+  const void* q;  int64_t q_stride_b, q_stride_n, q_stride_h; /* [B,n_q,h_q,d] */
+  const void* k;  int64_t k_stride_b, k_stride_n, k_stride_h; /* [B,n,h_kv,d]  */
+  const void* w_qr;      /* [d_s, d] contiguous (nn.Linear weight)            */
+  const void* w_kr;      /* [d_s, d] contiguous                               */
+  const void* codebook;  /* [codebook_heads, n_codes, d_s] contiguous         */
+  /* outputs */
+  void* indices;                 /* [B, n_q, h_kv, top_k] contiguous          */
+  ssa_index_dtype index_dtype;
+  int32_t* q_codes;              /* optional [B, n_q, h_kv, a] contiguous     */
+  int32_t* k_codes;              /* optional [B, n, h_kv, b] contiguous       */
+  int32_t* cand_counts;          /* optional [B, n_q, h_kv]: unique candidates */
+} SsaRouteArgs;
+
+/* Bytes of workspace ssa_route / ssa_code_assign need for these args. */
+size_t ssa_route_workspace_size(const SsaRouteArgs* args);
+
+/* CodebookRouter.forward(q, k, causal_mask, hard=True) -> indices
+ * (ssa/router.py:73-149).  Canonical semantics: candidates are the keys that
+ * share one of the query's top-a codes with their own top-b codes (and j <= i
+ * when causal); they are ranked by the group-mean logit mean_g(q_g.k_j)/sqrt(d)
+ * with the lower key index first among equal scores; fewer than min(k, n)
+ * candidates are followed by the lowest-index non-candidate keys; k > n
+ * is zero-padded (ssa/router.py:203-211). */
+ssa_status ssa_route(const SsaRouteArgs* args, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+/* CodebookRouter.get_code_assignment(k) -> [B, n, h_kv, b] codes
+ * (ssa/router.py:261-275).  Uses the k / w_kr / codebook fields of args and
+ * writes args->k_codes (required). */
+ssa_status ssa_code_assign(const SsaRouteArgs* args, void* workspace, size_t workspace_bytes,
+                           void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Sparse exact attention (stage 3)                                          */
+/* ------------------------------------------------------------------------ */
+typedef struct {
+  int32_t batch, n_q, n;      /* query rows, keys per sequence                */
+  int32_t q_offset;           /* sequence position of query row 0             */
+  int32_t h_q, h_kv, d, top_k;
+  int32_t causal;             /* 1: mask keys j > q_offset + i                */
+  float scale;                /* logits = (q . k) / scale  (ssa/attention.py:37-38,107) */
+  ssa_dtype dtype;            /* q, k, v and out                              */
+  const void* q; int64_t q_stride_b, q_stride_n, q_stride_h;        /* [B,n_q,h_q,d]   */
+  const void* k; int64_t k_stride_b, k_stride_n, k_stride_h;        /* [B,n,h_kv,d]    */
+  const void* v; int64_t v_stride_b, v_stride_n, v_stride_h;        /* [B,n,h_kv,d]    */
+  const void* indices; ssa_index_dtype index_dtype;
+  int64_t idx_stride_b, idx_stride_n, idx_stride_h;                 /* [B,n_q,h_kv,k]  */
+  void* out; int64_t out_stride_b, out_stride_n, out_stride_h;      /* [B,n_q,h_q,d]   */
+  int32_t* status;            /* optional device word, SSA_DEVICE_* bits      */
+} SsaAttnArgs;
+
+/* sparse_exact_attention(q, k, v, indices, scale) (ssa/attention.py:12-115)
+ * with the per-KV-head gather k[idx, h].  Online softmax in fp32. */
+ssa_status ssa_sparse_attn(const SsaAttnArgs* args, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Test hooks (bit-exact parity on caller-provided inputs)                   */
+/* ------------------------------------------------------------------------ */
+
+/* Top-`kk` of each row of fp32 `scores [rows, n_cols]`: indices sorted by
+ * score descending, lower column first among equal scores; -0.0 == +0.0.
+ * Runs the same selection code the fused scoring kernel uses
+ * (ssa/router.py:130,141).  kk <= 32. */
+ssa_status ssa_select_from_scores(const float* scores, int64_t rows, int32_t n_cols,
+                                  int32_t kk, int32_t* out_idx, void* stream);
+
+/* Code->key inverted index of k_codes [B, n, h_kv, b] (int32, contiguous):
+ * bucket_ptr [B, h_kv, n_codes+1] and bucket_keys [B, h_kv, n*b] (keys
+ * ascending within a bucket).  Workspace from ssa_route_workspace_size(). */
+ssa_status ssa_build_index(const SsaRouteArgs* args, const int32_t* k_codes,
+                           int32_t* bucket_ptr, int32_t* bucket_keys,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
+/* Stage 2 from given codes: candidate union, causal filter, group-mean
+ * re-score, top-k, filler and padding -- ssa_route without stage 1.
+ * Reads args->q, args->k, args->q_codes, args->k_codes; writes
+ * args->indices (and cand_counts if set). */
+ssa_status ssa_select_candidates(const SsaRouteArgs* args, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
+/* Human-readable text of a status code. */
+const char* ssa_status_str(ssa_status s);
+
+/* Text describing the last argument error of this thread (or ""). */
+const char* ssa_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SSA_B200_H_ */

@@ -113,7 +113,9 @@ def code_scores(route, codebook, temperature=1.0, dtype=np.float64):
     h_kv = route.shape[1]
     cb = l2_normalize(np.asarray(_codebook_per_head(codebook, h_kv), dtype=dtype))
     rn = l2_normalize(route)
-    s = np.einsum("shd,hcd->shc", rn, cb)
+    s = np.empty(rn.shape[:2] + (cb.shape[1],), dtype=np.result_type(rn, cb))
+    for h in range(h_kv):                                   # [n, d_s] @ [d_s, N_c] per head
+        s[:, h, :] = np.ascontiguousarray(rn[:, h, :]) @ cb[h].T
     return s / temperature
 
 
@@ -124,8 +126,26 @@ def stable_topk(scores: np.ndarray, kk: int) -> np.ndarray:
     Restates ``Tensor.topk`` (ssa/router.py:130,141,204) with the oracle's
     canonical tie rule.  ``-0.0`` and ``+0.0`` compare equal.
     """
-    order = np.argsort(-scores, axis=-1, kind="stable")
-    return order[..., :kk]
+    scores = np.asarray(scores)
+    n = scores.shape[-1]
+    if kk >= n or n <= 64:
+        order = np.argsort(-scores, axis=-1, kind="stable")
+        return order[..., :kk]
+    # threshold = kk-th largest value; keep every value above it and the
+    # lowest-index values equal to it, then order the kk survivors.
+    thr = np.partition(scores, n - kk, axis=-1)[..., n - kk:n - kk + 1]
+    sel = (scores >= thr).reshape(-1, n)
+    over = np.nonzero(sel.sum(axis=-1) > kk)[0]          # rows with ties across the threshold
+    if over.size:
+        s2 = scores.reshape(-1, n)[over]
+        t2 = thr.reshape(-1, 1)[over]
+        gt, eq = s2 > t2, s2 == t2
+        need = kk - gt.sum(axis=-1, keepdims=True)
+        sel[over] = gt | (eq & (np.cumsum(eq, axis=-1) <= need))
+    cols = np.nonzero(sel)[1].reshape(scores.shape[:-1] + (kk,))
+    vals = np.take_along_axis(scores, cols, axis=-1)
+    order = np.argsort(-vals, axis=-1, kind="stable")     # cols ascend, so ties keep index order
+    return np.take_along_axis(cols, order, axis=-1)
 
 
 def route_codes(q, k, w_qr, w_kr, codebook, a, b, temperature=1.0, dtype=np.float64):
@@ -259,33 +279,40 @@ def select_topk_index(q, k, q_codes, k_codes, n_codes, top_k, causal=True,
 
 
 def select_topk_dense(q, k, q_codes, k_codes, top_k, causal=True, dtype=np.float64,
-                      q_block=None):
+                      q_block=None, q_start=0):
     """Stage 2 as the reference computes it (ssa/router.py:170-214): the full
     ``[n, h_kv, g, n]`` logits, causal ``-inf``, group mean, candidate-mask
     ``-inf``, top-k over all ``n`` keys -- with the stable tie rule, which
     makes the ``-inf`` filler the lowest-index non-candidates.
 
-    O(n^2) per head, processed in query blocks of ``q_block`` rows.  This is
-    the CPU baseline's algorithm (the reference's own), and a cross-check of
-    :func:`select_topk_index`."""
-    n, h_q, d = q.shape
-    h_kv = k.shape[1]
+    O(n^2) per head, processed in query blocks of ``q_block`` rows.  ``q``
+    (and ``q_codes``) may hold a block of query rows at sequence positions
+    ``q_start, q_start+1, ...`` (used by the CPU baseline's bounded sample).
+    This is the CPU baseline's algorithm (the reference's own), and a
+    cross-check of :func:`select_topk_index`."""
+    n_q, h_q, d = q.shape
+    n, h_kv = k.shape[0], k.shape[1]
     g = h_q // h_kv
     eff = min(top_k, n)
-    out = np.zeros((n, h_kv, top_k), dtype=np.int64)
-    qb = q_block or n
+    n_codes = int(max(np.max(q_codes), np.max(k_codes))) + 1
+    out = np.zeros((n_q, h_kv, top_k), dtype=np.int64)
+    qb = q_block or n_q
     jj = np.arange(n)
     for h in range(h_kv):
-        qh = np.asarray(q[:, h * g:(h + 1) * g, :], dtype=dtype)     # [n, g, d]
+        qh = np.asarray(q[:, h * g:(h + 1) * g, :], dtype=dtype)     # [n_q, g, d]
         kh = np.asarray(k[:, h, :], dtype=dtype)                       # [n, d]
         kc = k_codes[:, h, :]
-        for i0 in range(0, n, qb):
-            i1 = min(i0 + qb, n)
-            full = np.einsum("sgd,td->sgt", qh[i0:i1], kh) / np.sqrt(d)   # [blk, g, n]
+        for i0 in range(0, n_q, qb):
+            i1 = min(i0 + qb, n_q)
+            full = (qh[i0:i1].reshape(-1, d) @ kh.T).reshape(i1 - i0, g, n) / np.sqrt(d)
             sc = full.mean(axis=1)                                      # [blk, n]
             if causal:
-                sc[jj[None, :] > np.arange(i0, i1)[:, None]] = -np.inf
-            cm = (q_codes[i0:i1, h, :, None, None] == kc[None, None, :, :]).any(axis=(1, 3))
+                sc[jj[None, :] > (q_start + np.arange(i0, i1))[:, None]] = -np.inf
+            # mask[i, j] = any(q_codes[i] == k_codes[j]) via a per-query code-membership row
+            member = np.zeros((i1 - i0, n_codes), dtype=bool)
+            np.put_along_axis(member, q_codes[i0:i1, h, :].astype(np.int64), True, axis=1)
+            cm = np.take_along_axis(member, np.broadcast_to(kc.reshape(1, -1), (i1 - i0, kc.size)),
+                                    axis=1).reshape(i1 - i0, n, -1).any(axis=2)
             sc[~cm] = -np.inf
             out[i0:i1, h, :eff] = stable_topk(sc, eff)
     return out
@@ -306,12 +333,12 @@ def route(q, k, w_qr, w_kr, codebook, a, b, top_k, causal=True, temperature=1.0,
 # ---------------------------------------------------------------------------
 
 def _softmax_attend(q_grouped, k_sel, v_sel, valid, scale):
-    logits = np.einsum("nhgd,nhkd->nhgk", q_grouped, k_sel) / scale
+    logits = np.matmul(q_grouped, np.swapaxes(k_sel, -1, -2)) / scale         # [n, h, g, kk]
     logits = np.where(valid[:, :, None, :], logits, -np.inf)
     m = logits.max(axis=-1, keepdims=True)
     p = np.exp(logits - m)
     p /= p.sum(axis=-1, keepdims=True)
-    return np.einsum("nhgk,nhkd->nhgd", p, v_sel)
+    return np.matmul(p, v_sel)
 
 
 def sparse_attention(q, k, v, indices, scale=None, causal=False, dtype=np.float64,
@@ -373,13 +400,13 @@ def dense_attention(q, k, v, causal=True, scale=None, dtype=np.float64):
         scale = np.sqrt(d)
     ke = np.repeat(k, g, axis=1)
     ve = np.repeat(v, g, axis=1)
-    logits = np.einsum("shd,thd->sht", q, ke) / scale
+    logits = np.matmul(q.transpose(1, 0, 2), ke.transpose(1, 2, 0)).transpose(1, 0, 2) / scale
     if causal:
         logits = np.where(np.tril(np.ones((n, n), dtype=bool))[:, None, :], logits, -np.inf)
     m = logits.max(axis=-1, keepdims=True)
     p = np.exp(logits - m)
     p /= p.sum(axis=-1, keepdims=True)
-    return np.einsum("sht,thd->shd", p, ve)
+    return np.matmul(p.transpose(1, 0, 2), ve.transpose(1, 0, 2)).transpose(1, 0, 2)
 
 
 # ---------------------------------------------------------------------------

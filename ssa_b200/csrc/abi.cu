@@ -1,0 +1,327 @@
+// C-ABI entry points of libssa_sm100a.so (declared in include/ssa_b200.h).
+//
+// This layer validates arguments, lays out the caller's workspace and
+// launches the stage kernels on the caller's stream.  It never allocates.
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+ssa_status fail(ssa_status s, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+ssa_status fail(ssa_status s, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return s;
+}
+
+ssa_status cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return SSA_OK;
+  return fail(SSA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+size_t elem_size(ssa_dtype t) { return t == SSA_F32 ? 4 : 2; }
+bool valid_dtype(ssa_dtype t) { return t == SSA_F32 || t == SSA_BF16 || t == SSA_F16; }
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+bool stride16(int64_t s, ssa_dtype t) { return (s * static_cast<int64_t>(elem_size(t))) % 16 == 0; }
+
+constexpr size_t kAlign = 256;
+size_t round_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+constexpr int kMaxCap = 16384;   // shared-memory candidate capacity limit
+
+int rescore_cap(int k_eff) {
+  int cap = 2048;
+  while (cap < k_eff) cap <<= 1;
+  return cap;
+}
+
+// Workspace regions for a route call.
+struct RouteLayout {
+  size_t q_route, k_route, cb_norm, q_codes, k_codes, counts, partials, bucket_ptr, bucket_keys;
+  size_t total;
+  int tiles;
+  int64_t chunks;
+};
+
+RouteLayout route_layout(const SsaRouteArgs& a) {
+  RouteLayout L{};
+  const int64_t B = a.batch, hk = a.h_kv;
+  size_t off = 0;
+  auto take = [&](size_t bytes) { size_t at = off; off += round_up(bytes); return at; };
+  L.q_route = take(static_cast<size_t>(B * hk * a.n_q * a.d_s) * 4);
+  L.k_route = take(static_cast<size_t>(B * hk * a.n * a.d_s) * 4);
+  L.cb_norm = take(static_cast<size_t>(a.codebook_heads) * a.n_codes * a.d_s * 4);
+  L.q_codes = take(static_cast<size_t>(B * a.n_q * hk * a.a) * 4);
+  L.k_codes = take(static_cast<size_t>(B * a.n * hk * a.b) * 4);
+  const int tile_keys = a.b > 0 ? ssa::index_tile_keys(a.b) : 1;
+  L.tiles = static_cast<int>(ssa::cdiv(a.n, tile_keys));
+  L.chunks = ssa::cdiv(static_cast<int64_t>(a.n_codes) * L.tiles, ssa::kScanChunk);
+  L.counts = take(static_cast<size_t>(B * hk) * a.n_codes * L.tiles * 4);
+  L.partials = take(static_cast<size_t>(B * hk * L.chunks) * 4);
+  L.bucket_ptr = take(static_cast<size_t>(B * hk) * (a.n_codes + 1) * 4);
+  L.bucket_keys = take(static_cast<size_t>(B * hk) * a.n * a.b * 4);
+  L.total = off;
+  return L;
+}
+
+// Validation shared by the router entry points.  `need_q` is false for
+// get_code_assignment, which reads only k.
+ssa_status check_route(const SsaRouteArgs* a, bool need_q, bool need_stage2) {
+  if (!a) return fail(SSA_ERR_INVALID_ARG, "args is NULL");
+  if (a->batch < 0 || a->n < 1 || a->n_q < 0 || a->q_offset < 0)
+    return fail(SSA_ERR_INVALID_ARG, "bad sizes batch=%d n=%d n_q=%d q_offset=%d", a->batch, a->n,
+                a->n_q, a->q_offset);
+  if (a->h_kv < 1 || a->h_q < 1 || a->h_q % a->h_kv != 0)
+    return fail(SSA_ERR_INVALID_ARG, "num_q_heads (%d) must be a multiple of num_kv_heads (%d)",
+                a->h_q, a->h_kv);
+  if (a->d < 8 || a->d > 256 || a->d % 8 != 0)
+    return fail(SSA_ERR_UNSUPPORTED, "head_dim %d: need a multiple of 8 in [8, 256]", a->d);
+  if (!(a->d_s == 4 || a->d_s == 8 || a->d_s == 16 || a->d_s == 32 || a->d_s == 64))
+    return fail(SSA_ERR_UNSUPPORTED, "route_dim %d: need 4, 8, 16, 32 or 64", a->d_s);
+  if (a->n_codes < 1 || a->n_codes > 32767)
+    return fail(SSA_ERR_UNSUPPORTED, "num_codebook %d: need 1..32767", a->n_codes);
+  if (a->b < 1 || a->b > 32 || a->b > a->n_codes)
+    return fail(SSA_ERR_UNSUPPORTED, "codes_per_key %d: need 1..min(32, num_codebook)", a->b);
+  if (need_q && (a->a < 1 || a->a > 32 || a->a > a->n_codes))
+    return fail(SSA_ERR_UNSUPPORTED, "codes_per_query %d: need 1..min(32, num_codebook)", a->a);
+  if (need_stage2) {
+    if (a->top_k < 1) return fail(SSA_ERR_INVALID_ARG, "top_k %d < 1", a->top_k);
+    if (std::min(a->top_k, a->n) > kMaxCap)
+      return fail(SSA_ERR_UNSUPPORTED, "min(top_k, n) = %d exceeds %d", std::min(a->top_k, a->n), kMaxCap);
+    if (!a->indices) return fail(SSA_ERR_INVALID_ARG, "indices is NULL");
+    if (a->index_dtype != SSA_I32 && a->index_dtype != SSA_I64)
+      return fail(SSA_ERR_INVALID_ARG, "bad index dtype");
+    if (static_cast<int64_t>(a->q_offset) + a->n_q > a->n)
+      return fail(SSA_ERR_INVALID_ARG, "q_offset + n_q (%d + %d) exceeds n (%d)", a->q_offset, a->n_q, a->n);
+  }
+  if (static_cast<int64_t>(a->n) * a->b >= (1ll << 31))
+    return fail(SSA_ERR_UNSUPPORTED, "n * codes_per_key must be < 2^31");
+  if (!(a->temperature > 0.f)) return fail(SSA_ERR_INVALID_ARG, "temperature must be > 0");
+  if (!valid_dtype(a->dtype) || !valid_dtype(a->w_dtype))
+    return fail(SSA_ERR_INVALID_ARG, "bad dtype");
+  if (a->codebook_heads != 1 && a->codebook_heads != a->h_kv)
+    return fail(SSA_ERR_INVALID_ARG, "codebook_heads %d must be 1 or num_kv_heads", a->codebook_heads);
+  if (!a->k || !a->w_kr || !a->codebook) return fail(SSA_ERR_INVALID_ARG, "k / w_kr / codebook is NULL");
+  if (need_q && (!a->q || !a->w_qr)) return fail(SSA_ERR_INVALID_ARG, "q / w_qr is NULL");
+  if (!aligned16(a->k) || !stride16(a->k_stride_n, a->dtype) || !stride16(a->k_stride_h, a->dtype) ||
+      !stride16(a->k_stride_b, a->dtype))
+    return fail(SSA_ERR_ALIGNMENT, "k must be 16-byte aligned with 16-byte strides");
+  if (need_q && (!aligned16(a->q) || !stride16(a->q_stride_n, a->dtype) ||
+                 !stride16(a->q_stride_h, a->dtype) || !stride16(a->q_stride_b, a->dtype)))
+    return fail(SSA_ERR_ALIGNMENT, "q must be 16-byte aligned with 16-byte strides");
+  return SSA_OK;
+}
+
+template <typename T>
+T* at(void* ws, size_t off) { return reinterpret_cast<T*>(static_cast<char*>(ws) + off); }
+
+ssa_status run_stage1(const SsaRouteArgs& a, const RouteLayout& L, void* ws, cudaStream_t st,
+                      bool queries, int32_t* q_codes, int32_t* k_codes) {
+  using namespace ssa;
+  cudaError_t e = launch_codebook_normalize(a.codebook, a.w_dtype, at<float>(ws, L.cb_norm),
+                                            static_cast<int64_t>(a.codebook_heads) * a.n_codes, a.d_s, st);
+  if (e != cudaSuccess) return cuda_status(e, "codebook_normalize");
+  // keys
+  RouteProjectParams kp{a.k, a.k_stride_b, a.k_stride_n, a.k_stride_h, a.w_kr,
+                        at<float>(ws, L.k_route), static_cast<int64_t>(a.batch) * a.h_kv * a.n, a.n,
+                        a.h_kv, 1, a.d, a.d_s};
+  e = launch_route_project(kp, a.dtype, a.w_dtype, st);
+  if (e != cudaSuccess) return cuda_status(e, "route_project(k)");
+  CodeSelectParams ks{at<float>(ws, L.k_route), at<float>(ws, L.cb_norm), k_codes,
+                      static_cast<int64_t>(a.batch) * a.h_kv, a.n, a.h_kv, a.codebook_heads,
+                      a.n_codes, a.d_s, a.b, a.temperature};
+  e = launch_code_select(ks, st);
+  if (e != cudaSuccess) return cuda_status(e, "code_select(k)");
+  if (queries && a.n_q > 0) {
+    RouteProjectParams qp{a.q, a.q_stride_b, a.q_stride_n, a.q_stride_h, a.w_qr,
+                          at<float>(ws, L.q_route), static_cast<int64_t>(a.batch) * a.h_kv * a.n_q,
+                          a.n_q, a.h_kv, a.h_q / a.h_kv, a.d, a.d_s};
+    e = launch_route_project(qp, a.dtype, a.w_dtype, st);
+    if (e != cudaSuccess) return cuda_status(e, "route_project(q)");
+    CodeSelectParams qs{at<float>(ws, L.q_route), at<float>(ws, L.cb_norm), q_codes,
+                        static_cast<int64_t>(a.batch) * a.h_kv, a.n_q, a.h_kv, a.codebook_heads,
+                        a.n_codes, a.d_s, a.a, a.temperature};
+    e = launch_code_select(qs, st);
+    if (e != cudaSuccess) return cuda_status(e, "code_select(q)");
+  }
+  return SSA_OK;
+}
+
+ssa::IndexParams index_params(const SsaRouteArgs& a, const RouteLayout& L, void* ws,
+                              const int32_t* k_codes, int32_t* bucket_ptr, int32_t* bucket_keys) {
+  ssa::IndexParams ip{};
+  ip.k_codes = k_codes;
+  ip.bucket_ptr = bucket_ptr;
+  ip.bucket_keys = bucket_keys;
+  ip.counts = at<uint32_t>(ws, L.counts);
+  ip.partials = at<uint32_t>(ws, L.partials);
+  ip.batch = a.batch;
+  ip.n = a.n;
+  ip.h_kv = a.h_kv;
+  ip.b = a.b;
+  ip.n_codes = a.n_codes;
+  ip.tile_keys = ssa::index_tile_keys(a.b);
+  ip.tiles = L.tiles;
+  ip.chunks = L.chunks;
+  return ip;
+}
+
+ssa_status run_stage2(const SsaRouteArgs& a, const RouteLayout& L, void* ws, cudaStream_t st,
+                      const int32_t* q_codes, const int32_t* k_codes) {
+  using namespace ssa;
+  IndexParams ip = index_params(a, L, ws, k_codes, at<int32_t>(ws, L.bucket_ptr),
+                                at<int32_t>(ws, L.bucket_keys));
+  cudaError_t e = launch_build_index(ip, st);
+  if (e != cudaSuccess) return cuda_status(e, "build_index");
+  RescoreParams rp{};
+  rp.q = a.q; rp.q_sb = a.q_stride_b; rp.q_sn = a.q_stride_n; rp.q_sh = a.q_stride_h;
+  rp.k = a.k; rp.k_sb = a.k_stride_b; rp.k_sn = a.k_stride_n; rp.k_sh = a.k_stride_h;
+  rp.q_codes = q_codes;
+  rp.k_codes = k_codes;
+  rp.bucket_ptr = ip.bucket_ptr;
+  rp.bucket_keys = ip.bucket_keys;
+  rp.out = a.indices;
+  rp.index_i64 = a.index_dtype == SSA_I64;
+  rp.cand_counts = a.cand_counts;
+  rp.batch = a.batch; rp.n = a.n; rp.n_q = a.n_q; rp.q_offset = a.q_offset;
+  rp.h_kv = a.h_kv; rp.group = a.h_q / a.h_kv; rp.d = a.d; rp.a = a.a; rp.b = a.b;
+  rp.n_codes = a.n_codes; rp.top_k = a.top_k; rp.causal = a.causal ? 1 : 0;
+  rp.cap = rescore_cap(std::min(a.top_k, a.n));
+  e = launch_rescore(rp, a.dtype, st);
+  return cuda_status(e, "rescore_topk");
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* ssa_status_str(ssa_status s) {
+  switch (s) {
+    case SSA_OK: return "ok";
+    case SSA_ERR_INVALID_ARG: return "invalid argument";
+    case SSA_ERR_UNSUPPORTED: return "unsupported size";
+    case SSA_ERR_WORKSPACE: return "workspace missing or too small";
+    case SSA_ERR_ALIGNMENT: return "misaligned pointer or stride";
+    case SSA_ERR_CUDA: return "CUDA error";
+    case SSA_ERR_DEVICE: return "device-side error";
+  }
+  return "unknown status";
+}
+
+const char* ssa_last_error(void) { return g_last_error.c_str(); }
+
+size_t ssa_route_workspace_size(const SsaRouteArgs* args) {
+  if (!args) return 0;
+  return route_layout(*args).total;
+}
+
+ssa_status ssa_route(const SsaRouteArgs* args, void* workspace, size_t workspace_bytes, void* stream) {
+  ssa_status s = check_route(args, true, true);
+  if (s != SSA_OK) return s;
+  const RouteLayout L = route_layout(*args);
+  if (!workspace || workspace_bytes < L.total)
+    return fail(SSA_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", L.total, workspace_bytes);
+  if (args->batch == 0 || args->n_q == 0) return SSA_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int32_t* qc = args->q_codes ? args->q_codes : at<int32_t>(workspace, L.q_codes);
+  int32_t* kc = args->k_codes ? args->k_codes : at<int32_t>(workspace, L.k_codes);
+  s = run_stage1(*args, L, workspace, st, true, qc, kc);
+  if (s != SSA_OK) return s;
+  return run_stage2(*args, L, workspace, st, qc, kc);
+}
+
+ssa_status ssa_code_assign(const SsaRouteArgs* args, void* workspace, size_t workspace_bytes,
+                           void* stream) {
+  ssa_status s = check_route(args, false, false);
+  if (s != SSA_OK) return s;
+  if (!args->k_codes) return fail(SSA_ERR_INVALID_ARG, "k_codes is NULL");
+  const RouteLayout L = route_layout(*args);
+  if (!workspace || workspace_bytes < L.total)
+    return fail(SSA_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", L.total, workspace_bytes);
+  if (args->batch == 0) return SSA_OK;
+  return run_stage1(*args, L, workspace, static_cast<cudaStream_t>(stream), false, nullptr,
+                    args->k_codes);
+}
+
+ssa_status ssa_select_from_scores(const float* scores, int64_t rows, int32_t n_cols, int32_t kk,
+                                  int32_t* out_idx, void* stream) {
+  if (!scores || !out_idx) return fail(SSA_ERR_INVALID_ARG, "NULL pointer");
+  if (rows < 0 || n_cols < 1 || kk < 1 || kk > 32 || kk > n_cols)
+    return fail(SSA_ERR_UNSUPPORTED, "need rows >= 0, 1 <= kk <= min(32, n_cols)");
+  cudaError_t e = ssa::launch_select_from_scores(scores, rows, n_cols, kk, out_idx,
+                                                 static_cast<cudaStream_t>(stream));
+  return cuda_status(e, "select_from_scores");
+}
+
+ssa_status ssa_build_index(const SsaRouteArgs* args, const int32_t* k_codes, int32_t* bucket_ptr,
+                           int32_t* bucket_keys, void* workspace, size_t workspace_bytes, void* stream) {
+  ssa_status s = check_route(args, false, false);
+  if (s != SSA_OK) return s;
+  if (!k_codes || !bucket_ptr || !bucket_keys) return fail(SSA_ERR_INVALID_ARG, "NULL pointer");
+  const RouteLayout L = route_layout(*args);
+  if (!workspace || workspace_bytes < L.total)
+    return fail(SSA_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", L.total, workspace_bytes);
+  if (args->batch == 0) return SSA_OK;
+  ssa::IndexParams ip = index_params(*args, L, workspace, k_codes, bucket_ptr, bucket_keys);
+  return cuda_status(ssa::launch_build_index(ip, static_cast<cudaStream_t>(stream)), "build_index");
+}
+
+ssa_status ssa_select_candidates(const SsaRouteArgs* args, void* workspace, size_t workspace_bytes,
+                                 void* stream) {
+  ssa_status s = check_route(args, true, true);
+  if (s != SSA_OK) return s;
+  if (!args->q_codes || !args->k_codes) return fail(SSA_ERR_INVALID_ARG, "q_codes / k_codes is NULL");
+  const RouteLayout L = route_layout(*args);
+  if (!workspace || workspace_bytes < L.total)
+    return fail(SSA_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", L.total, workspace_bytes);
+  if (args->batch == 0 || args->n_q == 0) return SSA_OK;
+  return run_stage2(*args, L, workspace, static_cast<cudaStream_t>(stream), args->q_codes,
+                    args->k_codes);
+}
+
+ssa_status ssa_sparse_attn(const SsaAttnArgs* a, void* stream) {
+  if (!a) return fail(SSA_ERR_INVALID_ARG, "args is NULL");
+  if (a->batch < 0 || a->n_q < 0 || a->n < 1 || a->q_offset < 0 || a->top_k < 1)
+    return fail(SSA_ERR_INVALID_ARG, "bad sizes");
+  if (a->h_kv < 1 || a->h_q % a->h_kv != 0)
+    return fail(SSA_ERR_INVALID_ARG, "num_q_heads (%d) must be a multiple of num_kv_heads (%d)", a->h_q, a->h_kv);
+  if (a->h_q / a->h_kv > 16) return fail(SSA_ERR_UNSUPPORTED, "GQA group size %d > 16", a->h_q / a->h_kv);
+  if (a->d < 8 || a->d > 256 || a->d % 8 != 0)
+    return fail(SSA_ERR_UNSUPPORTED, "head_dim %d: need a multiple of 8 in [8, 256]", a->d);
+  if (!valid_dtype(a->dtype)) return fail(SSA_ERR_INVALID_ARG, "bad dtype");
+  if (a->index_dtype != SSA_I32 && a->index_dtype != SSA_I64) return fail(SSA_ERR_INVALID_ARG, "bad index dtype");
+  if (!a->q || !a->k || !a->v || !a->indices || !a->out) return fail(SSA_ERR_INVALID_ARG, "NULL pointer");
+  if (!(a->scale != 0.f)) return fail(SSA_ERR_INVALID_ARG, "scale must be non-zero");
+  if (!aligned16(a->k) || !stride16(a->k_stride_n, a->dtype) || !stride16(a->k_stride_h, a->dtype) ||
+      !stride16(a->k_stride_b, a->dtype))
+    return fail(SSA_ERR_ALIGNMENT, "k must be 16-byte aligned with 16-byte strides");
+  if (a->batch == 0 || a->n_q == 0) return SSA_OK;
+  ssa::AttnParams p{};
+  p.q = a->q; p.q_sb = a->q_stride_b; p.q_sn = a->q_stride_n; p.q_sh = a->q_stride_h;
+  p.k = a->k; p.k_sb = a->k_stride_b; p.k_sn = a->k_stride_n; p.k_sh = a->k_stride_h;
+  p.v = a->v; p.v_sb = a->v_stride_b; p.v_sn = a->v_stride_n; p.v_sh = a->v_stride_h;
+  p.idx = a->indices; p.i_sb = a->idx_stride_b; p.i_sn = a->idx_stride_n; p.i_sh = a->idx_stride_h;
+  p.index_i64 = a->index_dtype == SSA_I64;
+  p.out = a->out; p.o_sb = a->out_stride_b; p.o_sn = a->out_stride_n; p.o_sh = a->out_stride_h;
+  p.status = a->status;
+  p.batch = a->batch; p.n_q = a->n_q; p.n = a->n; p.q_offset = a->q_offset;
+  p.h_kv = a->h_kv; p.group = a->h_q / a->h_kv; p.d = a->d; p.top_k = a->top_k;
+  p.causal = a->causal ? 1 : 0;
+  p.inv_scale = 1.0f / a->scale;
+  return cuda_status(ssa::launch_sparse_attn(p, a->dtype, static_cast<cudaStream_t>(stream)),
+                     "sparse_attn");
+}
+
+}  // extern "C"

@@ -1,0 +1,224 @@
+// K2: the code -> key inverted index (per batch element and KV head).
+//
+// The reference evaluates "key j shares a code with query i" as a dense
+// [n, h_kv, n] boolean mask (_build_candidate_mask, ssa/router.py:216-259).
+// Here the same relation is stored in linear memory, as the design document
+// describes (ssa_design.md:103-112): bucket c of head h holds every key j
+// with c among its top-b codes, keys ascending.
+//
+// Three phases, all deterministic:
+//   1. index_count_kernel  -- per key tile, a shared-memory histogram of
+//      codes (warp-aggregated shared atomics), written to counts[bh][c][t].
+//   2. scan (reduce / partials / apply) -- exclusive prefix over (c, t) per
+//      (bat, h): counts become write offsets, bucket_ptr[c] = offset[c][0].
+//   3. index_scatter_kernel -- each tile sorts its (code, entry) pairs in
+//      shared memory (bitonic; pairs are unique, so the order is fixed),
+//      then writes key j at offset[c][t] + rank within its code run.
+//      Keys are therefore ascending within every bucket.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace ssa {
+
+constexpr int kIndexThreads = 512;
+
+__global__ void __launch_bounds__(kIndexThreads) index_count_kernel(IndexParams p) {
+  extern __shared__ uint32_t hist[];          // [n_codes]
+  const int t = blockIdx.x;
+  const int bh = blockIdx.y;                  // bat * h_kv + h
+  const int h = bh % p.h_kv, bat = bh / p.h_kv;
+  for (int c = threadIdx.x; c < p.n_codes; c += blockDim.x) hist[c] = 0;
+  __syncthreads();
+  const int j0 = t * p.tile_keys;
+  const int nk = min(p.tile_keys, p.n - j0);
+  const int entries = nk * p.b;
+  for (int e = threadIdx.x; e < entries; e += blockDim.x) {
+    const int jl = e / p.b, s = e % p.b;
+    const int c = p.k_codes[((static_cast<int64_t>(bat) * p.n + j0 + jl) * p.h_kv + h) * p.b + s];
+    // warp-aggregated: one shared atomic per distinct code in the warp
+    const unsigned active = __activemask();
+    const unsigned peers = __match_any_sync(active, c);
+    const int leader = __ffs(peers) - 1;
+    if ((threadIdx.x % kWarp) == leader) atomicAdd(&hist[c], __popc(peers));
+  }
+  __syncthreads();
+  uint32_t* out = p.counts + static_cast<int64_t>(bh) * p.n_codes * p.tiles;
+  for (int c = threadIdx.x; c < p.n_codes; c += blockDim.x)
+    out[static_cast<int64_t>(c) * p.tiles + t] = hist[c];
+}
+
+// --- exclusive scan over counts[bh][0 .. n_codes*tiles) ----------------------
+template <int THREADS>
+__device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* warp_sums,
+                                                         uint32_t* total) {
+  const int lane = threadIdx.x % kWarp, warp = threadIdx.x / kWarp;
+  uint32_t x = v;
+#pragma unroll
+  for (int o = 1; o < kWarp; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == kWarp - 1) warp_sums[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    constexpr int W = THREADS / kWarp;
+    uint32_t s = lane < W ? warp_sums[lane] : 0u;
+#pragma unroll
+    for (int o = 1; o < kWarp; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, s, o);
+      if (lane >= o) s += y;
+    }
+    if (lane < W) warp_sums[lane] = s;      // inclusive
+    if (lane == W - 1) *total = s;
+  }
+  __syncthreads();
+  const uint32_t before = warp == 0 ? 0u : warp_sums[warp - 1];
+  const uint32_t r = before + x - v;
+  __syncthreads();
+  return r;
+}
+
+constexpr int kScanThreads = 1024;
+constexpr int kScanPerThread = kScanChunk / kScanThreads;
+
+__global__ void __launch_bounds__(kScanThreads) scan_reduce_kernel(IndexParams p) {
+  __shared__ uint32_t red[kScanThreads / kWarp];
+  const int64_t len = static_cast<int64_t>(p.n_codes) * p.tiles;
+  const int bh = blockIdx.y;
+  const int64_t chunk = blockIdx.x;
+  const uint32_t* src = p.counts + bh * len + chunk * kScanChunk;
+  const int64_t rest = len - chunk * kScanChunk;
+  const int64_t m = rest < kScanChunk ? rest : kScanChunk;
+  uint32_t s = 0;
+  for (int64_t e = threadIdx.x; e < m; e += kScanThreads) s += src[e];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (threadIdx.x % kWarp == 0) red[threadIdx.x / kWarp] = s;
+  __syncthreads();
+  if (threadIdx.x < kWarp) {
+    s = red[threadIdx.x];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (threadIdx.x == 0) p.partials[bh * p.chunks + chunk] = s;
+  }
+}
+
+__global__ void __launch_bounds__(kScanThreads) scan_partials_kernel(IndexParams p) {
+  __shared__ uint32_t ws[kScanThreads / kWarp];
+  __shared__ uint32_t tot;
+  const int bh = blockIdx.x;
+  uint32_t carry = 0;
+  uint32_t* part = p.partials + bh * p.chunks;
+  for (int64_t base = 0; base < p.chunks; base += kScanThreads) {
+    const int64_t e = base + threadIdx.x;
+    const uint32_t v = e < p.chunks ? part[e] : 0u;
+    const uint32_t ex = block_exclusive_scan<kScanThreads>(v, ws, &tot);
+    if (e < p.chunks) part[e] = carry + ex;
+    carry += tot;
+    __syncthreads();
+  }
+}
+
+__global__ void __launch_bounds__(kScanThreads) scan_apply_kernel(IndexParams p) {
+  __shared__ uint32_t ws[kScanThreads / kWarp];
+  __shared__ uint32_t tot;
+  const int64_t len = static_cast<int64_t>(p.n_codes) * p.tiles;
+  const int bh = blockIdx.y;
+  const int64_t chunk = blockIdx.x;
+  uint32_t* src = p.counts + bh * len + chunk * kScanChunk;
+  const int64_t rest = len - chunk * kScanChunk;
+  const int64_t m = rest < kScanChunk ? rest : kScanChunk;
+  uint32_t v[kScanPerThread];
+  uint32_t local = 0;
+#pragma unroll
+  for (int r = 0; r < kScanPerThread; ++r) {
+    const int64_t e = static_cast<int64_t>(threadIdx.x) * kScanPerThread + r;
+    v[r] = e < m ? src[e] : 0u;
+    local += v[r];
+  }
+  uint32_t run = block_exclusive_scan<kScanThreads>(local, ws, &tot) + p.partials[bh * p.chunks + chunk];
+  int32_t* ptr = p.bucket_ptr + static_cast<int64_t>(bh) * (p.n_codes + 1);
+#pragma unroll
+  for (int r = 0; r < kScanPerThread; ++r) {
+    const int64_t e = static_cast<int64_t>(threadIdx.x) * kScanPerThread + r;
+    if (e < m) {
+      src[e] = run;
+      const int64_t flat = chunk * kScanChunk + e;
+      if (flat % p.tiles == 0) ptr[flat / p.tiles] = static_cast<int32_t>(run);
+    }
+    run += v[r];
+  }
+  if (chunk == 0 && threadIdx.x == 0) ptr[p.n_codes] = p.n * p.b;
+}
+
+// --- stable scatter -------------------------------------------------------
+__global__ void __launch_bounds__(kIndexThreads) index_scatter_kernel(IndexParams p) {
+  __shared__ uint32_t keys[kIndexSortEntries];
+  const int t = blockIdx.x;
+  const int bh = blockIdx.y;
+  const int h = bh % p.h_kv, bat = bh / p.h_kv;
+  const int j0 = t * p.tile_keys;
+  const int nk = min(p.tile_keys, p.n - j0);
+  const int entries = nk * p.b;
+  int size = 1;
+  while (size < entries) size <<= 1;
+  // composite key (code << 16 | entry): unique within the tile
+  for (int e = threadIdx.x; e < size; e += blockDim.x) {
+    uint32_t kv = 0xffffffffu;
+    if (e < entries) {
+      const int jl = e / p.b, s = e % p.b;
+      const uint32_t c = static_cast<uint32_t>(
+          p.k_codes[((static_cast<int64_t>(bat) * p.n + j0 + jl) * p.h_kv + h) * p.b + s]);
+      kv = (c << 16) | static_cast<uint32_t>(e);
+    }
+    keys[e] = kv;
+  }
+  __syncthreads();
+  // ascending bitonic sort
+  for (int k2 = 2; k2 <= size; k2 <<= 1) {
+    for (int j = k2 >> 1; j > 0; j >>= 1) {
+      for (int e = threadIdx.x; e < size; e += blockDim.x) {
+        const int ixj = e ^ j;
+        if (ixj > e) {
+          const uint32_t x = keys[e], y = keys[ixj];
+          const bool up = (e & k2) == 0;
+          if ((x > y) == up) { keys[e] = y; keys[ixj] = x; }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  const uint32_t* off = p.counts + static_cast<int64_t>(bh) * p.n_codes * p.tiles;
+  int32_t* dst = p.bucket_keys + static_cast<int64_t>(bh) * p.n * p.b;
+  for (int e = threadIdx.x; e < entries; e += blockDim.x) {
+    const uint32_t kv = keys[e];
+    const uint32_t c = kv >> 16;
+    // first position of this code's run: lower bound of (c << 16)
+    int lo = 0, hi = e;
+    const uint32_t target = c << 16;
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (keys[mid] < target) lo = mid + 1; else hi = mid;
+    }
+    const uint32_t pos = off[static_cast<int64_t>(c) * p.tiles + t] + static_cast<uint32_t>(e - lo);
+    dst[pos] = j0 + static_cast<int32_t>((kv & 0xffffu) / p.b);
+  }
+}
+
+cudaError_t launch_build_index(const IndexParams& p, cudaStream_t st) {
+  const int bhs = p.batch * p.h_kv;
+  if (bhs == 0 || p.n == 0) return cudaSuccess;
+  const size_t hist_smem = static_cast<size_t>(p.n_codes) * sizeof(uint32_t);
+  cudaFuncSetAttribute(index_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       static_cast<int>(hist_smem));
+  dim3 g1(p.tiles, bhs);
+  index_count_kernel<<<g1, kIndexThreads, hist_smem, st>>>(p);
+  dim3 g2(static_cast<unsigned>(p.chunks), bhs);
+  scan_reduce_kernel<<<g2, kScanThreads, 0, st>>>(p);
+  scan_partials_kernel<<<bhs, kScanThreads, 0, st>>>(p);
+  scan_apply_kernel<<<g2, kScanThreads, 0, st>>>(p);
+  index_scatter_kernel<<<g1, kIndexThreads, 0, st>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace ssa

@@ -1,0 +1,86 @@
+// Kernel parameter blocks and launchers shared between the kernel files and
+// the C-ABI layer (abi.cu).  Internal to libssa_sm100a.so.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/ssa_b200.h"
+
+namespace ssa {
+
+// K0: routing projection.  rows = batch*h_kv*n_rows, row order (bat, h, i).
+struct RouteProjectParams {
+  const void* x;           // q [B,n_rows,h_q,d] (group>1) or k [B,n_rows,h_kv,d]
+  int64_t stride_b, stride_n, stride_h;
+  const void* w;           // [d_s, d]
+  float* out;              // [rows, d_s] L2-normalised route vectors
+  int64_t rows, n_rows;
+  int h_kv, group, d, d_s;
+};
+
+// K1: codebook scoring + top-kk selection.  Route rows in (bat, h, i) order.
+struct CodeSelectParams {
+  const float* route;      // [batch_heads * n_rows, d_s]
+  const float* codebook;   // normalised [codebook_heads, n_codes, d_s]
+  int32_t* codes;          // out [B, n_rows, h_kv, kk]
+  int64_t batch_heads, n_rows;
+  int h_kv, codebook_heads, n_codes, d_s, kk;
+  float temperature;
+};
+
+// K2: code -> key inverted index.
+struct IndexParams {
+  const int32_t* k_codes;  // [B, n, h_kv, b]
+  int32_t* bucket_ptr;     // [B*h_kv, n_codes+1]
+  int32_t* bucket_keys;    // [B*h_kv, n*b]
+  uint32_t* counts;        // [B*h_kv, n_codes, tiles] workspace
+  uint32_t* partials;      // [B*h_kv, chunks] workspace
+  int batch, n, h_kv, b, n_codes, tile_keys, tiles;
+  int64_t chunks;          // scan chunks per (bat, h)
+};
+
+constexpr int kIndexSortEntries = 4096;  // entries sorted per tile
+constexpr int kScanChunk = 4096;
+
+inline int index_tile_keys(int b) { return kIndexSortEntries / b; }
+
+// K3: candidate union + causal filter + re-score + top-k + filler.
+struct RescoreParams {
+  const void* q; int64_t q_sb, q_sn, q_sh;
+  const void* k; int64_t k_sb, k_sn, k_sh;
+  const int32_t* q_codes;      // [B, n_q, h_kv, a]
+  const int32_t* k_codes;      // [B, n, h_kv, b]
+  const int32_t* bucket_ptr;   // [B*h_kv, n_codes+1]
+  const int32_t* bucket_keys;  // [B*h_kv, n*b]
+  void* out; int index_i64;    // [B, n_q, h_kv, top_k]
+  int32_t* cand_counts;        // optional [B, n_q, h_kv]
+  int batch, n, n_q, q_offset, h_kv, group, d, a, b, n_codes, top_k, causal;
+  int cap;                     // shared-memory candidate capacity (power of two)
+};
+
+// K4: sparse exact attention.
+struct AttnParams {
+  const void* q; int64_t q_sb, q_sn, q_sh;
+  const void* k; int64_t k_sb, k_sn, k_sh;
+  const void* v; int64_t v_sb, v_sn, v_sh;
+  const void* idx; int64_t i_sb, i_sn, i_sh; int index_i64;
+  void* out; int64_t o_sb, o_sn, o_sh;
+  int32_t* status;
+  int batch, n_q, n, q_offset, h_kv, group, d, top_k, causal;
+  float inv_scale;
+};
+
+cudaError_t launch_route_project(const RouteProjectParams& p, ssa_dtype xt, ssa_dtype wt,
+                                 cudaStream_t st);
+cudaError_t launch_codebook_normalize(const void* cb, ssa_dtype wt, float* out, int64_t rows,
+                                      int d_s, cudaStream_t st);
+cudaError_t launch_code_select(const CodeSelectParams& p, cudaStream_t st);
+cudaError_t launch_select_from_scores(const float* scores, int64_t rows, int n_cols, int kk,
+                                      int32_t* out, cudaStream_t st);
+cudaError_t launch_build_index(const IndexParams& p, cudaStream_t st);
+cudaError_t launch_rescore(const RescoreParams& p, ssa_dtype dt, cudaStream_t st);
+size_t rescore_smem_bytes(int cap, int top_k);
+cudaError_t launch_sparse_attn(const AttnParams& p, ssa_dtype dt, cudaStream_t st);
+
+}  // namespace ssa

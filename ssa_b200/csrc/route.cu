@@ -1,0 +1,249 @@
+// Stage 1 of the SSA router: routing projection, codebook scoring and the
+// fused top-a (queries) / top-b (keys) code selection.
+//
+// Reference: CodebookRouter.forward, ssa/router.py:102-141, and
+// get_code_assignment, ssa/router.py:261-275.
+//
+//   q_route[i,h] = normalize( W_qr . mean_g q[i, h*g+g'] )      [d_s]
+//   k_route[j,h] = normalize( W_kr . k[j, h] )                  [d_s]
+//   score[r, c]  = (route[r] . normalize(codebook[h, c])) / temperature
+//   codes[r]     = top-a (queries) / top-b (keys) of score[r, :]
+//
+// The reference projects each query head and then averages over the GQA
+// group (ssa/router.py:102-112); projecting the group mean is the same
+// linear map, evaluated with g times fewer multiply-adds.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace ssa {
+
+// ---------------------------------------------------------------------------
+// K0: routing projection + L2 normalisation.
+// One warp per output row; lane c owns route component c (d_s <= 64, two
+// components per lane above 32).  W^T sits in shared memory as fp32 so that
+// lane c reads W^T[e][c] (consecutive addresses, conflict-free) and the
+// input row x[e] is a shared-memory broadcast.
+// ---------------------------------------------------------------------------
+template <typename T, typename TW>
+__global__ void __launch_bounds__(256) route_project_kernel(RouteProjectParams p) {
+  extern __shared__ float smem[];
+  const int d = p.d, d_s = p.d_s;
+  float* wt = smem;                          // [d][d_s]
+  float* xs = smem + d * d_s;                // [warps][d]
+  const TW* w = static_cast<const TW*>(p.w);
+  for (int t = threadIdx.x; t < d * d_s; t += blockDim.x) {
+    const int c = t / d, e = t % d;          // w is [d_s][d]
+    wt[e * d_s + c] = Elem<TW>::to_f(w[t]);
+  }
+  __syncthreads();
+  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+  const int warps = blockDim.x / kWarp;
+  float* x = xs + warp * d;
+  const T* src = static_cast<const T*>(p.x);
+  const float inv_g = 1.0f / static_cast<float>(p.group);
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * warps + warp; row < p.rows;
+       row += static_cast<int64_t>(gridDim.x) * warps) {
+    // row = ((bat * h_kv + h) * n_rows + i)
+    const int64_t i = row % p.n_rows;
+    const int64_t bh = row / p.n_rows;
+    const int h = static_cast<int>(bh % p.h_kv);
+    const int64_t bat = bh / p.h_kv;
+    const T* base = src + bat * p.stride_b + i * p.stride_n +
+                    static_cast<int64_t>(h) * p.group * p.stride_h;
+    for (int e = lane; e < d; e += kWarp) {
+      float acc = 0.f;
+      for (int gg = 0; gg < p.group; ++gg) acc += Elem<T>::to_f(base[gg * p.stride_h + e]);
+      x[e] = p.group == 1 ? acc : acc * inv_g;
+    }
+    __syncwarp();
+    float r0 = 0.f, r1 = 0.f;
+    const int c0 = lane, c1 = lane + kWarp;
+    if (c0 < d_s) {
+      for (int e = 0; e < d; ++e) r0 = fmaf(wt[e * d_s + c0], x[e], r0);
+    }
+    if (c1 < d_s) {
+      for (int e = 0; e < d; ++e) r1 = fmaf(wt[e * d_s + c1], x[e], r1);
+    }
+    float ss = r0 * r0 + r1 * r1;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float nrm = fmaxf(sqrtf(ss), 1e-12f);
+    float* out = p.out + row * d_s;
+    if (c0 < d_s) out[c0] = r0 / nrm;
+    if (c1 < d_s) out[c1] = r1 / nrm;
+    __syncwarp();
+  }
+}
+
+// Codebook rows -> L2-normalised fp32 copy [heads][n_codes][d_s].
+template <typename TW>
+__global__ void codebook_normalize_kernel(const TW* cb, float* out, int64_t rows, int d_s) {
+  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / kWarp) + warp;
+  if (row >= rows) return;
+  const float v0 = lane < d_s ? Elem<TW>::to_f(cb[row * d_s + lane]) : 0.f;
+  const float v1 = lane + kWarp < d_s ? Elem<TW>::to_f(cb[row * d_s + lane + kWarp]) : 0.f;
+  float ss = v0 * v0 + v1 * v1;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float nrm = fmaxf(sqrtf(ss), 1e-12f);
+  if (lane < d_s) out[row * d_s + lane] = v0 / nrm;
+  if (lane + kWarp < d_s) out[row * d_s + lane + kWarp] = v1 / nrm;
+}
+
+// ---------------------------------------------------------------------------
+// K1 (CUDA-core version): one thread per route row, scanning every code of its
+// head in increasing code order with a register top-K list.  The codebook
+// streams through shared memory in chunks; every thread of the block reads
+// the same code at the same time (broadcast).
+// ---------------------------------------------------------------------------
+constexpr int kSelThreads = 128;
+constexpr int kSelChunk = 128;   // codes per shared-memory chunk
+
+template <int KMAX, int DS>
+__global__ void __launch_bounds__(kSelThreads) code_select_kernel(CodeSelectParams p) {
+  __shared__ __align__(16) float cbs[kSelChunk * DS];
+  const int64_t tiles_per_head = cdiv(p.n_rows, kSelThreads);
+  const int64_t bh = blockIdx.x / tiles_per_head;        // bat * h_kv + h
+  const int64_t tile = blockIdx.x % tiles_per_head;
+  const int h = static_cast<int>(bh % p.h_kv);
+  const int64_t bat = bh / p.h_kv;
+  const int64_t i = tile * kSelThreads + threadIdx.x;
+  const bool active = i < p.n_rows;
+  const int64_t row = bh * p.n_rows + (active ? i : 0);
+  float r[DS];
+#pragma unroll
+  for (int e = 0; e < DS; e += 4) {
+    const float4 v = *reinterpret_cast<const float4*>(p.route + row * DS + e);
+    r[e] = v.x; r[e + 1] = v.y; r[e + 2] = v.z; r[e + 3] = v.w;
+  }
+  TopList<KMAX> top;
+  top.init();
+  const float* cb = p.codebook + static_cast<int64_t>(p.codebook_heads == 1 ? 0 : h) *
+                                     p.n_codes * DS;
+  const bool unit_temp = p.temperature == 1.0f;
+  for (int c0 = 0; c0 < p.n_codes; c0 += kSelChunk) {
+    const int cn = min(kSelChunk, p.n_codes - c0);
+    __syncthreads();
+    for (int t = threadIdx.x * 4; t < cn * DS; t += kSelThreads * 4)
+      *reinterpret_cast<float4*>(cbs + t) =
+          *reinterpret_cast<const float4*>(cb + static_cast<int64_t>(c0) * DS + t);
+    __syncthreads();
+    for (int c = 0; c < cn; ++c) {
+      const float4* cv = reinterpret_cast<const float4*>(cbs + c * DS);
+      float s = 0.f;
+#pragma unroll
+      for (int e = 0; e < DS / 4; ++e) {
+        const float4 w = cv[e];
+        s = fmaf(r[4 * e], w.x, s);
+        s = fmaf(r[4 * e + 1], w.y, s);
+        s = fmaf(r[4 * e + 2], w.z, s);
+        s = fmaf(r[4 * e + 3], w.w, s);
+      }
+      if (!unit_temp) s = s / p.temperature;
+      if (s > top.threshold()) top.insert(s, c0 + c);
+    }
+  }
+  if (!active) return;
+  // codes out: [bat][i][h][kk]
+  int32_t* out = p.codes + ((bat * p.n_rows + i) * p.h_kv + h) * p.kk;
+#pragma unroll
+  for (int t = 0; t < KMAX; ++t)
+    if (t < p.kk) out[t] = top.i[t];
+}
+
+// Selection on fed scores: the same TopList with the same push order.
+template <int KMAX>
+__global__ void select_from_scores_kernel(const float* scores, int64_t rows, int n_cols, int kk,
+                                          int32_t* out) {
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  TopList<KMAX> top;
+  top.init();
+  const float* s = scores + r * n_cols;
+  for (int c = 0; c < n_cols; ++c) {
+    const float v = s[c];
+    if (v > top.threshold()) top.insert(v, c);
+  }
+#pragma unroll
+  for (int t = 0; t < KMAX; ++t)
+    if (t < kk) out[r * kk + t] = top.i[t];
+}
+
+// ---------------------------------------------------------------------------
+// host-side launchers
+// ---------------------------------------------------------------------------
+cudaError_t launch_route_project(const RouteProjectParams& p, ssa_dtype xt, ssa_dtype wt,
+                                 cudaStream_t st) {
+  const int threads = 256;
+  const size_t smem = (static_cast<size_t>(p.d) * p.d_s + (threads / kWarp) * p.d) * sizeof(float);
+  int64_t blocks = cdiv(p.rows, threads / kWarp);
+  blocks = blocks > 148 * 16 ? 148 * 16 : blocks;
+  if (blocks < 1) return cudaSuccess;
+#define SSA_RP(T, TW)                                                                       \
+  do {                                                                                      \
+    auto kern = route_project_kernel<T, TW>;                                                \
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);     \
+    kern<<<(unsigned)blocks, threads, smem, st>>>(p);                                       \
+  } while (0)
+  if (xt == SSA_F32 && wt == SSA_F32) SSA_RP(float, float);
+  else if (xt == SSA_BF16 && wt == SSA_BF16) SSA_RP(__nv_bfloat16, __nv_bfloat16);
+  else if (xt == SSA_BF16 && wt == SSA_F32) SSA_RP(__nv_bfloat16, float);
+  else if (xt == SSA_F16 && wt == SSA_F16) SSA_RP(__half, __half);
+  else if (xt == SSA_F16 && wt == SSA_F32) SSA_RP(__half, float);
+  else if (xt == SSA_F32 && wt == SSA_BF16) SSA_RP(float, __nv_bfloat16);
+  else return cudaErrorInvalidValue;
+#undef SSA_RP
+  return cudaGetLastError();
+}
+
+cudaError_t launch_codebook_normalize(const void* cb, ssa_dtype wt, float* out, int64_t rows,
+                                      int d_s, cudaStream_t st) {
+  const int threads = 256;
+  const unsigned blocks = static_cast<unsigned>(cdiv(rows, threads / kWarp));
+  if (blocks == 0) return cudaSuccess;
+  if (wt == SSA_F32)
+    codebook_normalize_kernel<float><<<blocks, threads, 0, st>>>(static_cast<const float*>(cb), out, rows, d_s);
+  else if (wt == SSA_BF16)
+    codebook_normalize_kernel<__nv_bfloat16><<<blocks, threads, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(cb), out, rows, d_s);
+  else
+    codebook_normalize_kernel<__half><<<blocks, threads, 0, st>>>(static_cast<const __half*>(cb), out, rows, d_s);
+  return cudaGetLastError();
+}
+
+template <int DS>
+static cudaError_t launch_code_select_ds(const CodeSelectParams& p, cudaStream_t st) {
+  const int64_t blocks = p.batch_heads * cdiv(p.n_rows, kSelThreads);
+  if (blocks == 0) return cudaSuccess;
+  if (p.kk <= 4) code_select_kernel<4, DS><<<(unsigned)blocks, kSelThreads, 0, st>>>(p);
+  else if (p.kk <= 8) code_select_kernel<8, DS><<<(unsigned)blocks, kSelThreads, 0, st>>>(p);
+  else if (p.kk <= 16) code_select_kernel<16, DS><<<(unsigned)blocks, kSelThreads, 0, st>>>(p);
+  else code_select_kernel<32, DS><<<(unsigned)blocks, kSelThreads, 0, st>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_code_select(const CodeSelectParams& p, cudaStream_t st) {
+  switch (p.d_s) {
+    case 4: return launch_code_select_ds<4>(p, st);
+    case 8: return launch_code_select_ds<8>(p, st);
+    case 16: return launch_code_select_ds<16>(p, st);
+    case 32: return launch_code_select_ds<32>(p, st);
+    case 64: return launch_code_select_ds<64>(p, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_select_from_scores(const float* scores, int64_t rows, int n_cols, int kk,
+                                      int32_t* out, cudaStream_t st) {
+  const int threads = 128;
+  const unsigned blocks = static_cast<unsigned>(cdiv(rows, threads));
+  if (blocks == 0) return cudaSuccess;
+  if (kk <= 4) select_from_scores_kernel<4><<<blocks, threads, 0, st>>>(scores, rows, n_cols, kk, out);
+  else if (kk <= 8) select_from_scores_kernel<8><<<blocks, threads, 0, st>>>(scores, rows, n_cols, kk, out);
+  else if (kk <= 16) select_from_scores_kernel<16><<<blocks, threads, 0, st>>>(scores, rows, n_cols, kk, out);
+  else select_from_scores_kernel<32><<<blocks, threads, 0, st>>>(scores, rows, n_cols, kk, out);
+  return cudaGetLastError();
+}
+
+}  // namespace ssa

@@ -1,0 +1,279 @@
+"""PyTorch custom ops over the C ABI of libssa_sm100a.so.
+
+Each op takes CUDA tensors, allocates its outputs (and, for the router, its
+workspace) from the PyTorch caching allocator, and calls the library on the
+current CUDA stream.  CPU tensors raise: there is no CPU path.
+
+Ops (namespace ``ssa_b200``):
+    route(q, k, w_qr, w_kr, codebook, a, b, top_k, causal, temperature,
+          q_offset, index_i64) -> (indices, q_codes, k_codes, cand_counts)
+    code_assign(k, w_kr, codebook, b, temperature) -> k_codes
+    sparse_attn(q, k, v, indices, scale, causal, q_offset) -> out
+
+``q`` is ``[B, n_q, h_q, d]``, ``k``/``v`` are ``[B, n, h_kv, d]``, indices
+``[B, n_q, h_kv, top_k]``; the public API in :mod:`ssa_b200` adds the
+reference's unbatched ``[n, h, d]`` forms.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib as L
+
+_DT = {torch.float32: L.SSA_F32, torch.bfloat16: L.SSA_BF16, torch.float16: L.SSA_F16}
+
+
+def _checked() -> bool:
+    return os.environ.get("SSA_CHECKED", "1") != "0"
+
+
+def _require_cuda(*ts: torch.Tensor) -> torch.device:
+    dev = ts[0].device
+    for t in ts:
+        if t.device.type != "cuda":
+            raise RuntimeError("ssa_b200 ops need CUDA tensors (sm_100a); got a tensor on "
+                               f"{t.device}. There is no CPU implementation.")
+        if t.device != dev:
+            raise RuntimeError(f"tensors on different devices: {dev} and {t.device}")
+    return dev
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DT[t.dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {t.dtype}; use float32, bfloat16 or float16") from None
+
+
+def _last_contig(t: torch.Tensor) -> torch.Tensor:
+    return t if t.stride(-1) == 1 else t.contiguous()
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def route_args(q, k, w_qr, w_kr, codebook, a, b, top_k, causal, temperature, q_offset,
+               indices=None, index_i64=True, q_codes=None, k_codes=None, cand_counts=None):
+    """Fill an :class:`SsaRouteArgs` from 4-D tensors (no launch)."""
+    B, n_q, h_q, d = q.shape
+    _, n, h_kv, _ = k.shape
+    cb = codebook if codebook.dim() == 3 else codebook.unsqueeze(0)
+    args = L.SsaRouteArgs()
+    args.batch, args.n, args.n_q, args.q_offset = B, n, n_q, q_offset
+    args.h_q, args.h_kv, args.d, args.d_s = h_q, h_kv, d, w_kr.shape[0]
+    args.n_codes, args.a, args.b, args.top_k = cb.shape[1], a, b, top_k
+    args.causal, args.temperature = int(bool(causal)), float(temperature)
+    args.dtype, args.w_dtype, args.codebook_heads = _dtype_code(k), _dtype_code(w_kr), cb.shape[0]
+    args.q = _ptr(q)
+    args.q_stride_b, args.q_stride_n, args.q_stride_h = q.stride(0), q.stride(1), q.stride(2)
+    args.k = _ptr(k)
+    args.k_stride_b, args.k_stride_n, args.k_stride_h = k.stride(0), k.stride(1), k.stride(2)
+    args.w_qr, args.w_kr, args.codebook = _ptr(w_qr), _ptr(w_kr), _ptr(cb)
+    args.indices = _ptr(indices)
+    args.index_dtype = L.SSA_I64 if index_i64 else L.SSA_I32
+    args.q_codes, args.k_codes, args.cand_counts = _ptr(q_codes), _ptr(k_codes), _ptr(cand_counts)
+    return args
+
+
+def _prep_weights(w_qr, w_kr, codebook, x_dtype=None):
+    """Weights share one dtype: the input dtype or float32."""
+    wd = w_kr.dtype
+    if x_dtype is not None and wd not in (x_dtype, torch.float32):
+        wd = torch.float32
+    w_kr = w_kr.to(wd)
+    w_qr = w_qr.to(wd).contiguous()
+    w_kr = w_kr.contiguous()
+    codebook = codebook.to(wd).contiguous()
+    return w_qr, w_kr, codebook
+
+
+def workspace(args: L.SsaRouteArgs, device) -> torch.Tensor:
+    nbytes = L.lib().ssa_route_workspace_size(ctypes.byref(args))
+    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+
+
+# ---------------------------------------------------------------------------
+# route
+# ---------------------------------------------------------------------------
+@torch.library.custom_op("ssa_b200::route", mutates_args=())
+def route(q: torch.Tensor, k: torch.Tensor, w_qr: torch.Tensor, w_kr: torch.Tensor,
+          codebook: torch.Tensor, a: int, b: int, top_k: int, causal: bool, temperature: float,
+          q_offset: int, index_i64: bool) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    dev = _require_cuda(q, k, w_qr, w_kr, codebook)
+    q, k = _last_contig(q), _last_contig(k)
+    w_qr, w_kr, codebook = _prep_weights(w_qr, w_kr, codebook, k.dtype)
+    B, n_q, _, _ = q.shape
+    _, n, h_kv, _ = k.shape
+    indices = torch.empty((B, n_q, h_kv, top_k), dtype=torch.int64 if index_i64 else torch.int32,
+                          device=dev)
+    q_codes = torch.empty((B, n_q, h_kv, a), dtype=torch.int32, device=dev)
+    k_codes = torch.empty((B, n, h_kv, b), dtype=torch.int32, device=dev)
+    counts = torch.empty((B, n_q, h_kv), dtype=torch.int32, device=dev)
+    args = route_args(q, k, w_qr, w_kr, codebook, a, b, top_k, causal, temperature, q_offset,
+                      indices, index_i64, q_codes, k_codes, counts)
+    ws = workspace(args, dev)
+    with torch.cuda.device(dev):
+        L.check("ssa_route", L.lib().ssa_route(ctypes.byref(args), ws.data_ptr(), ws.numel(),
+                                               _stream(dev)))
+    return indices, q_codes, k_codes, counts
+
+
+@route.register_fake
+def _route_fake(q, k, w_qr, w_kr, codebook, a, b, top_k, causal, temperature, q_offset, index_i64):
+    B, n_q, _, _ = q.shape
+    _, n, h_kv, _ = k.shape
+    return (q.new_empty((B, n_q, h_kv, top_k), dtype=torch.int64 if index_i64 else torch.int32),
+            q.new_empty((B, n_q, h_kv, a), dtype=torch.int32),
+            q.new_empty((B, n, h_kv, b), dtype=torch.int32),
+            q.new_empty((B, n_q, h_kv), dtype=torch.int32))
+
+
+# ---------------------------------------------------------------------------
+# code_assign
+# ---------------------------------------------------------------------------
+@torch.library.custom_op("ssa_b200::code_assign", mutates_args=())
+def code_assign(k: torch.Tensor, w_kr: torch.Tensor, codebook: torch.Tensor, b: int,
+                temperature: float) -> torch.Tensor:
+    dev = _require_cuda(k, w_kr, codebook)
+    k = _last_contig(k)
+    _, w_kr, codebook = _prep_weights(w_kr, w_kr, codebook, k.dtype)
+    B, n, h_kv, _ = k.shape
+    k_codes = torch.empty((B, n, h_kv, b), dtype=torch.int32, device=dev)
+    # q-side fields mirror k (unused by ssa_code_assign)
+    args = route_args(k, k, w_kr, w_kr, codebook, 1, b, 1, False, temperature, 0,
+                      k_codes=k_codes)
+    args.n_q = 0
+    ws = workspace(args, dev)
+    with torch.cuda.device(dev):
+        L.check("ssa_code_assign", L.lib().ssa_code_assign(ctypes.byref(args), ws.data_ptr(),
+                                                           ws.numel(), _stream(dev)))
+    return k_codes
+
+
+@code_assign.register_fake
+def _code_assign_fake(k, w_kr, codebook, b, temperature):
+    B, n, h_kv, _ = k.shape
+    return k.new_empty((B, n, h_kv, b), dtype=torch.int32)
+
+
+# ---------------------------------------------------------------------------
+# sparse_attn
+# ---------------------------------------------------------------------------
+def attn_args(q, k, v, indices, out, scale, causal, q_offset, status=None):
+    B, n_q, h_q, d = q.shape
+    _, n, h_kv, _ = k.shape
+    args = L.SsaAttnArgs()
+    args.batch, args.n_q, args.n, args.q_offset = B, n_q, n, q_offset
+    args.h_q, args.h_kv, args.d, args.top_k = h_q, h_kv, d, indices.shape[-1]
+    args.causal, args.scale, args.dtype = int(bool(causal)), float(scale), _dtype_code(q)
+    args.q = q.data_ptr()
+    args.q_stride_b, args.q_stride_n, args.q_stride_h = q.stride(0), q.stride(1), q.stride(2)
+    args.k = k.data_ptr()
+    args.k_stride_b, args.k_stride_n, args.k_stride_h = k.stride(0), k.stride(1), k.stride(2)
+    args.v = v.data_ptr()
+    args.v_stride_b, args.v_stride_n, args.v_stride_h = v.stride(0), v.stride(1), v.stride(2)
+    args.indices = indices.data_ptr()
+    args.index_dtype = L.SSA_I64 if indices.dtype == torch.int64 else L.SSA_I32
+    args.idx_stride_b, args.idx_stride_n, args.idx_stride_h = (indices.stride(0), indices.stride(1),
+                                                                indices.stride(2))
+    args.out = out.data_ptr()
+    args.out_stride_b, args.out_stride_n, args.out_stride_h = out.stride(0), out.stride(1), out.stride(2)
+    args.status = _ptr(status)
+    return args
+
+
+@torch.library.custom_op("ssa_b200::sparse_attn", mutates_args=())
+def sparse_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices: torch.Tensor,
+                scale: float, causal: bool, q_offset: int) -> torch.Tensor:
+    dev = _require_cuda(q, k, v, indices)
+    if not (q.dtype == k.dtype == v.dtype):
+        raise TypeError(f"q, k, v dtypes differ: {q.dtype}, {k.dtype}, {v.dtype}")
+    if indices.dtype not in (torch.int64, torch.int32):
+        raise TypeError(f"indices must be int64 or int32, got {indices.dtype}")
+    q, k, v, indices = _last_contig(q), _last_contig(k), _last_contig(v), _last_contig(indices)
+    out = torch.empty(q.shape, dtype=q.dtype, device=dev)
+    check = _checked() and not torch.cuda.is_current_stream_capturing()
+    status = torch.zeros(1, dtype=torch.int32, device=dev) if check else None
+    args = attn_args(q, k, v, indices, out, scale, causal, q_offset, status)
+    with torch.cuda.device(dev):
+        L.check("ssa_sparse_attn", L.lib().ssa_sparse_attn(ctypes.byref(args), _stream(dev)))
+    if status is not None:
+        bits = int(status.item())
+        if bits & L.SSA_DEVICE_INDEX_OOB:
+            raise IndexError(f"sparse_exact_attention: an index is outside [0, {k.shape[1]})")
+    return out
+
+
+@sparse_attn.register_fake
+def _sparse_attn_fake(q, k, v, indices, scale, causal, q_offset):
+    return torch.empty_like(q)
+
+
+# ---------------------------------------------------------------------------
+# test hooks (not custom ops): bit-exact parity of the selection stages
+# ---------------------------------------------------------------------------
+def select_from_scores(scores: torch.Tensor, kk: int) -> torch.Tensor:
+    """Top-``kk`` of each row of fp32 ``scores [rows, n_cols]`` (score desc, index asc)."""
+    dev = _require_cuda(scores)
+    s = scores.to(torch.float32).contiguous()
+    rows, n_cols = s.reshape(-1, s.shape[-1]).shape
+    out = torch.empty((rows, kk), dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        L.check("ssa_select_from_scores",
+                L.lib().ssa_select_from_scores(s.data_ptr(), rows, n_cols, kk, out.data_ptr(),
+                                               _stream(dev)))
+    return out.reshape(*scores.shape[:-1], kk)
+
+
+def build_index(k_codes: torch.Tensor, n_codes: int, h_q: int = 1):
+    """Inverted index of ``k_codes [B, n, h_kv, b]`` -> ``(bucket_ptr, bucket_keys)``."""
+    dev = _require_cuda(k_codes)
+    kc = k_codes.to(torch.int32).contiguous()
+    B, n, h_kv, b = kc.shape
+    dummy_k = torch.empty((B, n, h_kv, 8), dtype=torch.float32, device=dev)
+    w = torch.empty((4, 8), dtype=torch.float32, device=dev)
+    cb = torch.empty((1, n_codes, 4), dtype=torch.float32, device=dev)
+    args = route_args(dummy_k, dummy_k, w, w, cb, 1, b, 1, False, 1.0, 0)
+    args.h_q = h_kv
+    ptr = torch.empty((B, h_kv, n_codes + 1), dtype=torch.int32, device=dev)
+    keys = torch.empty((B, h_kv, n * b), dtype=torch.int32, device=dev)
+    ws = workspace(args, dev)
+    with torch.cuda.device(dev):
+        L.check("ssa_build_index", L.lib().ssa_build_index(ctypes.byref(args), kc.data_ptr(),
+                                                           ptr.data_ptr(), keys.data_ptr(),
+                                                           ws.data_ptr(), ws.numel(), _stream(dev)))
+    return ptr, keys
+
+
+def select_candidates(q, k, q_codes, k_codes, n_codes, top_k, causal=True, q_offset=0,
+                      index_i64=True):
+    """Stage 2 alone from given codes -> ``(indices, cand_counts)``."""
+    dev = _require_cuda(q, k, q_codes, k_codes)
+    q, k = _last_contig(q), _last_contig(k)
+    qc = q_codes.to(torch.int32).contiguous()
+    kc = k_codes.to(torch.int32).contiguous()
+    B, n_q, h_q, d = q.shape
+    _, n, h_kv, _ = k.shape
+    w = torch.empty((4, d), dtype=k.dtype, device=dev)
+    cb = torch.empty((1, n_codes, 4), dtype=k.dtype, device=dev)
+    idx = torch.empty((B, n_q, h_kv, top_k), dtype=torch.int64 if index_i64 else torch.int32,
+                      device=dev)
+    counts = torch.empty((B, n_q, h_kv), dtype=torch.int32, device=dev)
+    args = route_args(q, k, w, w, cb, qc.shape[-1], kc.shape[-1], top_k, causal, 1.0, q_offset,
+                      idx, index_i64, qc, kc, counts)
+    ws = workspace(args, dev)
+    with torch.cuda.device(dev):
+        L.check("ssa_select_candidates",
+                L.lib().ssa_select_candidates(ctypes.byref(args), ws.data_ptr(), ws.numel(),
+                                              _stream(dev)))
+    return idx, counts

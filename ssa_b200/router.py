@@ -1,0 +1,105 @@
+"""Stages 1-2 of the ``ssa`` API: ``CodebookRouter`` on the sm_100a kernels."""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.nn as nn
+
+from . import ops
+from .utils import is_lower_triangular_mask
+
+_README_ALIASES = {"d": "head_dim", "d_s": "route_dim", "n_c": "num_codebook", "b": "codes_per_key",
+                   "a": "codes_per_query", "k": "top_k", "h_kv": "num_kv_heads"}
+
+
+class CodebookRouter(nn.Module):
+    """Content-dependent router: for every query position and KV head, the
+    indices of ``top_k`` keys (ssa/router.py:14-275).
+
+    Parameters and state_dict keys match the reference (``W_qr.weight``,
+    ``W_kr.weight`` ``[route_dim, head_dim]``; ``codebook``
+    ``[num_kv_heads, num_codebook, route_dim]``), so reference checkpoints
+    load unchanged.  A shared ``[num_codebook, route_dim]`` codebook (the
+    design-document form) is also accepted by :meth:`forward` via
+    ``load_state_dict``/assignment and is broadcast to every head.
+
+    The README spelling ``CodebookRouter(d=, d_s=, n_c=, b=, a=, k=)`` is
+    accepted as well.
+    """
+
+    def __init__(self, head_dim: int = 128, route_dim: int = 32, num_kv_heads: int = 8,
+                 num_codebook: int = 2048, codes_per_key: int = 4, codes_per_query: int = 16,
+                 top_k: int = 256, temperature: float = 1.0, **aliases):
+        cfg = dict(head_dim=head_dim, route_dim=route_dim, num_kv_heads=num_kv_heads,
+                   num_codebook=num_codebook, codes_per_key=codes_per_key,
+                   codes_per_query=codes_per_query, top_k=top_k)
+        for name, val in aliases.items():
+            if name not in _README_ALIASES:
+                raise TypeError(f"CodebookRouter got an unexpected keyword argument '{name}'")
+            cfg[_README_ALIASES[name]] = val
+        super().__init__()
+        self.head_dim = cfg["head_dim"]
+        self.route_dim = cfg["route_dim"]
+        self.num_kv_heads = cfg["num_kv_heads"]
+        self.num_codebook = cfg["num_codebook"]
+        self.codes_per_key = cfg["codes_per_key"]
+        self.codes_per_query = cfg["codes_per_query"]
+        self.top_k = cfg["top_k"]
+        self.temperature = temperature
+        self.W_qr = nn.Linear(self.head_dim, self.route_dim, bias=False)
+        self.W_kr = nn.Linear(self.head_dim, self.route_dim, bias=False)
+        self.codebook = nn.Parameter(
+            torch.randn(self.num_kv_heads, self.num_codebook, self.route_dim) / self.route_dim ** 0.5)
+
+    def _causal_flag(self, causal_mask: Optional[torch.Tensor], causal: Optional[bool]) -> bool:
+        if causal is not None:
+            return bool(causal)
+        if causal_mask is None:
+            return False
+        if not is_lower_triangular_mask(causal_mask):
+            raise ValueError("CodebookRouter supports no mask or the lower-triangular causal mask "
+                             "(build_causal_mask); got another mask")
+        return True
+
+    def route(self, q_full: torch.Tensor, k_full: torch.Tensor, causal: bool = True,
+              q_offset: int = 0, index_dtype: torch.dtype = torch.int64):
+        """Batched routing: ``q [B, n_q, h_q, d]``, ``k [B, n, h_kv, d]`` ->
+        ``(indices [B, n_q, h_kv, k], q_codes, k_codes, cand_counts)``."""
+        if q_full.shape[-2] % k_full.shape[-2]:
+            raise ValueError("num_q_heads must be divisible by num_kv_heads")
+        with torch.no_grad():
+            return ops.route(q_full, k_full, self.W_qr.weight, self.W_kr.weight, self.codebook,
+                             self.codes_per_query, self.codes_per_key, self.top_k, bool(causal),
+                             float(self.temperature), int(q_offset), index_dtype == torch.int64)
+
+    def forward(self, q_full: torch.Tensor, k_full: torch.Tensor,
+                causal_mask: Optional[torch.Tensor] = None, hard: bool = True,
+                causal: Optional[bool] = None) -> torch.Tensor:
+        """``q_full [n, h_q, d]``, ``k_full [n, h_kv, d]`` (RoPE applied) ->
+        int64 indices ``[n, h_kv, top_k]`` (ssa/router.py:73-149).
+
+        ``causal_mask`` may be ``None`` or the ``tril`` mask; ``causal=`` (the
+        README form) overrides it.  ``hard=False`` (Gumbel assignment) is
+        training-only and not provided.  Batched ``[B, n, h, d]`` inputs give
+        ``[B, n, h_kv, top_k]``."""
+        if not hard:
+            raise NotImplementedError("hard=False (Gumbel-softmax code assignment) is training-only "
+                                      "and is not part of the forward hot path")
+        is_causal = self._causal_flag(causal_mask, causal)
+        unbatched = q_full.dim() == 3
+        q4 = q_full.unsqueeze(0) if unbatched else q_full
+        k4 = k_full.unsqueeze(0) if unbatched else k_full
+        idx = self.route(q4, k4, is_causal)[0]
+        return idx[0] if unbatched else idx
+
+    def get_code_assignment(self, k_full: torch.Tensor) -> torch.Tensor:
+        """Top-``codes_per_key`` codes of each key ``[n, h_kv, b]`` (int64,
+        ssa/router.py:261-275)."""
+        unbatched = k_full.dim() == 3
+        k4 = k_full.unsqueeze(0) if unbatched else k_full
+        with torch.no_grad():
+            codes = ops.code_assign(k4, self.W_kr.weight, self.codebook, self.codes_per_key, 1.0)
+        codes = codes.long()
+        return codes[0] if unbatched else codes

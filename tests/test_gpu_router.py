@@ -1,0 +1,150 @@
+"""End-to-end router and module parity on the GPU.
+
+* the reference's own fixtures (codes, well-defined top-k rows, module
+  output) reproduced through the public API;
+* code overlap and final candidate-set overlap >= 99.9% against the float64
+  oracle on a planted-cluster config-3 slice (bf16);
+* k = n reproduces dense causal attention (config 2, fp32 and bf16).
+"""
+
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import ssa_b200 as ssa
+from oracle import ssa_oracle as O
+from ssa_b200 import workloads as W
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def _router_from(z, dims):
+    n, h_q, h_kv, d, d_s, n_c, a, b, k = (int(x) for x in dims)
+    r = ssa.CodebookRouter(head_dim=d, route_dim=d_s, num_kv_heads=h_kv, num_codebook=n_c,
+                           codes_per_key=b, codes_per_query=a, top_k=k).to(DEV)
+    with torch.no_grad():
+        r.W_qr.weight.copy_(torch.from_numpy(z["w_qr"]))
+        r.W_kr.weight.copy_(torch.from_numpy(z["w_kr"]))
+        r.codebook.copy_(torch.from_numpy(z["codebook"]))
+    return r
+
+
+def test_router_reproduces_reference_fixture():
+    z = np.load(os.path.join(GOLD, "stage1.npz"))
+    r = _router_from(z, z["dims"])
+    q = torch.from_numpy(z["q"]).to(DEV)
+    k = torch.from_numpy(z["k"]).to(DEV)
+    idx, q_codes, k_codes, _ = r.route(q[None], k[None], causal=True)
+    np.testing.assert_array_equal(q_codes[0].cpu().numpy(), z["top_q_codes"])
+    np.testing.assert_array_equal(k_codes[0].cpu().numpy(), z["k_code_assign"])
+    wd = z["well_defined"]
+    np.testing.assert_array_equal(idx[0].cpu().numpy()[wd], z["indices"][wd])
+    # public forward(): causal mask form and README causal= form agree
+    a = r(q, k, causal_mask=ssa.build_causal_mask(q.shape[0], device=DEV))
+    b2 = r(q, k, causal=True)
+    assert a.dtype == torch.int64 and torch.equal(a, b2) and torch.equal(a, idx[0])
+    ca = r.get_code_assignment(k)
+    np.testing.assert_array_equal(ca.cpu().numpy(), z["k_code_assign"])
+
+
+def test_module_reproduces_reference_fixture():
+    z = np.load(os.path.join(GOLD, "module.npz"))
+    hs, h_q, h_kv, d, n, d_s, n_c, b, a, k = (int(x) for x in z["dims"])
+    m = ssa.SSAAttention(hidden_size=hs, num_q_heads=h_q, num_kv_heads=h_kv, head_dim=d, route_dim=d_s,
+                         num_codebook=n_c, codes_per_key=b, codes_per_query=a, top_k=k)
+    sd = {kk[3:].replace("__", "."): torch.from_numpy(z[kk]) for kk in z.files if kk.startswith("sd_")}
+    m.load_state_dict(sd)
+    m = m.to(DEV)
+    with torch.no_grad():
+        y = m(torch.from_numpy(z["x"]).to(DEV), freqs=torch.from_numpy(z["freqs"]).to(DEV))
+    rows = z["well_defined_rows"]
+    np.testing.assert_allclose(y[0].cpu().numpy()[rows], z["y"][0][rows], rtol=1e-4, atol=1e-5)
+    # every row (including filler rows) against the oracle's canonical module
+    w = {kk: v.numpy() for kk, v in sd.items()}
+    y_or, _ = O.module_forward(z["x"], w, h_q, h_kv, d, n_c, a, b, k, freqs=z["freqs"])
+    np.testing.assert_allclose(y[0].cpu().numpy(), y_or[0], rtol=1e-4, atol=1e-5)
+
+
+def _overlap(a, b):
+    """Mean |set(a_row) & set(b_row)| / k over rows of [..., k] index arrays."""
+    a = np.sort(a.reshape(-1, a.shape[-1]), axis=1)
+    b = np.sort(b.reshape(-1, b.shape[-1]), axis=1)
+    hits = 0
+    for x, y in zip(a, b):
+        hits += np.intersect1d(x, y, assume_unique=False).size
+    return hits / a.size
+
+
+def test_config3_slice_overlap_bf16():
+    shape = W.Shape(n=4096, h_q=32, h_kv=8, d=128, d_s=32, n_codes=4096, a=16, b=4, top_k=256)
+    t = W.make_inputs(shape, seed=3, dtype=torch.bfloat16)
+    r = ssa.CodebookRouter(head_dim=128, route_dim=32, num_kv_heads=8, num_codebook=4096,
+                           codes_per_key=4, codes_per_query=16, top_k=256).to(DEV)
+    with torch.no_grad():
+        r.W_qr.weight.copy_(t["w_qr"])
+        r.W_kr.weight.copy_(t["w_kr"])
+        r.codebook.copy_(t["codebook"])
+    idx, q_codes, k_codes, counts = r.route(t["q"], t["k"], causal=True)
+    qn = t["q"][0].double().cpu().numpy()
+    kn = t["k"][0].double().cpu().numpy()
+    oq, ok = O.route_codes(qn, kn, t["w_qr"].cpu().numpy(), t["w_kr"].cpu().numpy(),
+                           t["codebook"].cpu().numpy(), 16, 4)
+    q_same = (np.sort(q_codes[0].cpu().numpy(), -1) == np.sort(oq, -1)).all(-1).mean()
+    k_same = (np.sort(k_codes[0].cpu().numpy(), -1) == np.sort(ok, -1)).all(-1).mean()
+    assert q_same >= 0.999 and k_same >= 0.999, (q_same, k_same)
+    ref = O.select_topk_index(qn, kn, oq, ok, 4096, 256, causal=True)
+    ov = _overlap(idx[0].cpu().numpy(), ref)
+    assert ov >= 0.999, ov
+    # stage 3 on the GPU's own indices against the oracle on the same indices
+    v = t["v"]
+    out = ssa.sparse_exact_attention(t["q"][0], t["k"][0], v[0], idx[0], is_causal=True)
+    ref_out = O.sparse_attention(qn, kn, v[0].double().cpu().numpy(), idx[0].cpu().numpy(), causal=True)
+    err = np.abs(out.double().cpu().numpy() - ref_out)
+    assert (err <= 1e-4 + 2e-3 * np.abs(ref_out)).all()
+
+
+@pytest.mark.parametrize("dtype,atol", [(torch.float32, 1e-5), (torch.bfloat16, 2e-3)])
+def test_k_equals_n_reproduces_dense(dtype, atol):
+    shape = W.CONFIG2
+    t = W.make_inputs(shape, seed=2, dtype=dtype, planted=False)
+    r = ssa.CodebookRouter(head_dim=64, route_dim=32, num_kv_heads=2, num_codebook=1024,
+                           codes_per_key=4, codes_per_query=16, top_k=4096).to(DEV)
+    q, k, v = t["q"][0], t["k"][0], t["v"][0]
+    idx = r(q, k, causal=True)
+    srt = torch.sort(idx, dim=-1).values
+    assert torch.equal(srt, torch.arange(4096, device=DEV).expand_as(srt))
+    out = ssa.sparse_exact_attention(q, k, v, idx, is_causal=True)
+    qd, kd, vd = q.double(), k.double(), v.double()
+    dense = ssa.dense_attention(qd, kd, vd, causal_mask=ssa.build_causal_mask(4096, device=DEV))
+    err = (out.double() - dense).abs()
+    assert float(err.max()) <= atol + atol * float(dense.abs().max()), float(err.max())
+
+
+def test_batched_module_matches_per_sequence_calls():
+    m = ssa.SSAAttention(hidden_size=256, num_q_heads=4, num_kv_heads=1, head_dim=64, route_dim=16,
+                         num_codebook=128, codes_per_key=4, codes_per_query=8, top_k=16).to(DEV)
+    x = torch.randn(2, 32, 256, device=DEV)
+    with torch.no_grad():
+        y = m(x)
+        y0, y1 = m(x[:1]), m(x[1:])
+    assert torch.allclose(y, torch.cat([y0, y1]), atol=1e-6)
+    with torch.no_grad():
+        yd = m(x, use_dense=True)
+    assert torch.isfinite(yd).all() and torch.isfinite(y).all()
+
+
+def test_router_deterministic_and_variable_lengths():
+    r = ssa.CodebookRouter(head_dim=64, route_dim=16, num_kv_heads=2, num_codebook=128, codes_per_key=4,
+                           codes_per_query=8, top_k=16).to(DEV)
+    for n in (1, 8, 16, 24, 33, 1000):
+        q = torch.randn(n, 8, 64, device=DEV)
+        k = torch.randn(n, 2, 64, device=DEV)
+        a = r(q, k, causal=True)
+        b = r(q, k, causal=True)
+        assert a.shape == (n, 2, 16) and torch.equal(a, b)
+        assert int(a.min()) >= 0 and int(a.max()) < n
