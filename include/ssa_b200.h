@@ -50,7 +50,9 @@ typedef enum {
 } ssa_status;
 
 /* Bits OR-ed into a device status word. */
-#define SSA_DEVICE_INDEX_OOB 0x1 /* sparse_attn: an index < 0 or >= n was skipped */
+#define SSA_DEVICE_INDEX_OOB 0x1   /* sparse_attn: an index < 0 or >= n was skipped  */
+#define SSA_DEVICE_TIMEOUT 0x100   /* route: a pipeline wait gave up (~1 s); the
+                                      affected codes are undefined                  */
 
 typedef enum { SSA_F32 = 0, SSA_BF16 = 1, SSA_F16 = 2 } ssa_dtype;
 typedef enum { SSA_I32 = 0, SSA_I64 = 1 } ssa_index_dtype;
@@ -88,6 +90,7 @@ typedef struct {
   int32_t* q_codes;              /* optional [B, n_q, h_kv, a] contiguous     */
   int32_t* k_codes;              /* optional [B, n, h_kv, b] contiguous       */
   int32_t* cand_counts;          /* optional [B, n_q, h_kv]: unique candidates */
+  int32_t* status;               /* optional device word, SSA_DEVICE_* bits   */
 } SsaRouteArgs;
 
 /* Bytes of workspace ssa_route / ssa_code_assign need for these args. */

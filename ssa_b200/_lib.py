@@ -17,6 +17,7 @@ LIB_PATH = os.path.join(HERE, "libssa_sm100a.so")
 SSA_F32, SSA_BF16, SSA_F16 = 0, 1, 2
 SSA_I32, SSA_I64 = 0, 1
 SSA_DEVICE_INDEX_OOB = 0x1
+SSA_DEVICE_TIMEOUT = 0x100
 STATUS_NAMES = {0: "SSA_OK", 1: "SSA_ERR_INVALID_ARG", 2: "SSA_ERR_UNSUPPORTED", 3: "SSA_ERR_WORKSPACE",
                 4: "SSA_ERR_ALIGNMENT", 5: "SSA_ERR_CUDA", 6: "SSA_ERR_DEVICE"}
 
@@ -36,7 +37,7 @@ class SsaRouteArgs(ctypes.Structure):
         ("k", _vp), ("k_stride_b", _c_i64), ("k_stride_n", _c_i64), ("k_stride_h", _c_i64),
         ("w_qr", _vp), ("w_kr", _vp), ("codebook", _vp),
         ("indices", _vp), ("index_dtype", _c_i32),
-        ("q_codes", _vp), ("k_codes", _vp), ("cand_counts", _vp),
+        ("q_codes", _vp), ("k_codes", _vp), ("cand_counts", _vp), ("status", _vp),
     ]
 
 

@@ -49,7 +49,8 @@ int rescore_cap(int k_eff) {
 
 // Workspace regions for a route call.
 struct RouteLayout {
-  size_t q_route, k_route, cb_norm, q_codes, k_codes, counts, partials, bucket_ptr, bucket_keys;
+  size_t q_route, k_route, cb_norm, cb_image, q_codes, k_codes, counts, partials, bucket_ptr,
+      bucket_keys;
   size_t total;
   int tiles;
   int64_t chunks;
@@ -63,6 +64,9 @@ RouteLayout route_layout(const SsaRouteArgs& a) {
   L.q_route = take(static_cast<size_t>(B * hk * a.n_q * a.d_s) * 4);
   L.k_route = take(static_cast<size_t>(B * hk * a.n * a.d_s) * 4);
   L.cb_norm = take(static_cast<size_t>(a.codebook_heads) * a.n_codes * a.d_s * 4);
+  L.cb_image = take(ssa::code_score_tc_supported(a.d_s, a.n_codes)
+                        ? ssa::codebook_image_bytes(a.codebook_heads, a.n_codes, a.d_s)
+                        : 0);
   L.q_codes = take(static_cast<size_t>(B * a.n_q * hk * a.a) * 4);
   L.k_codes = take(static_cast<size_t>(B * a.n * hk * a.b) * 4);
   const int tile_keys = a.b > 0 ? ssa::index_tile_keys(a.b) : 1;
@@ -127,22 +131,51 @@ ssa_status check_route(const SsaRouteArgs* a, bool need_q, bool need_stage2) {
 template <typename T>
 T* at(void* ws, size_t off) { return reinterpret_cast<T*>(static_cast<char*>(ws) + off); }
 
+// Codebook scoring + top-kk of `rows` routed vectors: the tcgen05 kernel when
+// the shape allows it (d_s 16/32, N_c a multiple of 256), else the CUDA-core one.
+cudaError_t score_and_select(const SsaRouteArgs& a, const RouteLayout& L, void* ws, const float* route,
+                             int64_t n_rows, int kk, int32_t* codes, cudaStream_t st) {
+  using namespace ssa;
+  const int64_t bhs = static_cast<int64_t>(a.batch) * a.h_kv;
+  if (code_score_tc_supported(a.d_s, a.n_codes)) {
+    CodeScoreTcParams tp{};
+    tp.route = route;
+    tp.image = at<unsigned char>(ws, L.cb_image);
+    tp.codes = codes;
+    tp.error = a.status;
+    tp.batch_heads = bhs;
+    tp.n_rows = n_rows;
+    tp.tiles_per_head = cdiv(n_rows, 128);
+    tp.h_kv = a.h_kv;
+    tp.codebook_heads = a.codebook_heads;
+    tp.n_codes = a.n_codes;
+    tp.kk = kk;
+    tp.temperature = a.temperature;
+    return launch_code_score_tc(tp, a.d_s, st);
+  }
+  CodeSelectParams sp{route, at<float>(ws, L.cb_norm), codes, bhs, n_rows, a.h_kv, a.codebook_heads,
+                      a.n_codes, a.d_s, kk, a.temperature};
+  return launch_code_select(sp, st);
+}
+
 ssa_status run_stage1(const SsaRouteArgs& a, const RouteLayout& L, void* ws, cudaStream_t st,
                       bool queries, int32_t* q_codes, int32_t* k_codes) {
   using namespace ssa;
   cudaError_t e = launch_codebook_normalize(a.codebook, a.w_dtype, at<float>(ws, L.cb_norm),
                                             static_cast<int64_t>(a.codebook_heads) * a.n_codes, a.d_s, st);
   if (e != cudaSuccess) return cuda_status(e, "codebook_normalize");
+  if (code_score_tc_supported(a.d_s, a.n_codes)) {
+    e = launch_codebook_image(at<float>(ws, L.cb_norm), at<void>(ws, L.cb_image), a.codebook_heads,
+                              a.n_codes, a.d_s, st);
+    if (e != cudaSuccess) return cuda_status(e, "codebook_image");
+  }
   // keys
   RouteProjectParams kp{a.k, a.k_stride_b, a.k_stride_n, a.k_stride_h, a.w_kr,
                         at<float>(ws, L.k_route), static_cast<int64_t>(a.batch) * a.h_kv * a.n, a.n,
                         a.h_kv, 1, a.d, a.d_s};
   e = launch_route_project(kp, a.dtype, a.w_dtype, st);
   if (e != cudaSuccess) return cuda_status(e, "route_project(k)");
-  CodeSelectParams ks{at<float>(ws, L.k_route), at<float>(ws, L.cb_norm), k_codes,
-                      static_cast<int64_t>(a.batch) * a.h_kv, a.n, a.h_kv, a.codebook_heads,
-                      a.n_codes, a.d_s, a.b, a.temperature};
-  e = launch_code_select(ks, st);
+  e = score_and_select(a, L, ws, at<float>(ws, L.k_route), a.n, a.b, k_codes, st);
   if (e != cudaSuccess) return cuda_status(e, "code_select(k)");
   if (queries && a.n_q > 0) {
     RouteProjectParams qp{a.q, a.q_stride_b, a.q_stride_n, a.q_stride_h, a.w_qr,
@@ -150,10 +183,7 @@ ssa_status run_stage1(const SsaRouteArgs& a, const RouteLayout& L, void* ws, cud
                           a.n_q, a.h_kv, a.h_q / a.h_kv, a.d, a.d_s};
     e = launch_route_project(qp, a.dtype, a.w_dtype, st);
     if (e != cudaSuccess) return cuda_status(e, "route_project(q)");
-    CodeSelectParams qs{at<float>(ws, L.q_route), at<float>(ws, L.cb_norm), q_codes,
-                        static_cast<int64_t>(a.batch) * a.h_kv, a.n_q, a.h_kv, a.codebook_heads,
-                        a.n_codes, a.d_s, a.a, a.temperature};
-    e = launch_code_select(qs, st);
+    e = score_and_select(a, L, ws, at<float>(ws, L.q_route), a.n_q, a.a, q_codes, st);
     if (e != cudaSuccess) return cuda_status(e, "code_select(q)");
   }
   return SSA_OK;

@@ -1,0 +1,480 @@
+// K1 on the 5th-generation tensor cores: codebook scoring with the top-a /
+// top-b code selection fused into the epilogue.
+//
+// Reference: ssa/router.py:116-141 -- cosine scores of every routed query /
+// key against every code of its KV head's codebook, then topk.  The score
+// matrix [rows, N_c] is never written to memory here: each 128-row tile's
+// scores live in TMEM one 256-code chunk at a time and are reduced to a
+// per-row top-K list by the epilogue warps.
+//
+// Precision: routed vectors and codes are unit vectors in fp32.  Each is split
+// into an f16 pair hi + lo (hi = f16(x), lo = f16(x - hi)); one kind::f16 MMA
+// with K = 3*d_s evaluates  a_hi.c_hi + a_lo.c_hi + a_hi.c_lo  with fp32
+// accumulation, which carries ~22 significant bits -- close enough to fp32
+// that code selection agrees with an fp32/fp64 evaluation except at genuine
+// near-ties.  A row = [a_hi | a_lo | a_hi], B row = [c_hi | c_hi | c_lo].
+//
+// CTA layout (one persistent CTA per SM, static round-robin over tiles):
+//   warp 0      producer: 1-D bulk copies (cp.async.bulk) of pre-laid-out
+//               codebook chunks into a 3-stage shared-memory ring;
+//   warp 1      TMEM allocation and the single-thread tcgen05.mma issuer
+//               (M=128, N=256, K=16 per instruction) into a double-buffered
+//               accumulator (2 x 256 TMEM columns);
+//   warps 2-9   epilogue, two warpgroups: each thread owns one row (TMEM lane)
+//               and half of every chunk's columns; tcgen05.ld -> register
+//               top-K list; the two halves merge at the end of the tile.
+//               The same warps build the next tile's A operand in shared
+//               memory while the current tile's MMAs run.
+// Operands use the K-major SWIZZLE_NONE canonical layout: 8-row x 16-byte
+// core matrices, SBO = 128 B between 8-row groups, LBO between 16-byte K
+// groups.
+//
+// Every wait is bounded (about one second); on expiry the CTA records an
+// error bit, stops issuing work, waits (bounded) for its copies and MMAs in
+// flight, frees TMEM and exits.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace ssa {
+namespace tc {
+
+constexpr int kM = 128;
+constexpr int kN = 256;
+constexpr int kStages = 3;
+constexpr int kEpiWG = 2;
+constexpr int kEpiWarps = 4 * kEpiWG;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kColsPerWG = kN / kEpiWG;
+constexpr uint64_t kWaitNs = 1000000000ull;   // 1 s
+
+template <int DS>
+struct Geo {
+  static constexpr int K = 3 * DS;
+  static constexpr int KG = K / 8;                 // 16-byte K groups per row
+  static constexpr int KSTEPS = K / 16;            // MMA instructions per chunk
+  static constexpr int A_LBO = (kM / 8) * 128;
+  static constexpr int B_LBO = (kN / 8) * 128;
+  static constexpr int A_BYTES = kM * K * 2;
+  static constexpr int B_BYTES = kN * K * 2;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: false after ~1 s (the caller then aborts).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    if (mbar_try(bar, parity)) return true;
+    if (globaltimer() - t0 > kWaitNs) return false;
+  }
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= 1ull << 46;                                   // descriptor version (sm_100)
+  return d;                                          // base offset 0, SWIZZLE_NONE
+}
+// kind::f16 instruction descriptor: D f32, A/B f16, both K-major, N=256, M=128.
+constexpr uint32_t kIdesc = (1u << 4) | (static_cast<uint32_t>(kN >> 3) << 17) |
+                            (static_cast<uint32_t>(kM >> 4) << 24);
+
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t ad, uint64_t bd, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(ad), "l"(bd), "r"(kIdesc), "r"(acc));
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]),
+        "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]),
+        "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Byte offset of element k of row r in a K-major SWIZZLE_NONE image whose K
+// groups are LBO bytes apart.
+__device__ __forceinline__ uint32_t img_off(int r, int kgroup, int lbo) {
+  return static_cast<uint32_t>(kgroup * lbo + (r >> 3) * 128 + (r & 7) * 16);
+}
+
+template <int DS, int KMAX>
+__global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcParams p) {
+  using G = Geo<DS>;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  unsigned char* a_img = base;                                   // 2 x A_BYTES
+  unsigned char* b_img = a_img + 2 * G::A_BYTES;                 // kStages x B_BYTES
+  uint64_t* merge_k = reinterpret_cast<uint64_t*>(b_img + kStages * G::B_BYTES);   // [kEpiWG-1][kM][KMAX]
+  uint64_t* bars = merge_k + (kEpiWG - 1) * kM * KMAX;
+  // barriers: b_full[kStages], b_empty[kStages], t_full[2], t_empty[2], a_ready[2]
+  const uint32_t b_full = smem_u32(bars);
+  const uint32_t b_empty = b_full + 8 * kStages;
+  const uint32_t t_full = b_empty + 8 * kStages;
+  const uint32_t t_empty = t_full + 16;
+  const uint32_t a_ready = t_empty + 16;
+  const uint32_t m_bar = a_ready + 16;           // epilogue-only barriers around the merge
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+  const int chunks = p.n_codes / kN;
+  const int64_t total_tiles = p.batch_heads * p.tiles_per_head;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(b_full + 8 * s, 1);
+      mbar_init(b_empty + 8 * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(t_full + 8 * b, 1);
+      mbar_init(t_empty + 8 * b, kEpiWarps);
+      mbar_init(a_ready + 8 * b, kEpiWarps);
+      mbar_init(m_bar + 8 * b, kEpiWarps);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(2 * kN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  auto fail = [&]() {
+    *abort_flag = 1;
+    if (p.error) atomicOr(p.error, 0x100);
+  };
+  // barrier of the epilogue warps only (mbarrier, bounded wait)
+  auto epi_sync = [&](uint32_t bar, uint32_t parity) {
+    __syncwarp();
+    if ((threadIdx.x % kWarp) == 0) mbar_arrive(bar);
+    return mbar_wait(bar, parity);
+  };
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      int64_t g = 0;
+      for (int64_t tile = blockIdx.x; tile < total_tiles && !*abort_flag; tile += gridDim.x) {
+        const int64_t bh = tile / p.tiles_per_head;
+        const int h = static_cast<int>(bh % p.h_kv);
+        const int cbh = p.codebook_heads == 1 ? 0 : h;
+        const unsigned char* src = p.image + static_cast<int64_t>(cbh) * chunks * G::B_BYTES;
+        for (int c = 0; c < chunks; ++c, ++g) {
+          const int s = static_cast<int>(g % kStages);
+          const uint32_t ph = static_cast<uint32_t>((g / kStages) & 1);
+          if (*abort_flag || !mbar_wait(b_empty + 8 * s, ph ^ 1u)) { fail(); break; }
+          mbar_expect_tx(b_full + 8 * s, G::B_BYTES);
+          bulk_g2s(smem_u32(b_img + s * G::B_BYTES), src + static_cast<int64_t>(c) * G::B_BYTES,
+                   G::B_BYTES, b_full + 8 * s);
+        }
+      }
+      // drain: every issued copy must have landed before the CTA exits
+      for (int64_t r = g - 1; r >= 0 && r >= g - kStages; --r) {
+        const int s = static_cast<int>(r % kStages);
+        mbar_wait(b_full + 8 * s, static_cast<uint32_t>((r / kStages) & 1));
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      int64_t g = 0, tl = 0;
+      bool issued = false;
+      for (int64_t tile = blockIdx.x; tile < total_tiles && !*abort_flag; tile += gridDim.x, ++tl) {
+        const int ab = static_cast<int>(tl & 1);
+        if (!mbar_wait(a_ready + 8 * ab, static_cast<uint32_t>((tl >> 1) & 1))) { fail(); break; }
+        fence_after();
+        const uint32_t a_base = smem_u32(a_img + ab * G::A_BYTES);
+        for (int c = 0; c < chunks; ++c, ++g) {
+          const int s = static_cast<int>(g % kStages);
+          const int buf = static_cast<int>(g & 1);
+          if (*abort_flag || !mbar_wait(b_full + 8 * s, static_cast<uint32_t>((g / kStages) & 1)) ||
+              !mbar_wait(t_empty + 8 * buf, static_cast<uint32_t>(((g >> 1) & 1) ^ 1))) {
+            fail();
+            break;
+          }
+          fence_after();
+          const uint32_t b_base = smem_u32(b_img + s * G::B_BYTES);
+          const uint32_t d = tmem_base + static_cast<uint32_t>(buf * kN);
+#pragma unroll
+          for (int ks = 0; ks < G::KSTEPS; ++ks) {
+            const uint64_t ad = sdesc(a_base + ks * 2 * G::A_LBO, G::A_LBO, 128);
+            const uint64_t bd = sdesc(b_base + ks * 2 * G::B_LBO, G::B_LBO, 128);
+            mma_f16(d, ad, bd, ks > 0 ? 1u : 0u);
+          }
+          mma_commit(b_empty + 8 * s);
+          mma_commit(t_full + 8 * buf);
+          issued = true;
+        }
+      }
+      if (issued) {   // the last commit covers every MMA issued: wait before TMEM is freed
+        const int64_t r = g - 1;
+        mbar_wait(t_full + 8 * (r & 1), static_cast<uint32_t>((r >> 1) & 1));
+      }
+    }
+  } else {
+    // ---------------- epilogue ----------------
+    const int ew = warp - 2;
+    const int wg = ew / 4;
+    const int quarter = warp & 3;                 // TMEM lane quarter of this warp
+    const int r = quarter * 32 + lane;            // row within the tile
+    const float inv_t = 1.0f / p.temperature;
+    const bool unit_t = p.temperature == 1.0f;
+
+    auto build_a = [&](int64_t tile, int ab) {
+      const int64_t bh = tile / p.tiles_per_head;
+      const int64_t i = (tile % p.tiles_per_head) * kM + r;
+      const bool valid = i < p.n_rows;
+      float x[DS];
+      if (valid) {
+        const float4* src = reinterpret_cast<const float4*>(p.route + (bh * p.n_rows + i) * DS);
+#pragma unroll
+        for (int e = 0; e < DS / 4; ++e) {
+          const float4 t = src[e];
+          x[4 * e] = t.x; x[4 * e + 1] = t.y; x[4 * e + 2] = t.z; x[4 * e + 3] = t.w;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < DS; ++e) x[e] = 0.f;
+      }
+      unsigned char* img = a_img + ab * G::A_BYTES;
+      // K groups: [0, DS/8) hi, [DS/8, 2DS/8) lo, [2DS/8, 3DS/8) hi
+#pragma unroll
+      for (int kg = 0; kg < G::KG; ++kg) {
+        if (kg % kEpiWG != wg) continue;
+        const int part = kg / (DS / 8);
+        const int e0 = (kg % (DS / 8)) * 8;
+        uint32_t w[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          __half h2[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const float v = x[e0 + 2 * t + u];
+            const __half hi = __float2half_rn(v);
+            h2[u] = part == 1 ? __float2half_rn(v - __half2float(hi)) : hi;
+          }
+          w[t] = static_cast<uint32_t>(__half_as_ushort(h2[0])) |
+                 (static_cast<uint32_t>(__half_as_ushort(h2[1])) << 16);
+        }
+        *reinterpret_cast<uint4*>(img + img_off(r, kg, G::A_LBO)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(a_ready + 8 * ab);
+    };
+
+    int64_t g = 0, tl = 0;
+    if (static_cast<int64_t>(blockIdx.x) < total_tiles) build_a(blockIdx.x, 0);
+    for (int64_t tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++tl) {
+      if (*abort_flag) break;
+      const int64_t next = tile + gridDim.x;
+      if (next < total_tiles) build_a(next, static_cast<int>((tl + 1) & 1));
+      TopList<KMAX> top;
+      top.init();
+      bool ok = true;
+      for (int c = 0; c < chunks; ++c, ++g) {
+        const int buf = static_cast<int>(g & 1);
+        if (*abort_flag || !mbar_wait(t_full + 8 * buf, static_cast<uint32_t>((g >> 1) & 1))) {
+          fail();
+          ok = false;
+          break;
+        }
+        fence_after();
+        const int col_base = c * kN + wg * kColsPerWG;
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                               static_cast<uint32_t>(buf * kN + wg * kColsPerWG);
+#pragma unroll 1
+        for (int part = 0; part < kColsPerWG / 32; ++part) {
+          uint32_t v[32];
+          tmem_ld32(taddr + part * 32, v);
+          if (part == kColsPerWG / 32 - 1) {    // accumulator drained: release it to the MMA warp
+            fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(t_empty + 8 * buf);
+          }
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float s = __uint_as_float(v[j]);
+            if (!unit_t) s = s * inv_t;
+            top.push(s, static_cast<uint32_t>(col_base + part * 32 + j));
+          }
+        }
+      }
+      if (!ok) break;
+      // merge the warpgroups' lists (ranking keys are unique: plain key inserts)
+      if (wg > 0) {
+#pragma unroll
+        for (int t = 0; t < KMAX; ++t) merge_k[((wg - 1) * kM + r) * KMAX + t] = top.key[t];
+      }
+      if (!epi_sync(m_bar, static_cast<uint32_t>(tl & 1))) { fail(); break; }
+      if (wg == 0) {
+        for (int w2 = 1; w2 < kEpiWG; ++w2)
+#pragma unroll
+          for (int t = 0; t < KMAX; ++t) {
+            const uint64_t kv = merge_k[((w2 - 1) * kM + r) * KMAX + t];
+            if (kv > top.key[KMAX - 1]) top.insert_key(kv);
+          }
+        const int64_t bh = tile / p.tiles_per_head;
+        const int64_t i = (tile % p.tiles_per_head) * kM + r;
+        if (i < p.n_rows) {
+          const int h = static_cast<int>(bh % p.h_kv);
+          const int64_t bat = bh / p.h_kv;
+          int32_t* out = p.codes + ((bat * p.n_rows + i) * p.h_kv + h) * p.kk;
+#pragma unroll
+          for (int t = 0; t < KMAX; ++t)
+            if (t < p.kk) out[t] = top.index(t);
+        }
+      }
+      if (!epi_sync(m_bar + 8, static_cast<uint32_t>(tl & 1))) { fail(); break; }
+    }
+  }
+
+  fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(2 * kN));
+  }
+}
+
+// Codebook chunk images: for head h and chunk c, the B operand of one MMA
+// chunk in the K-major SWIZZLE_NONE layout, rows = codes, K = [hi | hi | lo].
+template <int DS>
+__global__ void codebook_image_kernel(const float* cbn, unsigned char* img, int64_t heads, int n_codes) {
+  using G = Geo<DS>;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (t >= heads * n_codes) return;
+  const int64_t h = t / n_codes;
+  const int code = static_cast<int>(t % n_codes);
+  const int chunk = code / kN, rr = code % kN;
+  const float* x = cbn + t * DS;
+  unsigned char* dst = img + (h * (n_codes / kN) + chunk) * static_cast<int64_t>(G::B_BYTES);
+  for (int kg = 0; kg < G::KG; ++kg) {
+    const int part = kg / (DS / 8);
+    const int e0 = (kg % (DS / 8)) * 8;
+    uint32_t w[4];
+    for (int q = 0; q < 4; ++q) {
+      __half h2[2];
+      for (int u = 0; u < 2; ++u) {
+        const float v = x[e0 + 2 * q + u];
+        const __half hi = __float2half_rn(v);
+        h2[u] = part == 2 ? __float2half_rn(v - __half2float(hi)) : hi;
+      }
+      w[q] = static_cast<uint32_t>(__half_as_ushort(h2[0])) |
+             (static_cast<uint32_t>(__half_as_ushort(h2[1])) << 16);
+    }
+    *reinterpret_cast<uint4*>(dst + img_off(rr, kg, G::B_LBO)) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+template <int DS>
+size_t smem_bytes(int kmax) {
+  using G = Geo<DS>;
+  return 1024 + 2 * G::A_BYTES + kStages * G::B_BYTES + 2 * (kEpiWG - 1) * kM * kmax * 4 +
+         (2 * kStages + 8) * 8 + 16;
+}
+
+}  // namespace tc
+
+bool code_score_tc_supported(int d_s, int n_codes) {
+  return (d_s == 16 || d_s == 32) && n_codes % tc::kN == 0 && n_codes >= tc::kN;
+}
+
+size_t codebook_image_bytes(int heads, int n_codes, int d_s) {
+  return static_cast<size_t>(heads) * n_codes * 3 * d_s * 2;
+}
+
+cudaError_t launch_codebook_image(const float* cbn, void* img, int heads, int n_codes, int d_s,
+                                  cudaStream_t st) {
+  const int64_t n = static_cast<int64_t>(heads) * n_codes;
+  const unsigned blocks = static_cast<unsigned>(cdiv(n, 256));
+  if (d_s == 16) tc::codebook_image_kernel<16><<<blocks, 256, 0, st>>>(cbn, static_cast<unsigned char*>(img), heads, n_codes);
+  else tc::codebook_image_kernel<32><<<blocks, 256, 0, st>>>(cbn, static_cast<unsigned char*>(img), heads, n_codes);
+  return cudaGetLastError();
+}
+
+template <int DS, int KMAX>
+static cudaError_t launch_tc(const CodeScoreTcParams& p, cudaStream_t st) {
+  const size_t smem = tc::smem_bytes<DS>(KMAX);
+  auto kern = tc::code_score_tc_kernel<DS, KMAX>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t tiles = p.batch_heads * p.tiles_per_head;
+  const unsigned grid = static_cast<unsigned>(tiles < sms ? tiles : sms);
+  if (grid == 0) return cudaSuccess;
+  kern<<<grid, tc::kThreads, smem, st>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_code_score_tc(const CodeScoreTcParams& p, int d_s, cudaStream_t st) {
+  if (d_s == 32) {
+    if (p.kk <= 4) return launch_tc<32, 4>(p, st);
+    if (p.kk <= 8) return launch_tc<32, 8>(p, st);
+    if (p.kk <= 16) return launch_tc<32, 16>(p, st);
+    return launch_tc<32, 32>(p, st);
+  }
+  if (p.kk <= 4) return launch_tc<16, 4>(p, st);
+  if (p.kk <= 8) return launch_tc<16, 8>(p, st);
+  if (p.kk <= 16) return launch_tc<16, 16>(p, st);
+  return launch_tc<16, 32>(p, st);
+}
+
+}  // namespace ssa

@@ -83,39 +83,48 @@ __device__ __forceinline__ uint32_t rank_key_index(uint64_t key) {
   return ~static_cast<uint32_t>(key & 0xffffffffull);
 }
 
+__device__ __forceinline__ float float_from_key(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k ^ 0x80000000u) : ~k);
+}
+
 // ---------------------------------------------------------------------------
-// Sorted top-K list kept in registers by one thread (K small, static indices).
-// Elements are pushed in increasing index order; an element enters only if it
-// beats the current K-th score strictly, and is placed after every element
-// with an equal score -- so among equal scores the lower index wins, and the
-// list is ordered by (score desc, index asc).
+// Sorted top-K list kept in registers by one thread (K small, static indices),
+// ordered by (score desc, index asc).  Entries are 64-bit ranking keys
+// rank_key(score, index), compared as integers: keys are unique, so the order
+// is total and the tie rule (lower index first) holds whatever the order in
+// which elements are pushed.  Key 0 marks an empty slot (below every real key).
+// `thr` caches the K-th score as a float for a cheap pre-filter: an element
+// can enter only if score >= thr.
 // ---------------------------------------------------------------------------
 template <int K>
 struct TopList {
-  float s[K];
-  int32_t i[K];
+  uint64_t key[K];
+  float thr;
   __device__ __forceinline__ void init() {
 #pragma unroll
-    for (int t = 0; t < K; ++t) { s[t] = -INFINITY; i[t] = -1; }
+    for (int t = 0; t < K; ++t) key[t] = 0ull;
+    thr = -INFINITY;
   }
-  __device__ __forceinline__ float threshold() const { return s[K - 1]; }
-  // precondition: v > threshold() (or the list is not yet full: threshold -inf
-  // and v > -inf).  The list's i[] of empty slots is -1.
-  __device__ __forceinline__ void insert(float v, int32_t idx) {
-    // bubble the new element up from the bottom
-    float cs = v;
-    int32_t ci = idx;
+  __device__ __forceinline__ void insert_key(uint64_t kv) {
+    uint64_t c = kv;
 #pragma unroll
     for (int t = 0; t < K; ++t) {
-      // slot t takes the larger of (s[t], cs); ties keep the existing (lower index)
-      const bool take = cs > s[t];
-      const float ts = s[t];
-      const int32_t ti = i[t];
-      s[t] = take ? cs : ts;
-      i[t] = take ? ci : ti;
-      cs = take ? ts : cs;
-      ci = take ? ti : ci;
+      const uint64_t cur = key[t];
+      const bool take = c > cur;
+      key[t] = take ? c : cur;
+      c = take ? cur : c;
     }
+    thr = key[K - 1] ? float_from_key(static_cast<uint32_t>(key[K - 1] >> 32)) : -INFINITY;
+  }
+  // Offer (score, idx); -0.0 is folded into +0.0 by rank_key.
+  __device__ __forceinline__ void push(float score, uint32_t idx) {
+    if (score >= thr) {
+      const uint64_t kv = rank_key(score, idx);
+      if (kv > key[K - 1]) insert_key(kv);
+    }
+  }
+  __device__ __forceinline__ int32_t index(int t) const {
+    return key[t] ? static_cast<int32_t>(rank_key_index(key[t])) : -1;
   }
 };
 

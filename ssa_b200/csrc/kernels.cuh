@@ -29,6 +29,17 @@ struct CodeSelectParams {
   float temperature;
 };
 
+// K1 on tcgen05: rows in (bat, h, i) order, tiles of 128 rows within a head.
+struct CodeScoreTcParams {
+  const float* route;            // [batch_heads * n_rows, d_s] normalised
+  const unsigned char* image;    // codebook chunk images [codebook_heads][n_codes/256][...]
+  int32_t* codes;                // out [B, n_rows, h_kv, kk]
+  int32_t* error;                // optional device status word
+  int64_t batch_heads, n_rows, tiles_per_head;
+  int h_kv, codebook_heads, n_codes, kk;
+  float temperature;
+};
+
 // K2: code -> key inverted index.
 struct IndexParams {
   const int32_t* k_codes;  // [B, n, h_kv, b]
@@ -76,6 +87,11 @@ cudaError_t launch_route_project(const RouteProjectParams& p, ssa_dtype xt, ssa_
 cudaError_t launch_codebook_normalize(const void* cb, ssa_dtype wt, float* out, int64_t rows,
                                       int d_s, cudaStream_t st);
 cudaError_t launch_code_select(const CodeSelectParams& p, cudaStream_t st);
+bool code_score_tc_supported(int d_s, int n_codes);
+size_t codebook_image_bytes(int heads, int n_codes, int d_s);
+cudaError_t launch_codebook_image(const float* cbn, void* img, int heads, int n_codes, int d_s,
+                                  cudaStream_t st);
+cudaError_t launch_code_score_tc(const CodeScoreTcParams& p, int d_s, cudaStream_t st);
 cudaError_t launch_select_from_scores(const float* scores, int64_t rows, int n_cols, int kk,
                                       int32_t* out, cudaStream_t st);
 cudaError_t launch_build_index(const IndexParams& p, cudaStream_t st);

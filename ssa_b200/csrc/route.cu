@@ -141,7 +141,7 @@ __global__ void __launch_bounds__(kSelThreads) code_select_kernel(CodeSelectPara
         s = fmaf(r[4 * e + 3], w.w, s);
       }
       if (!unit_temp) s = s / p.temperature;
-      if (s > top.threshold()) top.insert(s, c0 + c);
+      top.push(s, static_cast<uint32_t>(c0 + c));
     }
   }
   if (!active) return;
@@ -149,7 +149,7 @@ __global__ void __launch_bounds__(kSelThreads) code_select_kernel(CodeSelectPara
   int32_t* out = p.codes + ((bat * p.n_rows + i) * p.h_kv + h) * p.kk;
 #pragma unroll
   for (int t = 0; t < KMAX; ++t)
-    if (t < p.kk) out[t] = top.i[t];
+    if (t < p.kk) out[t] = top.index(t);
 }
 
 // Selection on fed scores: the same TopList with the same push order.
@@ -162,12 +162,11 @@ __global__ void select_from_scores_kernel(const float* scores, int64_t rows, int
   top.init();
   const float* s = scores + r * n_cols;
   for (int c = 0; c < n_cols; ++c) {
-    const float v = s[c];
-    if (v > top.threshold()) top.insert(v, c);
+    top.push(s[c], static_cast<uint32_t>(c));
   }
 #pragma unroll
   for (int t = 0; t < KMAX; ++t)
-    if (t < kk) out[r * kk + t] = top.i[t];
+    if (t < kk) out[r * kk + t] = top.index(t);
 }
 
 // ---------------------------------------------------------------------------

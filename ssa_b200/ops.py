@@ -121,10 +121,15 @@ def route(q: torch.Tensor, k: torch.Tensor, w_qr: torch.Tensor, w_kr: torch.Tens
     counts = torch.empty((B, n_q, h_kv), dtype=torch.int32, device=dev)
     args = route_args(q, k, w_qr, w_kr, codebook, a, b, top_k, causal, temperature, q_offset,
                       indices, index_i64, q_codes, k_codes, counts)
+    check = _checked() and not torch.cuda.is_current_stream_capturing()
+    status = torch.zeros(1, dtype=torch.int32, device=dev) if check else None
+    args.status = _ptr(status)
     ws = workspace(args, dev)
     with torch.cuda.device(dev):
         L.check("ssa_route", L.lib().ssa_route(ctypes.byref(args), ws.data_ptr(), ws.numel(),
                                                _stream(dev)))
+    if status is not None and int(status.item()) & L.SSA_DEVICE_TIMEOUT:
+        raise RuntimeError("ssa_route: a device pipeline wait timed out; results are undefined")
     return indices, q_codes, k_codes, counts
 
 

@@ -17,6 +17,7 @@ import torch
 import ssa_b200 as ssa
 from oracle import ssa_oracle as O
 from ssa_b200 import workloads as W
+from _tol import assert_output_close
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -104,12 +105,11 @@ def test_config3_slice_overlap_bf16():
     v = t["v"]
     out = ssa.sparse_exact_attention(t["q"][0], t["k"][0], v[0], idx[0], is_causal=True)
     ref_out = O.sparse_attention(qn, kn, v[0].double().cpu().numpy(), idx[0].cpu().numpy(), causal=True)
-    err = np.abs(out.double().cpu().numpy() - ref_out)
-    assert (err <= 1e-4 + 2e-3 * np.abs(ref_out)).all()
+    assert_output_close(out, ref_out, torch.bfloat16)
 
 
-@pytest.mark.parametrize("dtype,atol", [(torch.float32, 1e-5), (torch.bfloat16, 2e-3)])
-def test_k_equals_n_reproduces_dense(dtype, atol):
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_k_equals_n_reproduces_dense(dtype):
     shape = W.CONFIG2
     t = W.make_inputs(shape, seed=2, dtype=dtype, planted=False)
     r = ssa.CodebookRouter(head_dim=64, route_dim=32, num_kv_heads=2, num_codebook=1024,
@@ -121,8 +121,35 @@ def test_k_equals_n_reproduces_dense(dtype, atol):
     out = ssa.sparse_exact_attention(q, k, v, idx, is_causal=True)
     qd, kd, vd = q.double(), k.double(), v.double()
     dense = ssa.dense_attention(qd, kd, vd, causal_mask=ssa.build_causal_mask(4096, device=DEV))
-    err = (out.double() - dense).abs()
-    assert float(err.max()) <= atol + atol * float(dense.abs().max()), float(err.max())
+    assert_output_close(out, dense, dtype)
+
+
+@pytest.mark.parametrize("d_s,n_codes,shared_cb,temp,dtype", [
+    (32, 512, False, 1.0, torch.float32),
+    (16, 1024, True, 0.7, torch.bfloat16),
+    (32, 4096, False, 1.0, torch.bfloat16),
+])
+def test_tensor_core_code_selection_matches_oracle(d_s, n_codes, shared_cb, temp, dtype):
+    """Shapes that take the tcgen05 scoring path (d_s 16/32, N_c % 256 == 0);
+    row counts are not multiples of the 128-row tile; batch of 2."""
+    B, n, h_q, h_kv, d, a, b = 2, 1000, 8, 2, 64, 16, 4
+    g = torch.Generator().manual_seed(n_codes + d_s)
+    q = torch.randn(B, n, h_q, d, generator=g).to(DEV, dtype)
+    k = torch.randn(B, n, h_kv, d, generator=g).to(DEV, dtype)
+    r = ssa.CodebookRouter(head_dim=d, route_dim=d_s, num_kv_heads=h_kv, num_codebook=n_codes,
+                           codes_per_key=b, codes_per_query=a, top_k=32, temperature=temp).to(DEV)
+    if shared_cb:
+        r.codebook = torch.nn.Parameter(torch.randn(n_codes, d_s, generator=g).to(DEV) / d_s ** 0.5)
+    _, q_codes, k_codes, _ = r.route(q, k, causal=True)
+    w = lambda p: p.detach().double().cpu().numpy()
+    for bi in range(B):
+        oq, ok = O.route_codes(q[bi].double().cpu().numpy(), k[bi].double().cpu().numpy(), w(r.W_qr.weight),
+                               w(r.W_kr.weight), w(r.codebook), a, b, temperature=temp)
+        q_rows = (np.sort(q_codes[bi].cpu().numpy(), -1) == np.sort(oq, -1)).all(-1).mean()
+        k_rows = (np.sort(k_codes[bi].cpu().numpy(), -1) == np.sort(ok, -1)).all(-1).mean()
+        assert q_rows >= 0.999 and k_rows >= 0.999, (q_rows, k_rows)
+    kc = r.get_code_assignment(k)
+    assert torch.equal(kc.int(), k_codes)
 
 
 def test_batched_module_matches_per_sequence_calls():
