@@ -50,7 +50,7 @@ int rescore_cap(int k_eff) {
 // Workspace regions for a route call.
 struct RouteLayout {
   size_t q_route, k_route, cb_norm, cb_image, q_codes, k_codes, counts, partials, bucket_ptr,
-      bucket_keys;
+      bucket_keys, ovf;
   size_t total;
   int tiles;
   int64_t chunks;
@@ -76,6 +76,7 @@ RouteLayout route_layout(const SsaRouteArgs& a) {
   L.partials = take(static_cast<size_t>(B * hk * L.chunks) * 4);
   L.bucket_ptr = take(static_cast<size_t>(B * hk) * (a.n_codes + 1) * 4);
   L.bucket_keys = take(static_cast<size_t>(B * hk) * a.n * a.b * 4);
+  L.ovf = take((1 + static_cast<size_t>(B * hk) * a.n_q) * 4);   // overflow count + unit list
   L.total = off;
   return L;
 }
@@ -229,6 +230,8 @@ ssa_status run_stage2(const SsaRouteArgs& a, const RouteLayout& L, void* ws, cud
   rp.h_kv = a.h_kv; rp.group = a.h_q / a.h_kv; rp.d = a.d; rp.a = a.a; rp.b = a.b;
   rp.n_codes = a.n_codes; rp.top_k = a.top_k; rp.causal = a.causal ? 1 : 0;
   rp.cap = rescore_cap(std::min(a.top_k, a.n));
+  rp.ovf_count = at<int32_t>(ws, L.ovf);
+  rp.ovf_list = at<int32_t>(ws, L.ovf) + 1;
   e = launch_rescore(rp, a.dtype, st);
   return cuda_status(e, "rescore_topk");
 }

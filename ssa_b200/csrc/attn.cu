@@ -29,8 +29,8 @@ __global__ void __launch_bounds__(kAttnWarps * kWarp) sparse_attn_kernel(AttnPar
   const int64_t unit = static_cast<int64_t>(blockIdx.x) * kAttnWarps + warp;
   const int64_t units = static_cast<int64_t>(p.n_q) * bhs;
   if (unit >= units) return;
-  const int i = static_cast<int>(unit / bhs);
-  const int r = static_cast<int>(unit % bhs);
+  const int r = static_cast<int>(unit / p.n_q);          // head-major order
+  const int i = static_cast<int>(unit % p.n_q);
   const int bat = r / p.h_kv, h = r % p.h_kv;
   const int d = p.d, g = p.group;
   float* qs = qs_all + static_cast<int64_t>(warp) * GMAX * d;
@@ -177,6 +177,7 @@ static cudaError_t launch_attn_t(const AttnParams& p, cudaStream_t st) {
 
 cudaError_t launch_sparse_attn(const AttnParams& p, ssa_dtype dt, cudaStream_t st) {
   if (static_cast<int64_t>(p.n_q) * p.batch * p.h_kv == 0) return cudaSuccess;
+  if (sparse_attn_mma_supported(p, dt)) return launch_sparse_attn_mma(p, dt, st);
   if (dt == SSA_F32) return launch_attn_t<float>(p, st);
   if (dt == SSA_BF16) return launch_attn_t<__nv_bfloat16>(p, st);
   return launch_attn_t<__half>(p, st);

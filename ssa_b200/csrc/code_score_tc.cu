@@ -40,7 +40,8 @@ namespace tc {
 
 constexpr int kM = 128;
 constexpr int kN = 256;
-constexpr int kStages = 3;
+constexpr int kStages = 2;
+constexpr int kCand = 16;          // pass-2 candidates buffered per thread
 constexpr int kEpiWG = 2;
 constexpr int kEpiWarps = 4 * kEpiWG;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
@@ -146,23 +147,49 @@ __device__ __forceinline__ uint32_t img_off(int r, int kgroup, int lbo) {
   return static_cast<uint32_t>(kgroup * lbo + (r >> 3) * 128 + (r & 7) * 16);
 }
 
+// Static bitonic sort (descending) of N floats held in registers.
+template <int N>
+__device__ __forceinline__ void sort_desc(float (&x)[N]) {
+#pragma unroll
+  for (int k2 = 2; k2 <= N; k2 <<= 1) {
+#pragma unroll
+    for (int j = k2 >> 1; j > 0; j >>= 1) {
+#pragma unroll
+      for (int e = 0; e < N; ++e) {
+        const int f = e ^ j;
+        if (f > e) {
+          const float a = x[e], b = x[f];
+          const bool desc = (e & k2) == 0;
+          x[e] = desc ? fmaxf(a, b) : fminf(a, b);
+          x[f] = desc ? fminf(a, b) : fmaxf(a, b);
+        }
+      }
+    }
+  }
+}
+
 template <int DS, int KMAX>
 __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcParams p) {
   using G = Geo<DS>;
+  constexpr int HI_KSTEPS = DS / 16;                      // pass 1: a_hi . c_hi only
+  constexpr uint32_t HI_BYTES = (DS / 8) * G::B_LBO;      // the c_hi third of a chunk image
+  constexpr int EPI = 32 * kEpiWarps;                     // epilogue threads
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  unsigned char* a_img = base;                                   // 2 x A_BYTES
-  unsigned char* b_img = a_img + 2 * G::A_BYTES;                 // kStages x B_BYTES
-  uint64_t* merge_k = reinterpret_cast<uint64_t*>(b_img + kStages * G::B_BYTES);   // [kEpiWG-1][kM][KMAX]
-  uint64_t* bars = merge_k + (kEpiWG - 1) * kM * KMAX;
-  // barriers: b_full[kStages], b_empty[kStages], t_full[2], t_empty[2], a_ready[2]
+  unsigned char* a_img = base;                                        // 2 x A_BYTES
+  unsigned char* b_img = a_img + 2 * G::A_BYTES;                      // kStages x B_BYTES
+  uint64_t* cand = reinterpret_cast<uint64_t*>(b_img + kStages * G::B_BYTES);   // [kCand][EPI]
+  uint64_t* merge_k = cand + kCand * EPI;                             // [kEpiWG-1][kM][KMAX]
+  float* bound = reinterpret_cast<float*>(merge_k + (kEpiWG - 1) * kM * KMAX);  // [kEpiWG][kM]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(bound + kEpiWG * kM);
+  // barriers: b_full[kStages], b_empty[kStages], t_full[2], t_empty[2], a_ready[2], m_bar[2]
   const uint32_t b_full = smem_u32(bars);
   const uint32_t b_empty = b_full + 8 * kStages;
   const uint32_t t_full = b_empty + 8 * kStages;
   const uint32_t t_empty = t_full + 16;
   const uint32_t a_ready = t_empty + 16;
-  const uint32_t m_bar = a_ready + 16;           // epilogue-only barriers around the merge
+  const uint32_t m_bar = a_ready + 16;           // epilogue-only barriers
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -206,21 +233,25 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
   };
 
   if (warp == 0) {
-    // ---------------- producer ----------------
+    // ---------------- producer: every tile streams its codebook twice ----------------
     if (lane == 0) {
       int64_t g = 0;
-      for (int64_t tile = blockIdx.x; tile < total_tiles && !*abort_flag; tile += gridDim.x) {
+      bool stop = false;
+      for (int64_t tile = blockIdx.x; tile < total_tiles && !stop; tile += gridDim.x) {
         const int64_t bh = tile / p.tiles_per_head;
         const int h = static_cast<int>(bh % p.h_kv);
         const int cbh = p.codebook_heads == 1 ? 0 : h;
         const unsigned char* src = p.image + static_cast<int64_t>(cbh) * chunks * G::B_BYTES;
-        for (int c = 0; c < chunks; ++c, ++g) {
-          const int s = static_cast<int>(g % kStages);
-          const uint32_t ph = static_cast<uint32_t>((g / kStages) & 1);
-          if (*abort_flag || !mbar_wait(b_empty + 8 * s, ph ^ 1u)) { fail(); break; }
-          mbar_expect_tx(b_full + 8 * s, G::B_BYTES);
-          bulk_g2s(smem_u32(b_img + s * G::B_BYTES), src + static_cast<int64_t>(c) * G::B_BYTES,
-                   G::B_BYTES, b_full + 8 * s);
+        for (int pass = 0; pass < 2 && !stop; ++pass) {
+          const uint32_t bytes = pass == 0 ? HI_BYTES : static_cast<uint32_t>(G::B_BYTES);
+          for (int c = 0; c < chunks; ++c, ++g) {
+            const int s = static_cast<int>(g % kStages);
+            const uint32_t ph = static_cast<uint32_t>((g / kStages) & 1);
+            if (*abort_flag || !mbar_wait(b_empty + 8 * s, ph ^ 1u)) { fail(); stop = true; break; }
+            mbar_expect_tx(b_full + 8 * s, bytes);
+            bulk_g2s(smem_u32(b_img + s * G::B_BYTES), src + static_cast<int64_t>(c) * G::B_BYTES, bytes,
+                     b_full + 8 * s);
+          }
         }
       }
       // drain: every issued copy must have landed before the CTA exits
@@ -233,32 +264,35 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       int64_t g = 0, tl = 0;
-      bool issued = false;
-      for (int64_t tile = blockIdx.x; tile < total_tiles && !*abort_flag; tile += gridDim.x, ++tl) {
+      bool issued = false, stop = false;
+      for (int64_t tile = blockIdx.x; tile < total_tiles && !stop; tile += gridDim.x, ++tl) {
         const int ab = static_cast<int>(tl & 1);
         if (!mbar_wait(a_ready + 8 * ab, static_cast<uint32_t>((tl >> 1) & 1))) { fail(); break; }
         fence_after();
         const uint32_t a_base = smem_u32(a_img + ab * G::A_BYTES);
-        for (int c = 0; c < chunks; ++c, ++g) {
-          const int s = static_cast<int>(g % kStages);
-          const int buf = static_cast<int>(g & 1);
-          if (*abort_flag || !mbar_wait(b_full + 8 * s, static_cast<uint32_t>((g / kStages) & 1)) ||
-              !mbar_wait(t_empty + 8 * buf, static_cast<uint32_t>(((g >> 1) & 1) ^ 1))) {
-            fail();
-            break;
+        for (int pass = 0; pass < 2 && !stop; ++pass) {
+          const int ksteps = pass == 0 ? HI_KSTEPS : G::KSTEPS;
+          for (int c = 0; c < chunks; ++c, ++g) {
+            const int s = static_cast<int>(g % kStages);
+            const int buf = static_cast<int>(g & 1);
+            if (*abort_flag || !mbar_wait(b_full + 8 * s, static_cast<uint32_t>((g / kStages) & 1)) ||
+                !mbar_wait(t_empty + 8 * buf, static_cast<uint32_t>(((g >> 1) & 1) ^ 1))) {
+              fail();
+              stop = true;
+              break;
+            }
+            fence_after();
+            const uint32_t b_base = smem_u32(b_img + s * G::B_BYTES);
+            const uint32_t d = tmem_base + static_cast<uint32_t>(buf * kN);
+            for (int ks = 0; ks < ksteps; ++ks) {
+              const uint64_t ad = sdesc(a_base + ks * 2 * G::A_LBO, G::A_LBO, 128);
+              const uint64_t bd = sdesc(b_base + ks * 2 * G::B_LBO, G::B_LBO, 128);
+              mma_f16(d, ad, bd, ks > 0 ? 1u : 0u);
+            }
+            mma_commit(b_empty + 8 * s);
+            mma_commit(t_full + 8 * buf);
+            issued = true;
           }
-          fence_after();
-          const uint32_t b_base = smem_u32(b_img + s * G::B_BYTES);
-          const uint32_t d = tmem_base + static_cast<uint32_t>(buf * kN);
-#pragma unroll
-          for (int ks = 0; ks < G::KSTEPS; ++ks) {
-            const uint64_t ad = sdesc(a_base + ks * 2 * G::A_LBO, G::A_LBO, 128);
-            const uint64_t bd = sdesc(b_base + ks * 2 * G::B_LBO, G::B_LBO, 128);
-            mma_f16(d, ad, bd, ks > 0 ? 1u : 0u);
-          }
-          mma_commit(b_empty + 8 * s);
-          mma_commit(t_full + 8 * buf);
-          issued = true;
         }
       }
       if (issued) {   // the last commit covers every MMA issued: wait before TMEM is freed
@@ -268,6 +302,7 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
     }
   } else {
     // ---------------- epilogue ----------------
+    const int et = threadIdx.x - 64;              // epilogue thread 0..EPI-1
     const int ew = warp - 2;
     const int wg = ew / 4;
     const int quarter = warp & 3;                 // TMEM lane quarter of this warp
@@ -318,50 +353,111 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
       if (lane == 0) mbar_arrive(a_ready + 8 * ab);
     };
 
+    // wait for accumulator chunk g and return its TMEM address for this thread
+    auto acquire = [&](int64_t gg, uint32_t& taddr) -> bool {
+      const int buf = static_cast<int>(gg & 1);
+      if (*abort_flag || !mbar_wait(t_full + 8 * buf, static_cast<uint32_t>((gg >> 1) & 1))) return false;
+      fence_after();
+      taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+              static_cast<uint32_t>(buf * kN + wg * kColsPerWG);
+      return true;
+    };
+    auto release = [&](int64_t gg) {
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(t_empty + 8 * (gg & 1));
+    };
+
     int64_t g = 0, tl = 0;
+    int msync = 0;                                 // epilogue barrier uses (parity source)
     if (static_cast<int64_t>(blockIdx.x) < total_tiles) build_a(blockIdx.x, 0);
     for (int64_t tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++tl) {
       if (*abort_flag) break;
       const int64_t next = tile + gridDim.x;
       if (next < total_tiles) build_a(next, static_cast<int>((tl + 1) & 1));
-      TopList<KMAX> top;
-      top.init();
       bool ok = true;
-      for (int c = 0; c < chunks; ++c, ++g) {
-        const int buf = static_cast<int>(g & 1);
-        if (*abort_flag || !mbar_wait(t_full + 8 * buf, static_cast<uint32_t>((g >> 1) & 1))) {
-          fail();
-          ok = false;
-          break;
-        }
-        fence_after();
-        const int col_base = c * kN + wg * kColsPerWG;
-        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
-                               static_cast<uint32_t>(buf * kN + wg * kColsPerWG);
+
+      // ---- pass 1: top-2 of 32 column groups on the a_hi . c_hi scores ----
+      float m1[32], m2[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) { m1[j] = -INFINITY; m2[j] = -INFINITY; }
+      for (int c = 0; c < chunks && ok; ++c, ++g) {
+        uint32_t taddr;
+        if (!acquire(g, taddr)) { ok = false; break; }
 #pragma unroll 1
         for (int part = 0; part < kColsPerWG / 32; ++part) {
           uint32_t v[32];
           tmem_ld32(taddr + part * 32, v);
-          if (part == kColsPerWG / 32 - 1) {    // accumulator drained: release it to the MMA warp
-            fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(t_empty + 8 * buf);
-          }
+          if (part == kColsPerWG / 32 - 1) release(g);
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            float s = __uint_as_float(v[j]);
-            if (!unit_t) s = s * inv_t;
-            top.push(s, static_cast<uint32_t>(col_base + part * 32 + j));
+            const float x = __uint_as_float(v[j]);
+            const float lo = fminf(m1[j], x);
+            m1[j] = fmaxf(m1[j], x);
+            m2[j] = fmaxf(m2[j], lo);
           }
         }
       }
-      if (!ok) break;
+      if (!ok) { fail(); break; }
+      // KMAX-th largest kept value: a lower bound (up to the dropped lo terms)
+      // on this thread's -- hence the row's -- KMAX-th largest score.
+      {
+        float kept[64];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) { kept[j] = m1[j]; kept[32 + j] = m2[j]; }
+        sort_desc<64>(kept);
+        bound[wg * kM + r] = kept[KMAX - 1];
+      }
+      if (!epi_sync(m_bar + 8 * (msync & 1), static_cast<uint32_t>((msync >> 1) & 1))) { fail(); break; }
+      ++msync;
+      float lb = bound[r];
+#pragma unroll
+      for (int w2 = 1; w2 < kEpiWG; ++w2) lb = fmaxf(lb, bound[w2 * kM + r]);
+      // |a.c - a_hi.c_hi| <= 2^-10 for unit vectors a, c (f16 rounding of each
+      // operand, Cauchy-Schwarz); 2^-9 leaves a margin for fp32 accumulation.
+      lb -= 1.0f / 512.0f;
+
+      // ---- pass 2: full-precision scores; keep only those >= lb ----
+      TopList<KMAX> top;
+      top.init();
+      int ncand = 0;
+      auto flush = [&]() {
+        for (int t = 0; t < ncand; ++t) {
+          const uint64_t kv = cand[t * EPI + et];
+          if (kv > top.key[KMAX - 1]) top.insert_key(kv);
+        }
+        ncand = 0;
+      };
+      for (int c = 0; c < chunks && ok; ++c, ++g) {
+        uint32_t taddr;
+        if (!acquire(g, taddr)) { ok = false; break; }
+        const int col_base = c * kN + wg * kColsPerWG;
+#pragma unroll 1
+        for (int part = 0; part < kColsPerWG / 32; ++part) {
+          uint32_t v[32];
+          tmem_ld32(taddr + part * 32, v);
+          if (part == kColsPerWG / 32 - 1) release(g);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float x = __uint_as_float(v[j]);
+            if (x >= lb) {
+              if (ncand == kCand) flush();
+              const float sc = unit_t ? x : x * inv_t;
+              cand[ncand * EPI + et] = rank_key(sc, static_cast<uint32_t>(col_base + part * 32 + j));
+              ++ncand;
+            }
+          }
+        }
+      }
+      if (!ok) { fail(); break; }
+      flush();
       // merge the warpgroups' lists (ranking keys are unique: plain key inserts)
       if (wg > 0) {
 #pragma unroll
         for (int t = 0; t < KMAX; ++t) merge_k[((wg - 1) * kM + r) * KMAX + t] = top.key[t];
       }
-      if (!epi_sync(m_bar, static_cast<uint32_t>(tl & 1))) { fail(); break; }
+      if (!epi_sync(m_bar + 8 * (msync & 1), static_cast<uint32_t>((msync >> 1) & 1))) { fail(); break; }
+      ++msync;
       if (wg == 0) {
         for (int w2 = 1; w2 < kEpiWG; ++w2)
 #pragma unroll
@@ -380,7 +476,10 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
             if (t < p.kk) out[t] = top.index(t);
         }
       }
-      if (!epi_sync(m_bar + 8, static_cast<uint32_t>(tl & 1))) { fail(); break; }
+      // the bound and merge buffers are rewritten next tile only after every
+      // epilogue warp is past this point
+      if (!epi_sync(m_bar + 8 * (msync & 1), static_cast<uint32_t>((msync >> 1) & 1))) { fail(); break; }
+      ++msync;
     }
   }
 
@@ -425,8 +524,8 @@ __global__ void codebook_image_kernel(const float* cbn, unsigned char* img, int6
 template <int DS>
 size_t smem_bytes(int kmax) {
   using G = Geo<DS>;
-  return 1024 + 2 * G::A_BYTES + kStages * G::B_BYTES + 2 * (kEpiWG - 1) * kM * kmax * 4 +
-         (2 * kStages + 8) * 8 + 16;
+  return 1024 + 2 * G::A_BYTES + kStages * G::B_BYTES + static_cast<size_t>(kCand) * 32 * kEpiWarps * 8 +
+         static_cast<size_t>(kEpiWG - 1) * kM * kmax * 8 + kEpiWG * kM * 4 + (2 * kStages + 8) * 8 + 16;
 }
 
 }  // namespace tc

@@ -68,6 +68,8 @@ struct RescoreParams {
   int32_t* cand_counts;        // optional [B, n_q, h_kv]
   int batch, n, n_q, q_offset, h_kv, group, d, a, b, n_codes, top_k, causal;
   int cap;                     // shared-memory candidate capacity (power of two)
+  int32_t* ovf_count;          // workspace: units left to the general path ...
+  int32_t* ovf_list;           // ... and their indices [B * n_q * h_kv]
 };
 
 // K4: sparse exact attention.
@@ -98,5 +100,7 @@ cudaError_t launch_build_index(const IndexParams& p, cudaStream_t st);
 cudaError_t launch_rescore(const RescoreParams& p, ssa_dtype dt, cudaStream_t st);
 size_t rescore_smem_bytes(int cap, int top_k);
 cudaError_t launch_sparse_attn(const AttnParams& p, ssa_dtype dt, cudaStream_t st);
+bool sparse_attn_mma_supported(const AttnParams& p, ssa_dtype dt);
+cudaError_t launch_sparse_attn_mma(const AttnParams& p, ssa_dtype dt, cudaStream_t st);
 
 }  // namespace ssa

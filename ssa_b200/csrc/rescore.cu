@@ -27,6 +27,8 @@
 // bitonic sort orders them.  If a query has more than `cap` distinct
 // candidates, a radix select over re-enumerated candidates finds the k-th key
 // first and only the top k are collected.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -119,22 +121,25 @@ __device__ __forceinline__ void bitonic_sort_desc(uint64_t* keys, int size) {
   }
 }
 
+// Unit index -> (bat, h, i): head-major (the K rows of the heads in flight stay
+// in L2); within a head the largest query positions first, since causal work
+// grows with i.
+__device__ __forceinline__ void unit_coords(const RescoreParams& p, int64_t unit, int& bh, int& i) {
+  bh = static_cast<int>(unit / p.n_q);
+  i = p.n_q - 1 - static_cast<int>(unit % p.n_q);
+}
+
+// One unit on a whole CTA (any candidate count, any k): the general path.
 template <typename T>
-__global__ void __launch_bounds__(kRsThreads) rescore_topk_kernel(RescoreParams p) {
-  __shared__ RsStatic s;
-  extern __shared__ __align__(16) unsigned char dyn[];
+__device__ void rescore_unit_block(const RescoreParams& p, int64_t unit, RsStatic& s, unsigned char* dyn) {
   uint64_t* keys = reinterpret_cast<uint64_t*>(dyn);
   float* qbar = reinterpret_cast<float*>(dyn + static_cast<size_t>(p.cap) * 8);
   uint32_t* bitmap = reinterpret_cast<uint32_t*>(qbar + 256);
   uint32_t* zpre = bitmap + cdiv(p.top_k, 32);
 
-  const int bhs = p.batch * p.h_kv;
-  const int64_t unit = blockIdx.x;
-  // largest query positions first: causal work grows with i
-  const int i = p.n_q - 1 - static_cast<int>(unit / bhs);
-  const int r = static_cast<int>(unit % bhs);
-  const int bat = r / p.h_kv, h = r % p.h_kv;
-  const int bh = bat * p.h_kv + h;
+  int bh, i;
+  unit_coords(p, unit, bh, i);
+  const int bat = bh / p.h_kv, h = bh % p.h_kv;
   const int pos = p.q_offset + i;
   const int a = p.a;
   const int k_eff = min(p.top_k, p.n);
@@ -301,23 +306,286 @@ __global__ void __launch_bounds__(kRsThreads) rescore_topk_kernel(RescoreParams 
   for (int e = k_eff + threadIdx.x; e < p.top_k; e += kRsThreads) put(e, 0);
   if (p.cand_counts && threadIdx.x == 0)
     p.cand_counts[(static_cast<int64_t>(bat) * p.n_q + i) * p.h_kv + h] = static_cast<int32_t>(cu);
+  __syncthreads();   // shared state is reused by the CTA's next unit
+}
+
+// General path: every unit (list == nullptr) or the units listed by the warp
+// kernel (count read on the device).
+template <typename T>
+__global__ void __launch_bounds__(kRsThreads) rescore_block_kernel(RescoreParams p, const int32_t* list,
+                                                                  const int32_t* list_count) {
+  __shared__ RsStatic s;
+  extern __shared__ __align__(16) unsigned char dyn[];
+  const int64_t n = list ? static_cast<int64_t>(*list_count)
+                         : static_cast<int64_t>(p.batch) * p.n_q * p.h_kv;
+  for (int64_t it = blockIdx.x; it < n; it += gridDim.x)
+    rescore_unit_block<T>(p, list ? static_cast<int64_t>(list[it]) : it, s, dyn);
+}
+
+// ---------------------------------------------------------------------------
+// Fast path: one warp per unit, no CTA barriers.  Candidates' ranking keys are
+// appended with warp-aggregated slots (ballot + popc) to a per-warp buffer of
+// kWarpCap keys and sorted in registers by a warp bitonic network (E keys per
+// lane, blocked layout: intra-lane stages are register compare-exchanges,
+// inter-lane stages use shuffles).  Units with more than kWarpCap distinct
+// candidates, or k > kWarpCap, are appended to an overflow list for the
+// general path.
+// ---------------------------------------------------------------------------
+constexpr int kWarpUnits = 4;
+constexpr int kWarpCap = 512;
+
+struct RsWarpSmem {
+  int32_t qc[kMaxCodesPerQuery];
+  int32_t lo[kMaxCodesPerQuery];
+  int32_t pre[kMaxCodesPerQuery + 1];
+  uint32_t bitmap[kWarpCap / 32];
+  float qbar[256];
+  uint64_t keys[kWarpCap];
+};
+
+// Descending bitonic sort of 32*E keys, key[e] of lane l at position l*E + e.
+template <int E>
+__device__ __forceinline__ void warp_sort_desc(uint64_t (&key)[E], int lane) {
+  constexpr int N = 32 * E;
+#pragma unroll
+  for (int k2 = 2; k2 <= N; k2 <<= 1) {
+#pragma unroll
+    for (int j = k2 >> 1; j > 0; j >>= 1) {
+      if (j < E) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const int f = e ^ j;
+          if (f > e) {
+            const int idx = lane * E + e;
+            const bool desc = (idx & k2) == 0;
+            const uint64_t x = key[e], y = key[f];
+            const bool swap = desc ? (x < y) : (x > y);
+            key[e] = swap ? y : x;
+            key[f] = swap ? x : y;
+          }
+        }
+      } else {
+        const int lx = j / E;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const int idx = lane * E + e;
+          const uint64_t other = __shfl_xor_sync(0xffffffffu, key[e], lx);
+          const bool desc = (idx & k2) == 0;
+          const bool lower = (lane & lx) == 0;     // the smaller position of the pair
+          const bool keep_max = desc == lower;
+          key[e] = keep_max ? (key[e] > other ? key[e] : other) : (key[e] < other ? key[e] : other);
+        }
+      }
+    }
+  }
+}
+
+template <int E>
+__device__ __forceinline__ void warp_sort_emit(const RsWarpSmem& s, int count, int nsel, int lane,
+                                               const RescoreParams& p, int64_t obase, uint64_t (&sorted_out)[16]) {
+  uint64_t key[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int idx = lane * E + e;
+    key[e] = idx < count ? s.keys[idx] : 0ull;
+  }
+  warp_sort_desc<E>(key, lane);
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int idx = lane * E + e;
+    if (idx < nsel) {
+      const int32_t j = static_cast<int32_t>(rank_key_index(key[e]));
+      if (p.index_i64) static_cast<int64_t*>(p.out)[obase + idx] = j;
+      else static_cast<int32_t*>(p.out)[obase + idx] = j;
+    }
+    sorted_out[e] = key[e];
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kWarpUnits * kWarp) rescore_warp_kernel(RescoreParams p) {
+  __shared__ RsWarpSmem smem[kWarpUnits];
+  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+  RsWarpSmem& s = smem[warp];
+  const int64_t units = static_cast<int64_t>(p.batch) * p.n_q * p.h_kv;
+  const int64_t unit = static_cast<int64_t>(blockIdx.x) * kWarpUnits + warp;
+  if (unit >= units) return;
+  int bh, i;
+  unit_coords(p, unit, bh, i);
+  const int bat = bh / p.h_kv, h = bh % p.h_kv;
+  const int pos = p.q_offset + i;
+  const int a = p.a;
+  const int k_eff = min(p.top_k, p.n);
+  const int32_t* bk = p.bucket_keys + static_cast<int64_t>(bh) * p.n * p.b;
+
+  int len = 0;
+  if (lane < a) {
+    const int c = p.q_codes[((static_cast<int64_t>(bat) * p.n_q + i) * p.h_kv + h) * a + lane];
+    const int32_t* ptr = p.bucket_ptr + static_cast<int64_t>(bh) * (p.n_codes + 1);
+    const int lo = ptr[c];
+    int hi = ptr[c + 1];
+    if (p.causal) {
+      int l = lo, u = hi;
+      while (l < u) {
+        const int mid = (l + u) >> 1;
+        if (bk[mid] <= pos) l = mid + 1; else u = mid;
+      }
+      hi = l;
+    }
+    s.qc[lane] = c;
+    s.lo[lane] = lo;
+    len = hi - lo;
+  }
+  int x = len;
+#pragma unroll
+  for (int o = 1; o < kWarp; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane < a) s.pre[lane + 1] = x;
+  if (lane == 0) s.pre[0] = 0;
+  const int total = __shfl_sync(0xffffffffu, x, a - 1);
+  {
+    const T* qrow = static_cast<const T*>(p.q) + bat * p.q_sb + static_cast<int64_t>(i) * p.q_sn +
+                    static_cast<int64_t>(h) * p.group * p.q_sh;
+    const float inv_g = 1.0f / static_cast<float>(p.group);
+    for (int e = lane; e < p.d; e += kWarp) {
+      float acc = 0.f;
+      for (int gg = 0; gg < p.group; ++gg) acc += Elem<T>::to_f(qrow[gg * p.q_sh + e]);
+      s.qbar[e] = p.group == 1 ? acc : acc * inv_g;
+    }
+  }
+  __syncwarp();
+
+  const int32_t* kcodes = p.k_codes + static_cast<int64_t>(bat) * p.n * p.h_kv * p.b;
+  const T* kbase = static_cast<const T*>(p.k) + bat * p.k_sb + static_cast<int64_t>(h) * p.k_sh;
+  int count = 0;
+  int t = 0;
+  for (int m0 = 0; m0 < total; m0 += kWarp) {
+    const int m = m0 + lane;
+    bool have = m < total;
+    uint64_t key = 0;
+    if (have) {
+      while (s.pre[t + 1] <= m) ++t;
+      const int32_t j = bk[s.lo[t] + (m - s.pre[t])];
+      bool dup = false;
+      if (t > 0) {
+        const int32_t* jc = kcodes + (static_cast<int64_t>(j) * p.h_kv + h) * p.b;
+        for (int y = 0; y < p.b && !dup; ++y) {
+          const int32_t c = jc[y];
+          for (int u = 0; u < t; ++u) dup |= (s.qc[u] == c);
+        }
+      }
+      if (dup) {
+        have = false;
+      } else {
+        const T* row = kbase + static_cast<int64_t>(j) * p.k_sn;
+        float acc0 = 0.f, acc1 = 0.f;
+        for (int e = 0; e < p.d; e += 8) {
+          float f[8];
+          load8<T>(row + e, f);
+          const float4 q0 = *reinterpret_cast<const float4*>(s.qbar + e);
+          const float4 q1 = *reinterpret_cast<const float4*>(s.qbar + e + 4);
+          acc0 = fmaf(f[0], q0.x, acc0); acc1 = fmaf(f[1], q0.y, acc1);
+          acc0 = fmaf(f[2], q0.z, acc0); acc1 = fmaf(f[3], q0.w, acc1);
+          acc0 = fmaf(f[4], q1.x, acc0); acc1 = fmaf(f[5], q1.y, acc1);
+          acc0 = fmaf(f[6], q1.z, acc0); acc1 = fmaf(f[7], q1.w, acc1);
+        }
+        key = rank_key(acc0 + acc1, static_cast<uint32_t>(j));
+      }
+    }
+    const unsigned bal = __ballot_sync(0xffffffffu, have);
+    const int slot = count + __popc(bal & ((1u << lane) - 1u));
+    if (have && slot < kWarpCap) s.keys[slot] = key;
+    count += __popc(bal);
+  }
+  if (count > kWarpCap || k_eff > kWarpCap) {
+    if (lane == 0) p.ovf_list[atomicAdd(p.ovf_count, 1)] = static_cast<int32_t>(unit);
+    return;
+  }
+  __syncwarp();
+  const int nsel = min(count, k_eff);
+  const int64_t obase = ((static_cast<int64_t>(bat) * p.n_q + i) * p.h_kv + h) * p.top_k;
+  uint64_t sorted[16];
+  int per_lane;
+  if (count <= 32 * 8) {
+    warp_sort_emit<8>(s, count, nsel, lane, p, obase, sorted);
+    per_lane = 8;
+  } else {
+    warp_sort_emit<16>(s, count, nsel, lane, p, obase, sorted);
+    per_lane = 16;
+  }
+  auto put = [&](int slot, int32_t j) {
+    if (p.index_i64) static_cast<int64_t*>(p.out)[obase + slot] = j;
+    else static_cast<int32_t*>(p.out)[obase + slot] = j;
+  };
+  if (count < k_eff) {
+    // filler: the lowest-index keys that are not candidates (k_eff <= kWarpCap)
+    const int need = k_eff - count;
+    const int words = (k_eff + 31) / 32;
+    if (lane < words) s.bitmap[lane] = 0u;
+    __syncwarp();
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      if (e < per_lane && lane * per_lane + e < count) {
+        const uint32_t j = rank_key_index(sorted[e]);
+        if (j < static_cast<uint32_t>(k_eff)) atomicOr(&s.bitmap[j >> 5], 1u << (j & 31));
+      }
+    }
+    __syncwarp();
+    uint32_t free_bits = 0;
+    if (lane < words) {
+      free_bits = ~s.bitmap[lane];
+      if (lane == words - 1 && (k_eff & 31)) free_bits &= (1u << (k_eff & 31)) - 1u;
+    }
+    const int nfree = __popc(free_bits);
+    int incl = nfree;
+#pragma unroll
+    for (int o = 1; o < kWarp; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    int rank = incl - nfree;
+    while (free_bits && rank < need) {
+      const int bit = __ffs(free_bits) - 1;
+      free_bits &= free_bits - 1;
+      put(count + rank, lane * 32 + bit);
+      ++rank;
+    }
+  }
+  for (int e = k_eff + lane; e < p.top_k; e += kWarp) put(e, 0);
+  if (p.cand_counts && lane == 0)
+    p.cand_counts[(static_cast<int64_t>(bat) * p.n_q + i) * p.h_kv + h] = count;
+}
+
+template <typename T>
+static cudaError_t launch_rescore_t(const RescoreParams& p, cudaStream_t st) {
+  const int64_t units = static_cast<int64_t>(p.batch) * p.n_q * p.h_kv;
+  const size_t smem = rescore_smem_bytes(p.cap, p.top_k);
+  cudaError_t e = cudaFuncSetAttribute(rescore_block_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  if (std::min(p.top_k, p.n) > kWarpCap || p.ovf_list == nullptr) {
+    rescore_block_kernel<T><<<static_cast<unsigned>(units), kRsThreads, smem, st>>>(p, nullptr, nullptr);
+    return cudaGetLastError();
+  }
+  e = cudaMemsetAsync(p.ovf_count, 0, sizeof(int32_t), st);
+  if (e != cudaSuccess) return e;
+  rescore_warp_kernel<T><<<static_cast<unsigned>(cdiv(units, kWarpUnits)), kWarpUnits * kWarp, 0, st>>>(p);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t grid = std::min<int64_t>(units, static_cast<int64_t>(sms) * 4);
+  rescore_block_kernel<T><<<static_cast<unsigned>(grid), kRsThreads, smem, st>>>(p, p.ovf_list, p.ovf_count);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_rescore(const RescoreParams& p, ssa_dtype dt, cudaStream_t st) {
   const int64_t units = static_cast<int64_t>(p.batch) * p.n_q * p.h_kv;
   if (units == 0) return cudaSuccess;
-  const size_t smem = rescore_smem_bytes(p.cap, p.top_k);
-#define SSA_RS(T)                                                                         \
-  do {                                                                                    \
-    cudaFuncSetAttribute(rescore_topk_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                         static_cast<int>(smem));                                         \
-    rescore_topk_kernel<T><<<static_cast<unsigned>(units), kRsThreads, smem, st>>>(p);    \
-  } while (0)
-  if (dt == SSA_F32) SSA_RS(float);
-  else if (dt == SSA_BF16) SSA_RS(__nv_bfloat16);
-  else SSA_RS(__half);
-#undef SSA_RS
-  return cudaGetLastError();
+  if (dt == SSA_F32) return launch_rescore_t<float>(p, st);
+  if (dt == SSA_BF16) return launch_rescore_t<__nv_bfloat16>(p, st);
+  return launch_rescore_t<__half>(p, st);
 }
 
 }  // namespace ssa

@@ -70,6 +70,8 @@ CASES = [
     (1000, 4, 1, 128, 512, 16, 4, 64, True),    # sparse: most rows need filler
     (5000, 2, 1, 32, 4, 2, 2, 64, True),        # > 2048 candidates: radix-select path
     (700, 16, 2, 128, 64, 16, 4, 256, True),
+    (1500, 4, 1, 64, 32, 4, 2, 300, True),      # 257..512 candidates: 16-per-lane warp sort
+    (600, 8, 2, 64, 16, 4, 2, 600, True),       # k > 512: every unit on the CTA-wide path
 ]
 
 
