@@ -32,6 +32,8 @@
 // Every wait is bounded (about one second); on expiry the CTA records an
 // error bit, stops issuing work, waits (bounded) for its copies and MMAs in
 // flight, frees TMEM and exits.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -41,7 +43,7 @@ namespace tc {
 constexpr int kM = 128;
 constexpr int kN = 256;
 constexpr int kStages = 2;
-constexpr int kCand = 16;          // pass-2 candidates buffered per thread
+constexpr int kCand = 32;          // pass-2 candidates buffered per thread (one full batch)
 constexpr int kEpiWG = 2;
 constexpr int kEpiWarps = 4 * kEpiWG;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
@@ -147,27 +149,6 @@ __device__ __forceinline__ uint32_t img_off(int r, int kgroup, int lbo) {
   return static_cast<uint32_t>(kgroup * lbo + (r >> 3) * 128 + (r & 7) * 16);
 }
 
-// Static bitonic sort (descending) of N floats held in registers.
-template <int N>
-__device__ __forceinline__ void sort_desc(float (&x)[N]) {
-#pragma unroll
-  for (int k2 = 2; k2 <= N; k2 <<= 1) {
-#pragma unroll
-    for (int j = k2 >> 1; j > 0; j >>= 1) {
-#pragma unroll
-      for (int e = 0; e < N; ++e) {
-        const int f = e ^ j;
-        if (f > e) {
-          const float a = x[e], b = x[f];
-          const bool desc = (e & k2) == 0;
-          x[e] = desc ? fmaxf(a, b) : fminf(a, b);
-          x[f] = desc ? fminf(a, b) : fmaxf(a, b);
-        }
-      }
-    }
-  }
-}
-
 template <int DS, int KMAX>
 __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcParams p) {
   using G = Geo<DS>;
@@ -179,9 +160,13 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   unsigned char* a_img = base;                                        // 2 x A_BYTES
   unsigned char* b_img = a_img + 2 * G::A_BYTES;                      // kStages x B_BYTES
-  uint64_t* cand = reinterpret_cast<uint64_t*>(b_img + kStages * G::B_BYTES);   // [kCand][EPI]
-  uint64_t* merge_k = cand + kCand * EPI;                             // [kEpiWG-1][kM][KMAX]
-  float* bound = reinterpret_cast<float*>(merge_k + (kEpiWG - 1) * kM * KMAX);  // [kEpiWG][kM]
+  // [kCand][EPI] pass-2 candidate keys; the same bytes hold the pass-1 kept
+  // values ([64][EPI] floats) and, after the last flush, the merge lists
+  // ([kEpiWG-1][kM][KMAX] keys).
+  uint64_t* cand = reinterpret_cast<uint64_t*>(b_img + kStages * G::B_BYTES);
+  float* kept = reinterpret_cast<float*>(cand);
+  uint64_t* merge_k = cand;
+  float* bound = reinterpret_cast<float*>(cand + kCand * EPI);       // [kEpiWG][kM]
   uint64_t* bars = reinterpret_cast<uint64_t*>(bound + kEpiWG * kM);
   // barriers: b_full[kStages], b_empty[kStages], t_full[2], t_empty[2], a_ready[2], m_bar[2]
   const uint32_t b_full = smem_u32(bars);
@@ -401,12 +386,26 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
       if (!ok) { fail(); break; }
       // KMAX-th largest kept value: a lower bound (up to the dropped lo terms)
       // on this thread's -- hence the row's -- KMAX-th largest score.
-      {
-        float kept[64];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) { kept[j] = m1[j]; kept[32 + j] = m2[j]; }
-        sort_desc<64>(kept);
-        bound[wg * kM + r] = kept[KMAX - 1];
+      for (int j = 0; j < 32; ++j) {
+        kept[j * EPI + et] = m1[j];
+        kept[(32 + j) * EPI + et] = m2[j];
+      }
+      {
+        float best[KMAX];
+#pragma unroll
+        for (int t = 0; t < KMAX; ++t) best[t] = -INFINITY;
+#pragma unroll 1
+        for (int u = 0; u < 64; ++u) {
+          float c = kept[u * EPI + et];
+#pragma unroll
+          for (int t = 0; t < KMAX; ++t) {
+            const float hi = fmaxf(best[t], c);
+            c = fminf(best[t], c);
+            best[t] = hi;
+          }
+        }
+        bound[wg * kM + r] = best[KMAX - 1];
       }
       if (!epi_sync(m_bar + 8 * (msync & 1), static_cast<uint32_t>((msync >> 1) & 1))) { fail(); break; }
       ++msync;
@@ -422,6 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
       top.init();
       int ncand = 0;
       auto flush = [&]() {
+#pragma unroll 1
         for (int t = 0; t < ncand; ++t) {
           const uint64_t kv = cand[t * EPI + et];
           if (kv > top.key[KMAX - 1]) top.insert_key(kv);
@@ -437,20 +437,28 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
           uint32_t v[32];
           tmem_ld32(taddr + part * 32, v);
           if (part == kColsPerWG / 32 - 1) release(g);
+          uint32_t hit = 0;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float x = __uint_as_float(v[j]);
-            if (x >= lb) {
-              if (ncand == kCand) flush();
-              const float sc = unit_t ? x : x * inv_t;
-              cand[ncand * EPI + et] = rank_key(sc, static_cast<uint32_t>(col_base + part * 32 + j));
-              ++ncand;
+          for (int j = 0; j < 32; ++j) hit |= (__uint_as_float(v[j]) >= lb ? 1u : 0u) << j;
+          if (hit) {
+            if (ncand + __popc(hit) > kCand) flush();      // the only flush site: keeps code small
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (hit & (1u << j)) {
+                const float x = __uint_as_float(v[j]);
+                cand[ncand * EPI + et] =
+                    rank_key(unit_t ? x : x * inv_t, static_cast<uint32_t>(col_base + part * 32 + j));
+                ++ncand;
+              }
             }
           }
         }
       }
       if (!ok) { fail(); break; }
       flush();
+      // every thread's candidates are consumed before the buffer holds merge lists
+      if (!epi_sync(m_bar + 8 * (msync & 1), static_cast<uint32_t>((msync >> 1) & 1))) { fail(); break; }
+      ++msync;
       // merge the warpgroups' lists (ranking keys are unique: plain key inserts)
       if (wg > 0) {
 #pragma unroll
@@ -459,12 +467,11 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
       if (!epi_sync(m_bar + 8 * (msync & 1), static_cast<uint32_t>((msync >> 1) & 1))) { fail(); break; }
       ++msync;
       if (wg == 0) {
-        for (int w2 = 1; w2 < kEpiWG; ++w2)
-#pragma unroll
-          for (int t = 0; t < KMAX; ++t) {
-            const uint64_t kv = merge_k[((w2 - 1) * kM + r) * KMAX + t];
-            if (kv > top.key[KMAX - 1]) top.insert_key(kv);
-          }
+#pragma unroll 1
+        for (int u = 0; u < (kEpiWG - 1) * KMAX; ++u) {
+          const uint64_t kv = merge_k[((u / KMAX) * kM + r) * KMAX + (u % KMAX)];
+          if (kv > top.key[KMAX - 1]) top.insert_key(kv);
+        }
         const int64_t bh = tile / p.tiles_per_head;
         const int64_t i = (tile % p.tiles_per_head) * kM + r;
         if (i < p.n_rows) {
@@ -524,8 +531,10 @@ __global__ void codebook_image_kernel(const float* cbn, unsigned char* img, int6
 template <int DS>
 size_t smem_bytes(int kmax) {
   using G = Geo<DS>;
-  return 1024 + 2 * G::A_BYTES + kStages * G::B_BYTES + static_cast<size_t>(kCand) * 32 * kEpiWarps * 8 +
-         static_cast<size_t>(kEpiWG - 1) * kM * kmax * 8 + kEpiWG * kM * 4 + (2 * kStages + 8) * 8 + 16;
+  const size_t shared = std::max<size_t>({static_cast<size_t>(kCand) * 32 * kEpiWarps * 8,
+                                          static_cast<size_t>(64) * 32 * kEpiWarps * 4,
+                                          static_cast<size_t>(kEpiWG - 1) * kM * kmax * 8});
+  return 1024 + 2 * G::A_BYTES + kStages * G::B_BYTES + shared + kEpiWG * kM * 4 + (2 * kStages + 8) * 8 + 16;
 }
 
 }  // namespace tc

@@ -335,15 +335,18 @@ constexpr int kWarpUnits = 4;
 constexpr int kWarpCap = 512;
 
 struct RsWarpSmem {
+  __align__(16) float qbar[256];     // read as float4: must stay 16-byte aligned
+  uint64_t keys[kWarpCap];
   int32_t qc[kMaxCodesPerQuery];
   int32_t lo[kMaxCodesPerQuery];
   int32_t pre[kMaxCodesPerQuery + 1];
   uint32_t bitmap[kWarpCap / 32];
-  float qbar[256];
-  uint64_t keys[kWarpCap];
 };
 
-// Descending bitonic sort of 32*E keys, key[e] of lane l at position l*E + e.
+// Descending bitonic sort of 32*E keys in a warp; key[e] of lane l sits at
+// position e*32 + l (cyclic layout: loads from and stores to consecutive
+// positions are conflict-free / coalesced).  Partners closer than 32
+// positions are exchanged with shuffles, farther ones inside the lane.
 template <int E>
 __device__ __forceinline__ void warp_sort_desc(uint64_t (&key)[E], int lane) {
   constexpr int N = 32 * E;
@@ -351,13 +354,12 @@ __device__ __forceinline__ void warp_sort_desc(uint64_t (&key)[E], int lane) {
   for (int k2 = 2; k2 <= N; k2 <<= 1) {
 #pragma unroll
     for (int j = k2 >> 1; j > 0; j >>= 1) {
-      if (j < E) {
+      if (j >= 32) {
 #pragma unroll
         for (int e = 0; e < E; ++e) {
-          const int f = e ^ j;
+          const int f = e ^ (j >> 5);
           if (f > e) {
-            const int idx = lane * E + e;
-            const bool desc = (idx & k2) == 0;
+            const bool desc = ((e * 32 + lane) & k2) == 0;
             const uint64_t x = key[e], y = key[f];
             const bool swap = desc ? (x < y) : (x > y);
             key[e] = swap ? y : x;
@@ -365,15 +367,15 @@ __device__ __forceinline__ void warp_sort_desc(uint64_t (&key)[E], int lane) {
           }
         }
       } else {
-        const int lx = j / E;
 #pragma unroll
         for (int e = 0; e < E; ++e) {
-          const int idx = lane * E + e;
-          const uint64_t other = __shfl_xor_sync(0xffffffffu, key[e], lx);
-          const bool desc = (idx & k2) == 0;
-          const bool lower = (lane & lx) == 0;     // the smaller position of the pair
+          const uint64_t other = __shfl_xor_sync(0xffffffffu, key[e], j);
+          const bool desc = ((e * 32 + lane) & k2) == 0;
+          const bool lower = (lane & j) == 0;
           const bool keep_max = desc == lower;
-          key[e] = keep_max ? (key[e] > other ? key[e] : other) : (key[e] < other ? key[e] : other);
+          const uint64_t mx = key[e] > other ? key[e] : other;
+          const uint64_t mn = key[e] > other ? other : key[e];
+          key[e] = keep_max ? mx : mn;
         }
       }
     }
@@ -382,23 +384,22 @@ __device__ __forceinline__ void warp_sort_desc(uint64_t (&key)[E], int lane) {
 
 template <int E>
 __device__ __forceinline__ void warp_sort_emit(const RsWarpSmem& s, int count, int nsel, int lane,
-                                               const RescoreParams& p, int64_t obase, uint64_t (&sorted_out)[16]) {
+                                               const RescoreParams& p, int64_t obase) {
   uint64_t key[E];
 #pragma unroll
   for (int e = 0; e < E; ++e) {
-    const int idx = lane * E + e;
+    const int idx = e * 32 + lane;
     key[e] = idx < count ? s.keys[idx] : 0ull;
   }
   warp_sort_desc<E>(key, lane);
 #pragma unroll
   for (int e = 0; e < E; ++e) {
-    const int idx = lane * E + e;
+    const int idx = e * 32 + lane;
     if (idx < nsel) {
       const int32_t j = static_cast<int32_t>(rank_key_index(key[e]));
       if (p.index_i64) static_cast<int64_t*>(p.out)[obase + idx] = j;
       else static_cast<int32_t*>(p.out)[obase + idx] = j;
     }
-    sorted_out[e] = key[e];
   }
 }
 
@@ -459,45 +460,62 @@ __global__ void __launch_bounds__(kWarpUnits * kWarp) rescore_warp_kernel(Rescor
 
   const int32_t* kcodes = p.k_codes + static_cast<int64_t>(bat) * p.n * p.h_kv * p.b;
   const T* kbase = static_cast<const T*>(p.k) + bat * p.k_sb + static_cast<int64_t>(h) * p.k_sh;
-  int count = 0;
-  int t = 0;
-  for (int m0 = 0; m0 < total; m0 += kWarp) {
-    const int m = m0 + lane;
-    bool have = m < total;
-    uint64_t key = 0;
-    if (have) {
-      while (s.pre[t + 1] <= m) ++t;
-      const int32_t j = bk[s.lo[t] + (m - s.pre[t])];
-      bool dup = false;
-      if (t > 0) {
-        const int32_t* jc = kcodes + (static_cast<int64_t>(j) * p.h_kv + h) * p.b;
-        for (int y = 0; y < p.b && !dup; ++y) {
-          const int32_t c = jc[y];
-          for (int u = 0; u < t; ++u) dup |= (s.qc[u] == c);
-        }
-      }
-      if (dup) {
-        have = false;
-      } else {
-        const T* row = kbase + static_cast<int64_t>(j) * p.k_sn;
-        float acc0 = 0.f, acc1 = 0.f;
-        for (int e = 0; e < p.d; e += 8) {
-          float f[8];
-          load8<T>(row + e, f);
-          const float4 q0 = *reinterpret_cast<const float4*>(s.qbar + e);
-          const float4 q1 = *reinterpret_cast<const float4*>(s.qbar + e + 4);
-          acc0 = fmaf(f[0], q0.x, acc0); acc1 = fmaf(f[1], q0.y, acc1);
-          acc0 = fmaf(f[2], q0.z, acc0); acc1 = fmaf(f[3], q0.w, acc1);
-          acc0 = fmaf(f[4], q1.x, acc0); acc1 = fmaf(f[5], q1.y, acc1);
-          acc0 = fmaf(f[6], q1.z, acc0); acc1 = fmaf(f[7], q1.w, acc1);
-        }
-        key = rank_key(acc0 + acc1, static_cast<uint32_t>(j));
+  // Two candidates per lane per iteration.  For each, the K row and the key's
+  // codes are loaded as soon as the key index is known, so the dedupe test
+  // and the dot product share one round trip to L2.
+  auto locate = [&](int m, int& t) -> int32_t {
+    while (s.pre[t + 1] <= m) ++t;
+    return bk[s.lo[t] + (m - s.pre[t])];
+  };
+  auto is_dup = [&](int32_t j, int t) -> bool {
+    bool dup = false;
+    if (t > 0) {
+      const int32_t* jc = kcodes + (static_cast<int64_t>(j) * p.h_kv + h) * p.b;
+      for (int y = 0; y < p.b; ++y) {
+        const int32_t c = jc[y];
+        for (int u = 0; u < t; ++u) dup |= (s.qc[u] == c);
       }
     }
-    const unsigned bal = __ballot_sync(0xffffffffu, have);
-    const int slot = count + __popc(bal & ((1u << lane) - 1u));
-    if (have && slot < kWarpCap) s.keys[slot] = key;
-    count += __popc(bal);
+    return dup;
+  };
+  int count = 0;
+  int t = 0;
+  for (int m0 = 0; m0 < total; m0 += 2 * kWarp) {
+    const int ma = m0 + lane, mb = ma + kWarp;
+    const bool ha = ma < total, hb = mb < total;
+    int ta = t;
+    const int32_t ja = ha ? locate(ma, ta) : 0;
+    int tb = ta;
+    const int32_t jb = hb ? locate(mb, tb) : ja;
+    t = hb ? tb : ta;
+    const T* ra = kbase + static_cast<int64_t>(ja) * p.k_sn;
+    const T* rb = kbase + static_cast<int64_t>(jb) * p.k_sn;
+    float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+    for (int e = 0; e < p.d; e += 8) {
+      float fa[8], fb[8];
+      load8<T>(ra + e, fa);
+      load8<T>(rb + e, fb);
+      const float4 q0 = *reinterpret_cast<const float4*>(s.qbar + e);
+      const float4 q1 = *reinterpret_cast<const float4*>(s.qbar + e + 4);
+      a0 = fmaf(fa[0], q0.x, a0); a1 = fmaf(fa[1], q0.y, a1);
+      a0 = fmaf(fa[2], q0.z, a0); a1 = fmaf(fa[3], q0.w, a1);
+      a0 = fmaf(fa[4], q1.x, a0); a1 = fmaf(fa[5], q1.y, a1);
+      a0 = fmaf(fa[6], q1.z, a0); a1 = fmaf(fa[7], q1.w, a1);
+      b0 = fmaf(fb[0], q0.x, b0); b1 = fmaf(fb[1], q0.y, b1);
+      b0 = fmaf(fb[2], q0.z, b0); b1 = fmaf(fb[3], q0.w, b1);
+      b0 = fmaf(fb[4], q1.x, b0); b1 = fmaf(fb[5], q1.y, b1);
+      b0 = fmaf(fb[6], q1.z, b0); b1 = fmaf(fb[7], q1.w, b1);
+    }
+    const bool keep_a = ha && !is_dup(ja, ta);
+    const bool keep_b = hb && !is_dup(jb, tb);
+    const unsigned bal_a = __ballot_sync(0xffffffffu, keep_a);
+    const unsigned bal_b = __ballot_sync(0xffffffffu, keep_b);
+    const unsigned below = (1u << lane) - 1u;
+    const int slot_a = count + __popc(bal_a & below);
+    const int slot_b = count + __popc(bal_a) + __popc(bal_b & below);
+    if (keep_a && slot_a < kWarpCap) s.keys[slot_a] = rank_key(a0 + a1, static_cast<uint32_t>(ja));
+    if (keep_b && slot_b < kWarpCap) s.keys[slot_b] = rank_key(b0 + b1, static_cast<uint32_t>(jb));
+    count += __popc(bal_a) + __popc(bal_b);
   }
   if (count > kWarpCap || k_eff > kWarpCap) {
     if (lane == 0) p.ovf_list[atomicAdd(p.ovf_count, 1)] = static_cast<int32_t>(unit);
@@ -506,15 +524,8 @@ __global__ void __launch_bounds__(kWarpUnits * kWarp) rescore_warp_kernel(Rescor
   __syncwarp();
   const int nsel = min(count, k_eff);
   const int64_t obase = ((static_cast<int64_t>(bat) * p.n_q + i) * p.h_kv + h) * p.top_k;
-  uint64_t sorted[16];
-  int per_lane;
-  if (count <= 32 * 8) {
-    warp_sort_emit<8>(s, count, nsel, lane, p, obase, sorted);
-    per_lane = 8;
-  } else {
-    warp_sort_emit<16>(s, count, nsel, lane, p, obase, sorted);
-    per_lane = 16;
-  }
+  if (count <= 32 * 8) warp_sort_emit<8>(s, count, nsel, lane, p, obase);
+  else warp_sort_emit<16>(s, count, nsel, lane, p, obase);
   auto put = [&](int slot, int32_t j) {
     if (p.index_i64) static_cast<int64_t*>(p.out)[obase + slot] = j;
     else static_cast<int32_t*>(p.out)[obase + slot] = j;
@@ -525,12 +536,9 @@ __global__ void __launch_bounds__(kWarpUnits * kWarp) rescore_warp_kernel(Rescor
     const int words = (k_eff + 31) / 32;
     if (lane < words) s.bitmap[lane] = 0u;
     __syncwarp();
-#pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      if (e < per_lane && lane * per_lane + e < count) {
-        const uint32_t j = rank_key_index(sorted[e]);
-        if (j < static_cast<uint32_t>(k_eff)) atomicOr(&s.bitmap[j >> 5], 1u << (j & 31));
-      }
+    for (int e = lane; e < count; e += kWarp) {
+      const uint32_t j = rank_key_index(s.keys[e]);
+      if (j < static_cast<uint32_t>(k_eff)) atomicOr(&s.bitmap[j >> 5], 1u << (j & 31));
     }
     __syncwarp();
     uint32_t free_bits = 0;
