@@ -98,6 +98,8 @@ cudaError_t launch_select_from_scores(const float* scores, int64_t rows, int n_c
                                       int32_t* out, cudaStream_t st);
 cudaError_t launch_build_index(const IndexParams& p, cudaStream_t st);
 cudaError_t launch_rescore(const RescoreParams& p, ssa_dtype dt, cudaStream_t st);
+bool rescore_mma_supported(const RescoreParams& p, ssa_dtype dt);
+cudaError_t launch_rescore_mma(const RescoreParams& p, ssa_dtype dt, cudaStream_t st);
 size_t rescore_smem_bytes(int cap, int top_k);
 cudaError_t launch_sparse_attn(const AttnParams& p, ssa_dtype dt, cudaStream_t st);
 bool sparse_attn_mma_supported(const AttnParams& p, ssa_dtype dt);

@@ -28,6 +28,7 @@
 // candidates, a radix select over re-enumerated candidates finds the k-th key
 // first and only the top k are collected.
 #include <algorithm>
+#include <type_traits>
 
 #include "common.cuh"
 #include "kernels.cuh"
@@ -579,7 +580,13 @@ static cudaError_t launch_rescore_t(const RescoreParams& p, cudaStream_t st) {
   }
   e = cudaMemsetAsync(p.ovf_count, 0, sizeof(int32_t), st);
   if (e != cudaSuccess) return e;
-  rescore_warp_kernel<T><<<static_cast<unsigned>(cdiv(units, kWarpUnits)), kWarpUnits * kWarp, 0, st>>>(p);
+  const ssa_dtype dt = sizeof(T) == 4 ? SSA_F32 : (std::is_same<T, __half>::value ? SSA_F16 : SSA_BF16);
+  if (rescore_mma_supported(p, dt)) {
+    e = launch_rescore_mma(p, dt, st);
+    if (e != cudaSuccess) return e;
+  } else {
+    rescore_warp_kernel<T><<<static_cast<unsigned>(cdiv(units, kWarpUnits)), kWarpUnits * kWarp, 0, st>>>(p);
+  }
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);

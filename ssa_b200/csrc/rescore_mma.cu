@@ -1,0 +1,416 @@
+// K3 fast path for 16-bit inputs: one warp per (bat, i, h) unit, candidate
+// re-scoring on tensor cores.
+//
+// Same contract as the CTA-wide path in rescore.cu (ssa/router.py:151-259:
+// candidates = keys sharing a code with the query, j <= i when causal;
+// ranked by qbar . k_j with the lower key index first among equal scores;
+// canonical filler; zero padding).  Steps, all inside one warp:
+//   1. the query's a buckets are located (causal cut by binary search) and
+//      walked 128 keys at a time (all loads of a group issued together); the
+//      first-match rule drops keys reached through an earlier code; kept key
+//      indices are compacted with ballots;
+//   2. kept keys are scored 32 at a time on the tensor cores (mma.sync
+//      m16n8k16).  B fragments are loaded straight from global memory into
+//      registers with 16-byte loads: the reduction (head-dim) axis is
+//      permuted identically in A and B so that each lane reads 8 consecutive
+//      elements of a key row per pair of k-steps.  The A operand holds qbar
+//      split into a 16-bit hi part (row 0) and lo part (row 8); both rows of
+//      each output column land in the same thread, so hi + lo gives
+//      qbar . k_j with fp32 accuracy;
+//   3. if there are more candidates than k, a warp radix select (8 bits per
+//      pass over the 64-bit ranking keys, in shared memory) finds the k-th
+//      key and the top k are compacted;
+//   4. the selected keys are sorted in registers (bitonic, 32*E keys) and
+//      written in order; filler and zero padding follow.
+// Units with more than kMmaCap candidates, or k > kMmaCap, go to the overflow
+// list and the CTA-wide path.
+#include "common.cuh"
+#include "kernels.cuh"
+#include "mma_utils.cuh"
+
+namespace ssa {
+
+constexpr int kMmaUnits = 4;        // warps (units) per CTA
+constexpr int kMmaCap = 512;        // candidates per unit on this path
+constexpr int kBatch = 32;          // candidates per MMA batch (4 n-tiles)
+constexpr int kWalk = 4;            // bucket-walk iterations whose loads are issued together
+
+template <int D>
+struct __align__(128) RsMmaSmem {
+  uint64_t keys[kMmaCap];                      // ranking keys of all candidates
+  uint64_t sel[kMmaCap];                       // kept key indices, then the selected keys
+  uint32_t hist[256];
+  int32_t qc[32];
+  int32_t lo[32];
+  int32_t pre[33];
+  uint32_t bitmap[kMmaCap / 32];
+};
+
+// Descending bitonic sort of 32*E keys (key[e] of lane l at position e*32+l).
+template <int E>
+__device__ __forceinline__ void sort_desc_cyclic(uint64_t (&key)[E], int lane) {
+  constexpr int N = 32 * E;
+#pragma unroll
+  for (int k2 = 2; k2 <= N; k2 <<= 1) {
+#pragma unroll
+    for (int j = k2 >> 1; j > 0; j >>= 1) {
+      if (j >= 32) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const int f = e ^ (j >> 5);
+          if (f > e) {
+            const bool desc = ((e * 32 + lane) & k2) == 0;
+            const uint64_t x = key[e], y = key[f];
+            const bool swap = desc ? (x < y) : (x > y);
+            key[e] = swap ? y : x;
+            key[f] = swap ? x : y;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const uint64_t other = __shfl_xor_sync(0xffffffffu, key[e], j);
+          const bool keep_max = (((e * 32 + lane) & k2) == 0) == ((lane & j) == 0);
+          const bool gt = key[e] > other;
+          key[e] = (gt == keep_max) ? key[e] : other;
+        }
+      }
+    }
+  }
+}
+
+template <int E>
+__device__ __forceinline__ void sort_and_write(const uint64_t* src, int nsel, int lane, const RescoreParams& p,
+                                               int64_t obase) {
+  uint64_t key[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int idx = e * 32 + lane;
+    key[e] = idx < nsel ? src[idx] : 0ull;
+  }
+  sort_desc_cyclic<E>(key, lane);
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int idx = e * 32 + lane;
+    if (idx < nsel) {
+      const int32_t j = static_cast<int32_t>(rank_key_index(key[e]));
+      if (p.index_i64) static_cast<int64_t*>(p.out)[obase + idx] = j;
+      else static_cast<int32_t*>(p.out)[obase + idx] = j;
+    }
+  }
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kMmaUnits * kWarp) rescore_mma_kernel(RescoreParams p) {
+  constexpr int SEGS = D * 2 / 16;
+  constexpr int KSTEPS = D / 16;
+  extern __shared__ __align__(128) unsigned char dyn[];
+  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+  RsMmaSmem<D>& s = reinterpret_cast<RsMmaSmem<D>*>(dyn)[warp];
+  const int64_t units = static_cast<int64_t>(p.batch) * p.n_q * p.h_kv;
+  const int64_t unit = static_cast<int64_t>(blockIdx.x) * kMmaUnits + warp;
+  if (unit >= units) return;
+  // head-major, largest query positions first within a head (as the CTA path)
+  const int bh = static_cast<int>(unit / p.n_q);
+  const int i = p.n_q - 1 - static_cast<int>(unit % p.n_q);
+  const int bat = bh / p.h_kv, h = bh % p.h_kv;
+  const int pos = p.q_offset + i;
+  const int a = p.a;
+  const int k_eff = min(p.top_k, p.n);
+  const int32_t* bk = p.bucket_keys + static_cast<int64_t>(bh) * p.n * p.b;
+  const int gid = lane >> 2, tig = lane & 3;
+
+  // ---- 1a. the query's buckets (causal prefix of each) ----
+  int len = 0;
+  if (lane < a) {
+    const int c = p.q_codes[((static_cast<int64_t>(bat) * p.n_q + i) * p.h_kv + h) * a + lane];
+    const int32_t* ptr = p.bucket_ptr + static_cast<int64_t>(bh) * (p.n_codes + 1);
+    const int lo = ptr[c];
+    int hi = ptr[c + 1];
+    if (p.causal) {
+      int l = lo, u = hi;
+      while (l < u) {
+        const int mid = (l + u) >> 1;
+        if (bk[mid] <= pos) l = mid + 1; else u = mid;
+      }
+      hi = l;
+    }
+    s.qc[lane] = c;
+    s.lo[lane] = lo;
+    len = hi - lo;
+  }
+  int incl = len;
+#pragma unroll
+  for (int o = 1; o < kWarp; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane < a) s.pre[lane + 1] = incl;
+  if (lane == 0) s.pre[0] = 0;
+  const int total = __shfl_sync(0xffffffffu, incl, a - 1);
+
+  // ---- qbar as A fragments: row 0 = hi part, row 8 = lo part (lanes 0..3) ----
+  // k-step pair kp covers head dims [32kp, 32kp+32); lane tig's 8 dims
+  // 32kp+8tig+{0..7} feed (k 2tig..2tig+1, k 2tig+8..2tig+9) of step 2kp and
+  // of step 2kp+1, matching the B fragments loaded below.
+  uint32_t qa[KSTEPS][4];
+  {
+    const T* qrow = static_cast<const T*>(p.q) + bat * p.q_sb + static_cast<int64_t>(i) * p.q_sn +
+                    static_cast<int64_t>(h) * p.group * p.q_sh;
+    const float inv_g = 1.0f / static_cast<float>(p.group);
+#pragma unroll
+    for (int kp = 0; kp < KSTEPS / 2; ++kp) {
+      qa[2 * kp][0] = qa[2 * kp][1] = qa[2 * kp][2] = qa[2 * kp][3] = 0u;
+      qa[2 * kp + 1][0] = qa[2 * kp + 1][1] = qa[2 * kp + 1][2] = qa[2 * kp + 1][3] = 0u;
+      if (gid == 0) {
+        float x[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) x[u] = 0.f;
+        const int e0 = kp * 32 + 8 * tig;
+        for (int gg = 0; gg < p.group; ++gg) {
+          float f[8];
+          load8<T>(qrow + static_cast<int64_t>(gg) * p.q_sh + e0, f);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) x[u] += f[u];
+        }
+        if (p.group != 1) {
+#pragma unroll
+          for (int u = 0; u < 8; ++u) x[u] *= inv_g;
+        }
+        split2<T>(x[0], x[1], qa[2 * kp][0], qa[2 * kp][1]);
+        split2<T>(x[2], x[3], qa[2 * kp][2], qa[2 * kp][3]);
+        split2<T>(x[4], x[5], qa[2 * kp + 1][0], qa[2 * kp + 1][1]);
+        split2<T>(x[6], x[7], qa[2 * kp + 1][2], qa[2 * kp + 1][3]);
+      }
+    }
+  }
+  __syncwarp();
+
+  // ---- 1b. walk the buckets: first-match dedupe, compact kept key indices ----
+  const int32_t* kcodes = p.k_codes + static_cast<int64_t>(bat) * p.n * p.h_kv * p.b;
+  int32_t* jlist = reinterpret_cast<int32_t*>(s.sel);
+  int count = 0;
+  int t = 0;
+  for (int m0 = 0; m0 < total; m0 += kWalk * kWarp) {
+    int32_t j[kWalk];
+    int tt[kWalk];
+    bool keep[kWalk];
+#pragma unroll
+    for (int w = 0; w < kWalk; ++w) {          // key indices of the group (coalesced within a bucket)
+      const int m = m0 + w * kWarp + lane;
+      keep[w] = m < total;
+      j[w] = 0;
+      if (keep[w]) {
+        while (s.pre[t + 1] <= m) ++t;
+        j[w] = bk[s.lo[t] + (m - s.pre[t])];
+      }
+      tt[w] = t;
+    }
+    if (p.b == 4) {
+      int4 c4[kWalk];
+#pragma unroll
+      for (int w = 0; w < kWalk; ++w)          // the keys' codes, all loads in flight together
+        c4[w] = keep[w] && tt[w] > 0
+                    ? *reinterpret_cast<const int4*>(kcodes + (static_cast<int64_t>(j[w]) * p.h_kv + h) * 4)
+                    : make_int4(-1, -1, -1, -1);
+#pragma unroll
+      for (int w = 0; w < kWalk; ++w)
+        for (int u = 0; u < tt[w]; ++u) {
+          const int32_t q = s.qc[u];
+          keep[w] &= (q != c4[w].x) & (q != c4[w].y) & (q != c4[w].z) & (q != c4[w].w);
+        }
+    } else {
+#pragma unroll
+      for (int w = 0; w < kWalk; ++w) {
+        if (keep[w] && tt[w] > 0) {
+          const int32_t* jc = kcodes + (static_cast<int64_t>(j[w]) * p.h_kv + h) * p.b;
+          for (int y = 0; y < p.b; ++y) {
+            const int32_t c = jc[y];
+            for (int u = 0; u < tt[w]; ++u) keep[w] &= (s.qc[u] != c);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int w = 0; w < kWalk; ++w) {
+      const unsigned bal = __ballot_sync(0xffffffffu, keep[w]);
+      const int slot = count + __popc(bal & ((1u << lane) - 1u));
+      if (keep[w] && slot < kMmaCap) jlist[slot] = j[w];
+      count += __popc(bal);
+    }
+  }
+  if (count > kMmaCap || k_eff > kMmaCap) {
+    if (lane == 0) p.ovf_list[atomicAdd(p.ovf_count, 1)] = static_cast<int32_t>(unit);
+    return;
+  }
+  __syncwarp();
+
+  // ---- 2. score the kept keys, 32 per batch, on tensor cores ----
+  const T* kbase = static_cast<const T*>(p.k) + bat * p.k_sb + static_cast<int64_t>(h) * p.k_sh;
+  for (int b0 = 0; b0 < count; b0 += kBatch) {
+    uint4 kr[4][KSTEPS / 2];
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {           // lane (gid, tig): key b0+8nt+gid, dims 32kp+8tig..+7
+      const int c = b0 + nt * 8 + gid;
+      const int32_t jj = jlist[c < count ? c : b0];
+      const T* row = kbase + static_cast<int64_t>(jj) * p.k_sn + 8 * tig;
+#pragma unroll
+      for (int kp = 0; kp < KSTEPS / 2; ++kp) kr[nt][kp] = __ldg(reinterpret_cast<const uint4*>(row + kp * 32));
+    }
+    float sc[4][4];
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+#pragma unroll
+      for (int kp = 0; kp < KSTEPS / 2; ++kp) {
+        mma16816<T>(sc[nt], qa[2 * kp], kr[nt][kp].x, kr[nt][kp].y);
+        mma16816<T>(sc[nt], qa[2 * kp + 1], kr[nt][kp].z, kr[nt][kp].w);
+      }
+    }
+    if (gid == 0) {
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int c = b0 + nt * 8 + 2 * tig + e;
+          if (c < count)
+            s.keys[c] = rank_key(sc[nt][e] + sc[nt][2 + e], static_cast<uint32_t>(jlist[c]));
+        }
+      }
+    }
+  }
+  __syncwarp();
+
+  // ---- 3. keep the top k: radix select over the 64-bit keys ----
+  const int64_t obase = ((static_cast<int64_t>(bat) * p.n_q + i) * p.h_kv + h) * p.top_k;
+  const uint64_t* src = s.keys;
+  int nsel = count;
+  if (count > k_eff) {
+    uint64_t prefix = 0ull, mask = 0ull;
+    int need = k_eff;
+    for (int shift = 56; shift >= 0; shift -= 8) {
+      for (int b = lane; b < 256; b += kWarp) s.hist[b] = 0u;
+      __syncwarp();
+      for (int idx = lane; idx < count; idx += kWarp) {
+        const uint64_t kv = s.keys[idx];
+        if ((kv & mask) == prefix) atomicAdd(&s.hist[(kv >> shift) & 255u], 1u);
+      }
+      __syncwarp();
+      // lane l owns digits 255-8l .. 248-8l (descending)
+      uint32_t cnt[8];
+      uint32_t local = 0;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        cnt[q] = s.hist[255 - 8 * lane - q];
+        local += cnt[q];
+      }
+      uint32_t inc = local;
+#pragma unroll
+      for (int o = 1; o < kWarp; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += y;
+      }
+      const uint32_t exc = inc - local;
+      const bool mine = exc < static_cast<uint32_t>(need) && static_cast<uint32_t>(need) <= inc;
+      int dsel = 0;
+      uint32_t above = 0, dcount = 0;
+      if (mine) {
+        uint32_t acc = exc;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          if (dcount == 0 && acc + cnt[q] >= static_cast<uint32_t>(need)) {
+            dsel = 255 - 8 * lane - q;
+            above = acc;
+            dcount = cnt[q];
+          }
+          acc += cnt[q];
+        }
+      }
+      const int src_lane = __ffs(__ballot_sync(0xffffffffu, mine)) - 1;
+      dsel = __shfl_sync(0xffffffffu, dsel, src_lane);
+      above = __shfl_sync(0xffffffffu, above, src_lane);
+      dcount = __shfl_sync(0xffffffffu, dcount, src_lane);
+      prefix |= static_cast<uint64_t>(dsel) << shift;
+      mask |= 0xffull << shift;
+      need -= static_cast<int>(above);
+      if (dcount == static_cast<uint32_t>(need)) break;
+      __syncwarp();
+    }
+    // compact the keys >= prefix (exactly k_eff of them) into sel[]
+    int base = 0;
+    for (int idx0 = 0; idx0 < count; idx0 += kWarp) {
+      const int idx = idx0 + lane;
+      const uint64_t kv = idx < count ? s.keys[idx] : 0ull;
+      const bool take = idx < count && kv >= prefix;
+      const unsigned bal = __ballot_sync(0xffffffffu, take);
+      if (take) s.sel[base + __popc(bal & ((1u << lane) - 1u))] = kv;
+      base += __popc(bal);
+    }
+    __syncwarp();
+    src = s.sel;
+    nsel = k_eff;
+  }
+
+  // ---- 4. sort the selected keys, write them; filler; padding ----
+  if (nsel <= 32 * 8) sort_and_write<8>(src, nsel, lane, p, obase);
+  else sort_and_write<16>(src, nsel, lane, p, obase);
+  auto put = [&](int slot, int32_t jj) {
+    if (p.index_i64) static_cast<int64_t*>(p.out)[obase + slot] = jj;
+    else static_cast<int32_t*>(p.out)[obase + slot] = jj;
+  };
+  if (count < k_eff) {
+    const int need = k_eff - count;
+    const int words = (k_eff + 31) / 32;
+    if (lane < words) s.bitmap[lane] = 0u;
+    __syncwarp();
+    for (int e = lane; e < count; e += kWarp) {
+      const uint32_t jj = rank_key_index(s.keys[e]);
+      if (jj < static_cast<uint32_t>(k_eff)) atomicOr(&s.bitmap[jj >> 5], 1u << (jj & 31));
+    }
+    __syncwarp();
+    uint32_t free_bits = 0;
+    if (lane < words) {
+      free_bits = ~s.bitmap[lane];
+      if (lane == words - 1 && (k_eff & 31)) free_bits &= (1u << (k_eff & 31)) - 1u;
+    }
+    const int nfree = __popc(free_bits);
+    int fin = nfree;
+#pragma unroll
+    for (int o = 1; o < kWarp; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, fin, o);
+      if (lane >= o) fin += y;
+    }
+    int rank = fin - nfree;
+    while (free_bits && rank < need) {
+      const int bit = __ffs(free_bits) - 1;
+      free_bits &= free_bits - 1;
+      put(count + rank, lane * 32 + bit);
+      ++rank;
+    }
+  }
+  for (int e = k_eff + lane; e < p.top_k; e += kWarp) put(e, 0);
+  if (p.cand_counts && lane == 0)
+    p.cand_counts[(static_cast<int64_t>(bat) * p.n_q + i) * p.h_kv + h] = count;
+}
+
+bool rescore_mma_supported(const RescoreParams& p, ssa_dtype dt) {
+  return (dt == SSA_BF16 || dt == SSA_F16) && (p.d == 64 || p.d == 128) && p.a <= 32;
+}
+
+template <typename T, int D>
+static cudaError_t launch_mma_t(const RescoreParams& p, cudaStream_t st) {
+  const int64_t units = static_cast<int64_t>(p.batch) * p.n_q * p.h_kv;
+  const size_t smem = sizeof(RsMmaSmem<D>) * kMmaUnits;
+  auto kern = rescore_mma_kernel<T, D>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  kern<<<static_cast<unsigned>(cdiv(units, kMmaUnits)), kMmaUnits * kWarp, smem, st>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rescore_mma(const RescoreParams& p, ssa_dtype dt, cudaStream_t st) {
+  if (dt == SSA_BF16) return p.d == 64 ? launch_mma_t<__nv_bfloat16, 64>(p, st) : launch_mma_t<__nv_bfloat16, 128>(p, st);
+  return p.d == 64 ? launch_mma_t<__half, 64>(p, st) : launch_mma_t<__half, 128>(p, st);
+}
+
+}  // namespace ssa
