@@ -50,7 +50,7 @@ int rescore_cap(int k_eff) {
 // Workspace regions for a route call.
 struct RouteLayout {
   size_t q_route, k_route, cb_norm, cb_image, q_codes, k_codes, counts, partials, bucket_ptr,
-      bucket_keys, ovf;
+      bucket_keys, ovf, ovf2;
   size_t total;
   int tiles;
   int64_t chunks;
@@ -77,6 +77,7 @@ RouteLayout route_layout(const SsaRouteArgs& a) {
   L.bucket_ptr = take(static_cast<size_t>(B * hk) * (a.n_codes + 1) * 4);
   L.bucket_keys = take(static_cast<size_t>(B * hk) * a.n * a.b * 4);
   L.ovf = take((1 + static_cast<size_t>(B * hk) * a.n_q) * 4);   // overflow count + unit list
+  L.ovf2 = take((1 + static_cast<size_t>(B * hk) * a.n_q) * 4);  // second-tier count + list
   L.total = off;
   return L;
 }
@@ -232,6 +233,8 @@ ssa_status run_stage2(const SsaRouteArgs& a, const RouteLayout& L, void* ws, cud
   rp.cap = rescore_cap(std::min(a.top_k, a.n));
   rp.ovf_count = at<int32_t>(ws, L.ovf);
   rp.ovf_list = at<int32_t>(ws, L.ovf) + 1;
+  rp.ovf2_count = at<int32_t>(ws, L.ovf2);
+  rp.ovf2_list = at<int32_t>(ws, L.ovf2) + 1;
   e = launch_rescore(rp, a.dtype, st);
   return cuda_status(e, "rescore_topk");
 }

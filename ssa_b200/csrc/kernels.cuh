@@ -70,6 +70,8 @@ struct RescoreParams {
   int cap;                     // shared-memory candidate capacity (power of two)
   int32_t* ovf_count;          // workspace: units left to the general path ...
   int32_t* ovf_list;           // ... and their indices [B * n_q * h_kv]
+  int32_t* ovf2_count;         // workspace: units passed from the first warp tier ...
+  int32_t* ovf2_list;          // ... to the second [B * n_q * h_kv]
 };
 
 // K4: sparse exact attention.

@@ -22,28 +22,29 @@
 //      key and the top k are compacted;
 //   4. the selected keys are sorted in registers (bitonic, 32*E keys) and
 //      written in order; filler and zero padding follow.
-// Units with more than kMmaCap candidates, or k > kMmaCap, go to the overflow
-// list and the CTA-wide path.
+// Two tiers: every unit first runs with room for 512 candidates (4 warps per
+// CTA); units with more go to an overflow list that a second launch runs with
+// room for 2048 (2 warps per CTA, persistent over the list).  Units beyond
+// that, or with k > 512, go to the CTA-wide path.
 #include "common.cuh"
 #include "kernels.cuh"
 #include "mma_utils.cuh"
 
 namespace ssa {
 
-constexpr int kMmaUnits = 4;        // warps (units) per CTA
-constexpr int kMmaCap = 512;        // candidates per unit on this path
+constexpr int kMaxSel = 512;        // k handled on this path
 constexpr int kBatch = 32;          // candidates per MMA batch (4 n-tiles)
 constexpr int kWalk = 4;            // bucket-walk iterations whose loads are issued together
 
-template <int D>
+template <int CAP>
 struct __align__(128) RsMmaSmem {
-  uint64_t keys[kMmaCap];                      // ranking keys of all candidates
-  uint64_t sel[kMmaCap];                       // kept key indices, then the selected keys
+  uint64_t keys[CAP];                          // ranking keys of all candidates
+  uint64_t sel[CAP];                           // kept key indices, then the selected keys
   uint32_t hist[256];
   int32_t qc[32];
   int32_t lo[32];
   int32_t pre[33];
-  uint32_t bitmap[kMmaCap / 32];
+  uint32_t bitmap[kMaxSel / 32];
 };
 
 // Descending bitonic sort of 32*E keys (key[e] of lane l at position e*32+l).
@@ -100,16 +101,10 @@ __device__ __forceinline__ void sort_and_write(const uint64_t* src, int nsel, in
   }
 }
 
-template <typename T, int D>
-__global__ void __launch_bounds__(kMmaUnits * kWarp) rescore_mma_kernel(RescoreParams p) {
-  constexpr int SEGS = D * 2 / 16;
+template <typename T, int D, int CAP>
+__device__ __forceinline__ void rescore_mma_unit(const RescoreParams& p, int64_t unit, RsMmaSmem<CAP>& s,
+                                                 int lane, int32_t* out_list, int32_t* out_count) {
   constexpr int KSTEPS = D / 16;
-  extern __shared__ __align__(128) unsigned char dyn[];
-  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
-  RsMmaSmem<D>& s = reinterpret_cast<RsMmaSmem<D>*>(dyn)[warp];
-  const int64_t units = static_cast<int64_t>(p.batch) * p.n_q * p.h_kv;
-  const int64_t unit = static_cast<int64_t>(blockIdx.x) * kMmaUnits + warp;
-  if (unit >= units) return;
   // head-major, largest query positions first within a head (as the CTA path)
   const int bh = static_cast<int>(unit / p.n_q);
   const int i = p.n_q - 1 - static_cast<int>(unit % p.n_q);
@@ -235,12 +230,12 @@ __global__ void __launch_bounds__(kMmaUnits * kWarp) rescore_mma_kernel(RescoreP
     for (int w = 0; w < kWalk; ++w) {
       const unsigned bal = __ballot_sync(0xffffffffu, keep[w]);
       const int slot = count + __popc(bal & ((1u << lane) - 1u));
-      if (keep[w] && slot < kMmaCap) jlist[slot] = j[w];
+      if (keep[w] && slot < CAP) jlist[slot] = j[w];
       count += __popc(bal);
     }
   }
-  if (count > kMmaCap || k_eff > kMmaCap) {
-    if (lane == 0) p.ovf_list[atomicAdd(p.ovf_count, 1)] = static_cast<int32_t>(unit);
+  if (count > CAP || k_eff > kMaxSel) {
+    if (lane == 0) out_list[atomicAdd(out_count, 1)] = static_cast<int32_t>(unit);
     return;
   }
   __syncwarp();
@@ -393,6 +388,28 @@ __global__ void __launch_bounds__(kMmaUnits * kWarp) rescore_mma_kernel(RescoreP
     p.cand_counts[(static_cast<int64_t>(bat) * p.n_q + i) * p.h_kv + h] = count;
 }
 
+// All units (LIST false) or the units of a list (count read on the device;
+// warps stride over it).
+template <typename T, int D, int CAP, int UNITS, bool LIST>
+__global__ void __launch_bounds__(UNITS * kWarp) rescore_mma_kernel(RescoreParams p, const int32_t* in_list,
+                                                                    const int32_t* in_count, int32_t* out_list,
+                                                                    int32_t* out_count) {
+  extern __shared__ __align__(128) unsigned char dyn[];
+  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+  RsMmaSmem<CAP>& s = reinterpret_cast<RsMmaSmem<CAP>*>(dyn)[warp];
+  const int64_t wi = static_cast<int64_t>(blockIdx.x) * UNITS + warp;
+  if constexpr (!LIST) {
+    const int64_t units = static_cast<int64_t>(p.batch) * p.n_q * p.h_kv;
+    if (wi < units) rescore_mma_unit<T, D, CAP>(p, wi, s, lane, out_list, out_count);
+  } else {
+    const int64_t n = *in_count;
+    for (int64_t it = wi; it < n; it += static_cast<int64_t>(gridDim.x) * UNITS) {
+      rescore_mma_unit<T, D, CAP>(p, in_list[it], s, lane, out_list, out_count);
+      __syncwarp();
+    }
+  }
+}
+
 bool rescore_mma_supported(const RescoreParams& p, ssa_dtype dt) {
   return (dt == SSA_BF16 || dt == SSA_F16) && (p.d == 64 || p.d == 128) && p.a <= 32;
 }
@@ -400,11 +417,27 @@ bool rescore_mma_supported(const RescoreParams& p, ssa_dtype dt) {
 template <typename T, int D>
 static cudaError_t launch_mma_t(const RescoreParams& p, cudaStream_t st) {
   const int64_t units = static_cast<int64_t>(p.batch) * p.n_q * p.h_kv;
-  const size_t smem = sizeof(RsMmaSmem<D>) * kMmaUnits;
-  auto kern = rescore_mma_kernel<T, D>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  // tier 1: every unit, room for 512 candidates; overflow -> ovf list
+  constexpr int U1 = 4, C1 = 512;
+  const size_t smem1 = sizeof(RsMmaSmem<C1>) * U1;
+  auto k1 = rescore_mma_kernel<T, D, C1, U1, false>;
+  cudaError_t e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem1));
   if (e != cudaSuccess) return e;
-  kern<<<static_cast<unsigned>(cdiv(units, kMmaUnits)), kMmaUnits * kWarp, smem, st>>>(p);
+  e = cudaMemsetAsync(p.ovf2_count, 0, sizeof(int32_t), st);
+  if (e != cudaSuccess) return e;
+  k1<<<static_cast<unsigned>(cdiv(units, U1)), U1 * kWarp, smem1, st>>>(p, nullptr, nullptr, p.ovf2_list,
+                                                                       p.ovf2_count);
+  // tier 2: the overflow units, room for 2048; overflow -> the CTA-wide path
+  constexpr int U2 = 2, C2 = 2048;
+  const size_t smem2 = sizeof(RsMmaSmem<C2>) * U2;
+  auto k2 = rescore_mma_kernel<T, D, C2, U2, true>;
+  e = cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem2));
+  if (e != cudaSuccess) return e;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  k2<<<static_cast<unsigned>(sms * 3), U2 * kWarp, smem2, st>>>(p, p.ovf2_list, p.ovf2_count, p.ovf_list,
+                                                                p.ovf_count);
   return cudaGetLastError();
 }
 
