@@ -22,7 +22,14 @@
 
 namespace ssa {
 
-constexpr int kMmaWarps = 4;
+#ifndef SSA_ATTN_WARPS
+#define SSA_ATTN_WARPS 4
+#endif
+#ifndef SSA_ATTN_STAGES
+#define SSA_ATTN_STAGES 2
+#endif
+constexpr int kMmaWarps = SSA_ATTN_WARPS;     // warps (units) per CTA
+constexpr int kStages = SSA_ATTN_STAGES;      // chunks of 16 keys per warp ring
 constexpr int kChunk = 16;
 
 // byte offset of 16-byte segment `seg` of row `row` in a [kChunk][D] tile
@@ -39,7 +46,7 @@ __global__ void __launch_bounds__(kMmaWarps * kWarp) sparse_attn_mma_kernel(Attn
   constexpr int NT = D / 8;                       // PV n-tiles
   extern __shared__ __align__(128) unsigned char smem[];
   const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
-  unsigned char* wbuf = smem + warp * (4 * TILE);  // [stage][K|V][TILE]
+  unsigned char* wbuf = smem + warp * (2 * kStages * TILE);  // [stage][K|V][TILE]
   const uint32_t wbase = static_cast<uint32_t>(__cvta_generic_to_shared(wbuf));
 
   const int64_t units = static_cast<int64_t>(p.batch) * p.h_kv * p.n_q;
@@ -111,19 +118,27 @@ __global__ void __launch_bounds__(kMmaWarps * kWarp) sparse_attn_mma_kernel(Attn
   float l0 = 0.f, l1 = 0.f;                       // this thread's partial row sums
   const float sl2 = p.inv_scale * 1.4426950408889634f;
 
-  int64_t j_cur = load_index(0);
-  issue(0, 0, j_cur);
+  // ring of kStages chunks: chunk c lives in stage c % kStages; one cp.async
+  // group per chunk (empty groups past the end keep wait_group constant)
+  int64_t jring[kStages];
+#pragma unroll
+  for (int sidx = 0; sidx < kStages - 1; ++sidx) {
+    jring[sidx] = sidx < nchunks ? load_index(sidx) : -1;
+    if (sidx < nchunks) issue(sidx, sidx, jring[sidx]);
+    else cp_commit();
+  }
   for (int c = 0; c < nchunks; ++c) {
-    const int stage = c & 1;
-    int64_t j_next = -1;
-    if (c + 1 < nchunks) {
-      j_next = load_index(c + 1);
-      issue(c + 1, stage ^ 1, j_next);
-      cp_wait<1>();
+    const int stage = c % kStages;
+    const int nx = c + kStages - 1;
+    if (nx < nchunks) {
+      jring[nx % kStages] = load_index(nx);
+      issue(nx, nx % kStages, jring[nx % kStages]);
     } else {
-      cp_wait<0>();
+      cp_commit();
     }
+    cp_wait<kStages - 1>();
     __syncwarp();
+    const int64_t j_cur = jring[stage];
     // validity of the chunk's 16 keys
     bool valid = false;
     if (lane < kChunk) {
@@ -219,7 +234,6 @@ __global__ void __launch_bounds__(kMmaWarps * kWarp) sparse_attn_mma_kernel(Attn
       mma16816<T>(o[2 * t2 + 1], pb, b2, b3);
     }
     __syncwarp();
-    j_cur = j_next;
   }
   // ---- normalise and store rows gid (< g) ----
   l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
@@ -255,7 +269,7 @@ template <typename T, int D>
 static cudaError_t launch_mma(const AttnParams& p, cudaStream_t st) {
   const int64_t units = static_cast<int64_t>(p.batch) * p.h_kv * p.n_q;
   const unsigned blocks = static_cast<unsigned>(cdiv(units, kMmaWarps));
-  const size_t smem = static_cast<size_t>(kMmaWarps) * 4 * kChunk * D * 2;
+  const size_t smem = static_cast<size_t>(kMmaWarps) * 2 * kStages * kChunk * D * 2;
   auto kern = sparse_attn_mma_kernel<T, D>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
