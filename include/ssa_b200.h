@@ -8,7 +8,9 @@
  *    device; sizes are element counts; strides are in ELEMENTS and the last
  *    (feature) dimension of every tensor must be contiguous.
  *  - The library never allocates device memory.  Scratch space is passed in
- *    as `workspace` (size from ssa_route_workspace_size()).
+ *    as `workspace` (size from ssa_route_workspace_size()); the one entry
+ *    point without a workspace, ssa_build_index_noalloc, uses a fixed 16 MiB
+ *    array built into the library instead.
  *  - Every kernel is launched on the given stream; calls are asynchronous.
  *    Argument errors are reported synchronously through the return code.
  *    Data-dependent errors found on the device (an index outside [0, n))
@@ -152,6 +154,24 @@ ssa_status ssa_select_from_scores(const float* scores, int64_t rows, int32_t n_c
 ssa_status ssa_build_index(const SsaRouteArgs* args, const int32_t* k_codes,
                            int32_t* bucket_ptr, int32_t* bucket_keys,
                            void* workspace, size_t workspace_bytes, void* stream);
+
+/* ssa_build_index without a workspace, for callers that cannot allocate
+ * device memory -- code running where cudaMalloc is unavailable or forbidden
+ * (inside a stream capture, under a runtime that owns all device memory, or
+ * in a real-time loop that must not allocate).  No reference counterpart: the
+ * reference never builds this index.
+ *
+ * Scratch (per-tile code counts and scan partials) comes from a 16 MiB array
+ * inside the library, held on every GPU that loads it until the process
+ * exits; calls needing more return SSA_ERR_UNSUPPORTED.  The first call on a
+ * device looks up that array's device address (cudaGetSymbolAddress), so make
+ * it before any stream capture.  Every call on a device uses the same array:
+ * calls that overlap on the GPU (different streams, no ordering) race and
+ * corrupt each other's result.  Nothing in the array needs clearing: each call
+ * writes every scratch word it reads.  Outputs and limits otherwise as
+ * ssa_build_index. */
+ssa_status ssa_build_index_noalloc(const SsaRouteArgs* args, const int32_t* k_codes,
+                                   int32_t* bucket_ptr, int32_t* bucket_keys, void* stream);
 
 /* Stage 2 from given codes: candidate union, causal filter, group-mean
  * re-score, top-k, filler and padding -- ssa_route without stage 1.

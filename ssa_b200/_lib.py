@@ -65,6 +65,7 @@ SIGNATURES = {
     "ssa_select_from_scores": (ctypes.c_int, [_vp, _c_i64, _c_i32, _c_i32, _vp, _vp]),
     "ssa_build_index": (ctypes.c_int, [ctypes.POINTER(SsaRouteArgs), _vp, _vp, _vp, _vp,
                                        ctypes.c_size_t, _vp]),
+    "ssa_build_index_noalloc": (ctypes.c_int, [ctypes.POINTER(SsaRouteArgs), _vp, _vp, _vp, _vp]),
     "ssa_select_candidates": (ctypes.c_int, [ctypes.POINTER(SsaRouteArgs), _vp, ctypes.c_size_t, _vp]),
     "ssa_status_str": (ctypes.c_char_p, [ctypes.c_int]),
     "ssa_last_error": (ctypes.c_char_p, []),

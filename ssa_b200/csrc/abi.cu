@@ -6,6 +6,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "common.cuh"
@@ -239,6 +240,41 @@ ssa_status run_stage2(const SsaRouteArgs& a, const RouteLayout& L, void* ws, cud
   return cuda_status(e, "rescore_topk");
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free index build (ssa_build_index_noalloc)
+//
+// For callers that cannot allocate device memory: code running inside a CUDA
+// stream capture (where cudaMalloc is not allowed), under a runtime that owns
+// all device memory, or in a loop that must never allocate.  Its scratch -- the per-tile code counts and the scan partials that
+// ssa_build_index takes from the caller's workspace -- lives in this
+// file-scope device array instead.  Every GPU that loads the library holds the
+// array until the process exits.  Host code cannot use the symbol itself as a
+// device address, so the address is looked up once per device (with that
+// device current) by cudaGetSymbolAddress and cached.
+// ---------------------------------------------------------------------------
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;   // 16 MiB
+__device__ __align__(256) unsigned char g_index_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_addr[kMaxDevices] = {};
+
+ssa_status noalloc_scratch(void** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(SSA_ERR_UNSUPPORTED, "device ordinal %d >= %d", dev, kMaxDevices);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_addr[dev] == nullptr) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_index_scratch);
+    if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(index scratch)");
+    g_scratch_addr[dev] = ptr;
+  }
+  *out = g_scratch_addr[dev];
+  return SSA_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -312,6 +348,33 @@ ssa_status ssa_build_index(const SsaRouteArgs* args, const int32_t* k_codes, int
   if (args->batch == 0) return SSA_OK;
   ssa::IndexParams ip = index_params(*args, L, workspace, k_codes, bucket_ptr, bucket_keys);
   return cuda_status(ssa::launch_build_index(ip, static_cast<cudaStream_t>(stream)), "build_index");
+}
+
+ssa_status ssa_build_index_noalloc(const SsaRouteArgs* args, const int32_t* k_codes, int32_t* bucket_ptr,
+                                   int32_t* bucket_keys, void* stream) {
+  ssa_status s = check_route(args, false, false);
+  if (s != SSA_OK) return s;
+  if (!k_codes || !bucket_ptr || !bucket_keys) return fail(SSA_ERR_INVALID_ARG, "NULL pointer");
+  // the index build reads only the counts and partials regions of the layout
+  const RouteLayout L = route_layout(*args);
+  const size_t counts_bytes = round_up(static_cast<size_t>(args->batch) * args->h_kv * args->n_codes * L.tiles * 4);
+  const size_t partial_bytes = static_cast<size_t>(args->batch) * args->h_kv * L.chunks * 4;
+  if (counts_bytes + partial_bytes > kNoAllocScratchBytes)
+    return fail(SSA_ERR_UNSUPPORTED,
+                "index build needs %zu bytes of scratch; the allocation-free entry point holds %zu "
+                "(use ssa_build_index with a workspace)",
+                counts_bytes + partial_bytes, kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  s = noalloc_scratch(&scratch);
+  if (s != SSA_OK) return s;
+  if (args->batch == 0) return SSA_OK;
+  RouteLayout S{};
+  S.counts = 0;
+  S.partials = counts_bytes;
+  S.tiles = L.tiles;
+  S.chunks = L.chunks;
+  ssa::IndexParams ip = index_params(*args, S, scratch, k_codes, bucket_ptr, bucket_keys);
+  return cuda_status(ssa::launch_build_index(ip, static_cast<cudaStream_t>(stream)), "build_index_noalloc");
 }
 
 ssa_status ssa_select_candidates(const SsaRouteArgs* args, void* workspace, size_t workspace_bytes,
