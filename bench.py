@@ -46,7 +46,11 @@ sys.path.insert(0, ROOT)
 
 METRIC = "SSA fwd tokens/s per GPU (n=32k, k=256, bf16) and % of HBM/tensor roofline"
 UNIT = "tokens/s"
-LAUNCHES_PER_STEP = 12   # route: cb-normalize, 2x projection, 2x code select, index (count, 3x scan, scatter), rescore; attn: 1
+# kernels of libssa_sm100a.so launched per step (config 3, bf16): route = codebook normalise,
+# codebook tensor-core image, 2x projection, 2x tcgen05 code scoring, index (count, 3x scan,
+# scatter), re-score tier 1, tier 2, general overflow pass; attention = 1.  (Two 4-byte
+# cudaMemsetAsync of the overflow counters are not kernels and not counted.)
+LAUNCHES_PER_STEP = 15
 
 
 def parse():
@@ -181,7 +185,7 @@ def run_reference(args):
     t_cpu = cpu_inputs(shape, args.seed)
     vals, secs = [], []
     for it in range(args.warmup + args.steps):
-        v, s, sample = cpu_sample(t_cpu, shape, rows=128)
+        v, s, sample = cpu_sample(t_cpu, shape, rows=64)
         if it >= args.warmup:
             vals.append(v)
             secs.append(s)
@@ -273,6 +277,7 @@ def run_ours(args):
         total_ms = float(tt.item())
     ms_step = total_ms / args.steps
     value = world * n / (ms_step / 1e3)
+    in_mb = sum(x.numel() * x.element_size() for x in (q, k, v)) / 1e6
 
     # roofline of the sparse-attention kernel (one launch per step)
     hbm, tflops, peak_kind = load_peaks()
@@ -344,9 +349,9 @@ def run_ours(args):
                 "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
                 "data": "synthetic (seeded: Q/K ~ N(0,1), 5% planted keys around 64 centroids, V ~ N(0,1))",
-                "config": {"workload": "config3 (op-level sweep at n=32768)", **shape.asdict(),
+                "config": {"workload": f"config3 (op-level sweep at n={n})", **shape.asdict(),
                            "per_rank": "one independent sequence per GPU",
-                           "l2": "inputs 403 MB > 126 MB L2, no flush",
+                           "l2": f"inputs {in_mb:.0f} MB > 126 MB L2, no flush",
                            "parallelism": f"batch-units x{world}"},
                 "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
                 "gpu_launches": LAUNCHES_PER_STEP * args.steps}
