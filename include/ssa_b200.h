@@ -53,6 +53,9 @@ typedef enum {
 
 /* Bits OR-ed into a device status word. */
 #define SSA_DEVICE_INDEX_OOB 0x1   /* sparse_attn: an index < 0 or >= n was skipped  */
+#define SSA_DEVICE_BAD_CODE 0x2    /* a caller-given code outside [0, n_codes) was
+                                      read as code 0; the index and the indices are
+                                      undefined                                     */
 #define SSA_DEVICE_TIMEOUT 0x100   /* route: a pipeline wait gave up (~1 s); the
                                       affected codes are undefined                  */
 
@@ -90,7 +93,8 @@ typedef struct {
   void* indices;                 /* [B, n_q, h_kv, top_k] contiguous          */
   ssa_index_dtype index_dtype;
   int32_t* q_codes;              /* optional [B, n_q, h_kv, a] contiguous     */
-  int32_t* k_codes;              /* optional [B, n, h_kv, b] contiguous       */
+  int32_t* k_codes;              /* optional [B, n, h_kv, b] contiguous,
+                                    16-byte aligned                           */
   int32_t* cand_counts;          /* optional [B, n_q, h_kv]: unique candidates */
   int32_t* status;               /* optional device word, SSA_DEVICE_* bits   */
 } SsaRouteArgs;
@@ -113,6 +117,18 @@ ssa_status ssa_route(const SsaRouteArgs* args, void* workspace, size_t workspace
  * writes args->k_codes (required). */
 ssa_status ssa_code_assign(const SsaRouteArgs* args, void* workspace, size_t workspace_bytes,
                            void* stream);
+
+/* CodebookRouter.forward (ssa/router.py:73-149) with the key codes given:
+ * reads args->k_codes [B, n, h_kv, b] -- as ssa_code_assign writes them, the
+ * b codes of one key distinct -- instead of computing them from k, then
+ * computes the query codes and runs stage 2 exactly as ssa_route.  For query
+ * shards of one long sequence: each GPU assigns codes to its own key shard
+ * (ssa_code_assign), the shards' codes and keys are gathered, and every GPU
+ * routes its own queries (q_offset, n_q) against all n keys.  A code outside
+ * [0, n_codes) sets SSA_DEVICE_BAD_CODE.  The reference computes the key codes
+ * inline (ssa/router.py:114-130); the split is this library's. */
+ssa_status ssa_route_with_key_codes(const SsaRouteArgs* args, void* workspace,
+                                   size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Sparse exact attention (stage 3)                                          */

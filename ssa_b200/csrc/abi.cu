@@ -122,6 +122,9 @@ ssa_status check_route(const SsaRouteArgs* a, bool need_q, bool need_stage2) {
     return fail(SSA_ERR_INVALID_ARG, "codebook_heads %d must be 1 or num_kv_heads", a->codebook_heads);
   if (!a->k || !a->w_kr || !a->codebook) return fail(SSA_ERR_INVALID_ARG, "k / w_kr / codebook is NULL");
   if (need_q && (!a->q || !a->w_qr)) return fail(SSA_ERR_INVALID_ARG, "q / w_qr is NULL");
+  // the re-score reads the b = 4 codes of a key as one 16-byte vector
+  if (a->k_codes && !aligned16(a->k_codes))
+    return fail(SSA_ERR_ALIGNMENT, "k_codes must be 16-byte aligned");
   if (!aligned16(a->k) || !stride16(a->k_stride_n, a->dtype) || !stride16(a->k_stride_h, a->dtype) ||
       !stride16(a->k_stride_b, a->dtype))
     return fail(SSA_ERR_ALIGNMENT, "k must be 16-byte aligned with 16-byte strides");
@@ -162,7 +165,7 @@ cudaError_t score_and_select(const SsaRouteArgs& a, const RouteLayout& L, void* 
 }
 
 ssa_status run_stage1(const SsaRouteArgs& a, const RouteLayout& L, void* ws, cudaStream_t st,
-                      bool queries, int32_t* q_codes, int32_t* k_codes) {
+                      bool keys, bool queries, int32_t* q_codes, int32_t* k_codes) {
   using namespace ssa;
   cudaError_t e = launch_codebook_normalize(a.codebook, a.w_dtype, at<float>(ws, L.cb_norm),
                                             static_cast<int64_t>(a.codebook_heads) * a.n_codes, a.d_s, st);
@@ -172,14 +175,15 @@ ssa_status run_stage1(const SsaRouteArgs& a, const RouteLayout& L, void* ws, cud
                               a.n_codes, a.d_s, st);
     if (e != cudaSuccess) return cuda_status(e, "codebook_image");
   }
-  // keys
-  RouteProjectParams kp{a.k, a.k_stride_b, a.k_stride_n, a.k_stride_h, a.w_kr,
-                        at<float>(ws, L.k_route), static_cast<int64_t>(a.batch) * a.h_kv * a.n, a.n,
-                        a.h_kv, 1, a.d, a.d_s};
-  e = launch_route_project(kp, a.dtype, a.w_dtype, st);
-  if (e != cudaSuccess) return cuda_status(e, "route_project(k)");
-  e = score_and_select(a, L, ws, at<float>(ws, L.k_route), a.n, a.b, k_codes, st);
-  if (e != cudaSuccess) return cuda_status(e, "code_select(k)");
+  if (keys) {
+    RouteProjectParams kp{a.k, a.k_stride_b, a.k_stride_n, a.k_stride_h, a.w_kr,
+                          at<float>(ws, L.k_route), static_cast<int64_t>(a.batch) * a.h_kv * a.n, a.n,
+                          a.h_kv, 1, a.d, a.d_s};
+    e = launch_route_project(kp, a.dtype, a.w_dtype, st);
+    if (e != cudaSuccess) return cuda_status(e, "route_project(k)");
+    e = score_and_select(a, L, ws, at<float>(ws, L.k_route), a.n, a.b, k_codes, st);
+    if (e != cudaSuccess) return cuda_status(e, "code_select(k)");
+  }
   if (queries && a.n_q > 0) {
     RouteProjectParams qp{a.q, a.q_stride_b, a.q_stride_n, a.q_stride_h, a.w_qr,
                           at<float>(ws, L.q_route), static_cast<int64_t>(a.batch) * a.h_kv * a.n_q,
@@ -200,6 +204,7 @@ ssa::IndexParams index_params(const SsaRouteArgs& a, const RouteLayout& L, void*
   ip.bucket_keys = bucket_keys;
   ip.counts = at<uint32_t>(ws, L.counts);
   ip.partials = at<uint32_t>(ws, L.partials);
+  ip.status = a.status;
   ip.batch = a.batch;
   ip.n = a.n;
   ip.h_kv = a.h_kv;
@@ -228,6 +233,7 @@ ssa_status run_stage2(const SsaRouteArgs& a, const RouteLayout& L, void* ws, cud
   rp.out = a.indices;
   rp.index_i64 = a.index_dtype == SSA_I64;
   rp.cand_counts = a.cand_counts;
+  rp.status = a.status;
   rp.batch = a.batch; rp.n = a.n; rp.n_q = a.n_q; rp.q_offset = a.q_offset;
   rp.h_kv = a.h_kv; rp.group = a.h_q / a.h_kv; rp.d = a.d; rp.a = a.a; rp.b = a.b;
   rp.n_codes = a.n_codes; rp.top_k = a.top_k; rp.causal = a.causal ? 1 : 0;
@@ -309,9 +315,25 @@ ssa_status ssa_route(const SsaRouteArgs* args, void* workspace, size_t workspace
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int32_t* qc = args->q_codes ? args->q_codes : at<int32_t>(workspace, L.q_codes);
   int32_t* kc = args->k_codes ? args->k_codes : at<int32_t>(workspace, L.k_codes);
-  s = run_stage1(*args, L, workspace, st, true, qc, kc);
+  s = run_stage1(*args, L, workspace, st, true, true, qc, kc);
   if (s != SSA_OK) return s;
   return run_stage2(*args, L, workspace, st, qc, kc);
+}
+
+ssa_status ssa_route_with_key_codes(const SsaRouteArgs* args, void* workspace, size_t workspace_bytes,
+                                   void* stream) {
+  ssa_status s = check_route(args, true, true);
+  if (s != SSA_OK) return s;
+  if (!args->k_codes) return fail(SSA_ERR_INVALID_ARG, "k_codes is NULL (it is the input here)");
+  const RouteLayout L = route_layout(*args);
+  if (!workspace || workspace_bytes < L.total)
+    return fail(SSA_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", L.total, workspace_bytes);
+  if (args->batch == 0 || args->n_q == 0) return SSA_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int32_t* qc = args->q_codes ? args->q_codes : at<int32_t>(workspace, L.q_codes);
+  s = run_stage1(*args, L, workspace, st, false, true, qc, nullptr);
+  if (s != SSA_OK) return s;
+  return run_stage2(*args, L, workspace, st, qc, args->k_codes);
 }
 
 ssa_status ssa_code_assign(const SsaRouteArgs* args, void* workspace, size_t workspace_bytes,
@@ -323,7 +345,7 @@ ssa_status ssa_code_assign(const SsaRouteArgs* args, void* workspace, size_t wor
   if (!workspace || workspace_bytes < L.total)
     return fail(SSA_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", L.total, workspace_bytes);
   if (args->batch == 0) return SSA_OK;
-  return run_stage1(*args, L, workspace, static_cast<cudaStream_t>(stream), false, nullptr,
+  return run_stage1(*args, L, workspace, static_cast<cudaStream_t>(stream), true, false, nullptr,
                     args->k_codes);
 }
 

@@ -132,6 +132,16 @@ __device__ __forceinline__ void set_status(int32_t* status, int32_t bits) {
   if (status) atomicOr(status, bits);
 }
 
+// Codes can come from the caller (ssa_build_index, ssa_select_candidates,
+// ssa_route_with_key_codes).  One outside [0, n_codes) is flagged and read as
+// code 0, so that no input can make the index kernels address memory outside
+// the histogram, the offsets or the bucket table.
+__device__ __forceinline__ int checked_code(int c, int n_codes, int32_t* status) {
+  if (static_cast<unsigned>(c) < static_cast<unsigned>(n_codes)) return c;
+  set_status(status, SSA_DEVICE_BAD_CODE);
+  return 0;
+}
+
 __host__ __device__ constexpr inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 }  // namespace ssa

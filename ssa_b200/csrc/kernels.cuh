@@ -47,6 +47,7 @@ struct IndexParams {
   int32_t* bucket_keys;    // [B*h_kv, n*b]
   uint32_t* counts;        // [B*h_kv, n_codes, tiles] workspace
   uint32_t* partials;      // [B*h_kv, chunks] workspace
+  int32_t* status;         // optional device word (SSA_DEVICE_BAD_CODE)
   int batch, n, h_kv, b, n_codes, tile_keys, tiles;
   int64_t chunks;          // scan chunks per (bat, h)
 };
@@ -66,6 +67,7 @@ struct RescoreParams {
   const int32_t* bucket_keys;  // [B*h_kv, n*b]
   void* out; int index_i64;    // [B, n_q, h_kv, top_k]
   int32_t* cand_counts;        // optional [B, n_q, h_kv]
+  int32_t* status;             // optional device word (SSA_DEVICE_BAD_CODE)
   int batch, n, n_q, q_offset, h_kv, group, d, a, b, n_codes, top_k, causal;
   int cap;                     // shared-memory candidate capacity (power of two)
   int32_t* ovf_count;          // workspace: units left to the general path ...

@@ -149,7 +149,8 @@ __device__ void rescore_unit_block(const RescoreParams& p, int64_t unit, RsStati
   if (threadIdx.x < kWarp) {
     int len = 0;
     if (threadIdx.x < a) {
-      const int c = p.q_codes[((static_cast<int64_t>(bat) * p.n_q + i) * p.h_kv + h) * a + threadIdx.x];
+      const int c = checked_code(p.q_codes[((static_cast<int64_t>(bat) * p.n_q + i) * p.h_kv + h) * a + threadIdx.x],
+                                 p.n_codes, p.status);
       const int32_t* ptr = p.bucket_ptr + static_cast<int64_t>(bh) * (p.n_codes + 1);
       const int lo = ptr[c];
       int hi = ptr[c + 1];
@@ -422,7 +423,8 @@ __global__ void __launch_bounds__(kWarpUnits * kWarp) rescore_warp_kernel(Rescor
 
   int len = 0;
   if (lane < a) {
-    const int c = p.q_codes[((static_cast<int64_t>(bat) * p.n_q + i) * p.h_kv + h) * a + lane];
+    const int c = checked_code(p.q_codes[((static_cast<int64_t>(bat) * p.n_q + i) * p.h_kv + h) * a + lane],
+                               p.n_codes, p.status);
     const int32_t* ptr = p.bucket_ptr + static_cast<int64_t>(bh) * (p.n_codes + 1);
     const int lo = ptr[c];
     int hi = ptr[c + 1];

@@ -118,7 +118,8 @@ __device__ __forceinline__ void rescore_mma_unit(const RescoreParams& p, int64_t
   // ---- 1a. the query's buckets (causal prefix of each) ----
   int len = 0;
   if (lane < a) {
-    const int c = p.q_codes[((static_cast<int64_t>(bat) * p.n_q + i) * p.h_kv + h) * a + lane];
+    const int c = checked_code(p.q_codes[((static_cast<int64_t>(bat) * p.n_q + i) * p.h_kv + h) * a + lane],
+                               p.n_codes, p.status);
     const int32_t* ptr = p.bucket_ptr + static_cast<int64_t>(bh) * (p.n_codes + 1);
     const int lo = ptr[c];
     int hi = ptr[c + 1];

@@ -144,6 +144,53 @@ def _route_fake(q, k, w_qr, w_kr, codebook, a, b, top_k, causal, temperature, q_
 
 
 # ---------------------------------------------------------------------------
+# route_with_key_codes
+# ---------------------------------------------------------------------------
+@torch.library.custom_op("ssa_b200::route_with_key_codes", mutates_args=())
+def route_with_key_codes(q: torch.Tensor, k: torch.Tensor, k_codes: torch.Tensor, w_qr: torch.Tensor,
+                         w_kr: torch.Tensor, codebook: torch.Tensor, a: int, top_k: int, causal: bool,
+                         temperature: float, q_offset: int, index_i64: bool) -> torch.Tensor:
+    """Stages 1-2 for the query rows ``q [B, n_q, h_q, d]`` at sequence positions
+    ``q_offset ..`` against all keys ``k [B, n, h_kv, d]``, whose codes
+    ``k_codes [B, n, h_kv, b]`` (from :func:`code_assign`) are given."""
+    dev = _require_cuda(q, k, k_codes, w_qr, w_kr, codebook)
+    q, k = _last_contig(q), _last_contig(k)
+    kc = k_codes.to(torch.int32).contiguous()
+    w_qr, w_kr, codebook = _prep_weights(w_qr, w_kr, codebook, k.dtype)
+    B, n_q, _, _ = q.shape
+    _, n, h_kv, _ = k.shape
+    if tuple(kc.shape[:3]) != (B, n, h_kv):
+        raise ValueError(f"k_codes shape {tuple(kc.shape)} does not match k {tuple(k.shape)}")
+    indices = torch.empty((B, n_q, h_kv, top_k), dtype=torch.int64 if index_i64 else torch.int32,
+                          device=dev)
+    args = route_args(q, k, w_qr, w_kr, codebook, a, kc.shape[-1], top_k, causal, temperature,
+                      q_offset, indices, index_i64, None, kc, None)
+    check = _checked() and not torch.cuda.is_current_stream_capturing()
+    status = torch.zeros(1, dtype=torch.int32, device=dev) if check else None
+    args.status = _ptr(status)
+    ws = workspace(args, dev)
+    with torch.cuda.device(dev):
+        L.check("ssa_route_with_key_codes",
+                L.lib().ssa_route_with_key_codes(ctypes.byref(args), ws.data_ptr(), ws.numel(),
+                                                 _stream(dev)))
+    if status is not None:
+        bits = int(status.item())
+        if bits & L.SSA_DEVICE_BAD_CODE:
+            raise ValueError(f"ssa_route_with_key_codes: a key code is outside [0, {codebook.shape[-2]})")
+        if bits & L.SSA_DEVICE_TIMEOUT:
+            raise RuntimeError("ssa_route_with_key_codes: a device pipeline wait timed out")
+    return indices
+
+
+@route_with_key_codes.register_fake
+def _route_with_key_codes_fake(q, k, k_codes, w_qr, w_kr, codebook, a, top_k, causal, temperature,
+                               q_offset, index_i64):
+    B, n_q, _, _ = q.shape
+    h_kv = k.shape[2]
+    return q.new_empty((B, n_q, h_kv, top_k), dtype=torch.int64 if index_i64 else torch.int32)
+
+
+# ---------------------------------------------------------------------------
 # code_assign
 # ---------------------------------------------------------------------------
 @torch.library.custom_op("ssa_b200::code_assign", mutates_args=())

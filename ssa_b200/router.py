@@ -74,6 +74,27 @@ class CodebookRouter(nn.Module):
                              self.codes_per_query, self.codes_per_key, self.top_k, bool(causal),
                              float(self.temperature), int(q_offset), index_dtype == torch.int64)
 
+    def key_codes(self, k_full: torch.Tensor) -> torch.Tensor:
+        """Batched key codes ``[B, n, h_kv, b]`` int32 of ``k [B, n, h_kv, d]``
+        (the input :meth:`route_with_key_codes` takes)."""
+        with torch.no_grad():
+            return ops.code_assign(k_full, self.W_kr.weight, self.codebook, self.codes_per_key, 1.0)
+
+    def route_with_key_codes(self, q_full: torch.Tensor, k_full: torch.Tensor, k_codes: torch.Tensor,
+                             causal: bool = True, q_offset: int = 0,
+                             index_dtype: torch.dtype = torch.int64) -> torch.Tensor:
+        """:meth:`route` for the query rows ``q [B, n_q, h_q, d]`` at positions
+        ``q_offset ..`` against all keys ``k [B, n, h_kv, d]`` whose codes are
+        given (``k_codes [B, n, h_kv, b]``, e.g. gathered from per-shard
+        :meth:`key_codes`) -> indices ``[B, n_q, h_kv, top_k]``."""
+        if q_full.shape[-2] % k_full.shape[-2]:
+            raise ValueError("num_q_heads must be divisible by num_kv_heads")
+        with torch.no_grad():
+            return ops.route_with_key_codes(q_full, k_full, k_codes, self.W_qr.weight,
+                                            self.W_kr.weight, self.codebook, self.codes_per_query,
+                                            self.top_k, bool(causal), float(self.temperature),
+                                            int(q_offset), index_dtype == torch.int64)
+
     def forward(self, q_full: torch.Tensor, k_full: torch.Tensor,
                 causal_mask: Optional[torch.Tensor] = None, hard: bool = True,
                 causal: Optional[bool] = None) -> torch.Tensor:

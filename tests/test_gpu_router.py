@@ -175,3 +175,52 @@ def test_router_deterministic_and_variable_lengths():
         b = r(q, k, causal=True)
         assert a.shape == (n, 2, 16) and torch.equal(a, b)
         assert int(a.min()) >= 0 and int(a.max()) < n
+
+
+def _random_router(n_c=1024, d=128, d_s=32, h_kv=2, a=8, b=4, k=64, seed=3):
+    torch.manual_seed(seed)
+    return ssa.CodebookRouter(head_dim=d, route_dim=d_s, num_kv_heads=h_kv, num_codebook=n_c,
+                              codes_per_key=b, codes_per_query=a, top_k=k).to(DEV)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_route_with_key_codes_matches_route_on_query_shards(dtype):
+    r = _random_router()
+    g = torch.Generator(device="cpu").manual_seed(5)
+    n = 3000
+    q = torch.randn((2, n, 8, 128), generator=g).to(DEV, dtype)
+    k = torch.randn((2, n, 2, 128), generator=g).to(DEV, dtype)
+    full, _, k_codes, _ = r.route(q, k, causal=True)
+    codes = r.key_codes(k)
+    assert torch.equal(codes, k_codes)
+    for start, length in [(0, 700), (700, 1100), (1800, 1200), (2999, 1)]:
+        got = r.route_with_key_codes(q[:, start:start + length], k, codes, causal=True, q_offset=start)
+        assert torch.equal(got, full[:, start:start + length]), (start, length)
+
+
+def test_route_with_key_codes_flags_codes_outside_the_codebook():
+    r = _random_router(n_c=512)
+    q = torch.randn((1, 600, 8, 128), device=DEV, dtype=torch.bfloat16)
+    k = torch.randn((1, 600, 2, 128), device=DEV, dtype=torch.bfloat16)
+    codes = r.key_codes(k)
+    for bad in (512, -1, 1 << 20):
+        c = codes.clone()
+        c[0, 17, 1, 2] = bad
+        with pytest.raises(ValueError, match="outside"):
+            r.route_with_key_codes(q, k, c, causal=True)
+    # the device word is clear again on valid codes
+    r.route_with_key_codes(q, k, codes, causal=True)
+    torch.cuda.synchronize()
+
+
+def test_route_with_key_codes_refuses_unaligned_codes():
+    from ssa_b200._lib import SSAError
+    r = _random_router(n_c=512)
+    q = torch.randn((1, 64, 8, 128), device=DEV, dtype=torch.bfloat16)
+    k = torch.randn((1, 64, 2, 128), device=DEV, dtype=torch.bfloat16)
+    codes = r.key_codes(k)
+    buf = torch.empty(codes.numel() + 1, dtype=torch.int32, device=DEV)
+    shifted = buf[1:].view(codes.shape)                      # 4 bytes past a 16-byte boundary
+    shifted.copy_(codes)
+    with pytest.raises(SSAError, match="aligned"):
+        r.route_with_key_codes(q, k, shifted, causal=True)
