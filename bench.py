@@ -185,7 +185,7 @@ def run_reference(args):
     t_cpu = cpu_inputs(shape, args.seed)
     vals, secs = [], []
     for it in range(args.warmup + args.steps):
-        v, s, sample = cpu_sample(t_cpu, shape, rows=64)
+        v, s, sample = cpu_sample(t_cpu, shape, rows=256)
         if it >= args.warmup:
             vals.append(v)
             secs.append(s)
@@ -340,7 +340,7 @@ def run_ours(args):
     if rank == 0 and world == 1 and not args.no_cpu:
         cores = os.cpu_count() or 1
         torch.set_num_threads(cores)
-        cv, cs, sample = cpu_sample(cpu_inputs(shape, args.seed), shape, rows=128)
+        cv, cs, sample = cpu_sample(cpu_inputs(shape, args.seed), shape, rows=1024)
         cpu = {"value": cv, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample,
                "sample_seconds": cs}
 

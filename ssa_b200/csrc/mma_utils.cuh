@@ -24,6 +24,22 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t&
                : "r"(addr));
 }
 
+// 2^x by the MUFU.EX2 instruction (PTX ex2.approx.ftz.f32; relative error
+// about 2^-22, subnormal results flushed to zero; 2^-inf = +0).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Transpose of an 8x8 matrix of 16-bit elements held in the m8n8 fragment
+// layout (lane l: row l/4, elements 2(l%4), 2(l%4)+1).
+__device__ __forceinline__ uint32_t movm_t(uint32_t a) {
+  uint32_t d;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+  return d;
+}
+
 template <typename T>
 __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1);
 template <>

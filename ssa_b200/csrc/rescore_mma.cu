@@ -32,6 +32,9 @@
 
 namespace ssa {
 
+#ifndef SSA_RS_UNITS
+#define SSA_RS_UNITS 4
+#endif
 constexpr int kMaxSel = 512;        // k handled on this path
 constexpr int kBatch = 32;          // candidates per MMA batch (4 n-tiles)
 constexpr int kWalk = 4;            // bucket-walk iterations whose loads are issued together
@@ -47,20 +50,22 @@ struct __align__(128) RsMmaSmem {
   uint32_t bitmap[kMaxSel / 32];
 };
 
-// Descending bitonic sort of 32*E keys (key[e] of lane l at position e*32+l).
+// Descending bitonic sort of 32*E keys, blocked layout: key[e] of lane l is
+// at position l*E + e, so the stages with partner distance < E compare within
+// a lane and only log2(32) of every log2(32*E) stages shuffle.
 template <int E>
-__device__ __forceinline__ void sort_desc_cyclic(uint64_t (&key)[E], int lane) {
+__device__ __forceinline__ void sort_desc_blocked(uint64_t (&key)[E], int lane) {
   constexpr int N = 32 * E;
 #pragma unroll
   for (int k2 = 2; k2 <= N; k2 <<= 1) {
 #pragma unroll
     for (int j = k2 >> 1; j > 0; j >>= 1) {
-      if (j >= 32) {
+      if (j < E) {
 #pragma unroll
         for (int e = 0; e < E; ++e) {
-          const int f = e ^ (j >> 5);
+          const int f = e ^ j;
           if (f > e) {
-            const bool desc = ((e * 32 + lane) & k2) == 0;
+            const bool desc = ((lane * E + e) & k2) == 0;
             const uint64_t x = key[e], y = key[f];
             const bool swap = desc ? (x < y) : (x > y);
             key[e] = swap ? y : x;
@@ -70,8 +75,9 @@ __device__ __forceinline__ void sort_desc_cyclic(uint64_t (&key)[E], int lane) {
       } else {
 #pragma unroll
         for (int e = 0; e < E; ++e) {
-          const uint64_t other = __shfl_xor_sync(0xffffffffu, key[e], j);
-          const bool keep_max = (((e * 32 + lane) & k2) == 0) == ((lane & j) == 0);
+          const uint64_t other = __shfl_xor_sync(0xffffffffu, key[e], j / E);
+          const int pos = lane * E + e;
+          const bool keep_max = ((pos & k2) == 0) == ((pos & j) == 0);
           const bool gt = key[e] > other;
           key[e] = (gt == keep_max) ? key[e] : other;
         }
@@ -85,14 +91,14 @@ __device__ __forceinline__ void sort_and_write(const uint64_t* src, int nsel, in
                                                int64_t obase) {
   uint64_t key[E];
 #pragma unroll
-  for (int e = 0; e < E; ++e) {
+  for (int e = 0; e < E; ++e) {              // any input order: read conflict-free
     const int idx = e * 32 + lane;
     key[e] = idx < nsel ? src[idx] : 0ull;
   }
-  sort_desc_cyclic<E>(key, lane);
+  sort_desc_blocked<E>(key, lane);
 #pragma unroll
   for (int e = 0; e < E; ++e) {
-    const int idx = e * 32 + lane;
+    const int idx = lane * E + e;
     if (idx < nsel) {
       const int32_t j = static_cast<int32_t>(rank_key_index(key[e]));
       if (p.index_i64) static_cast<int64_t*>(p.out)[obase + idx] = j;
@@ -148,35 +154,51 @@ __device__ __forceinline__ void rescore_mma_unit(const RescoreParams& p, int64_t
   // ---- qbar as A fragments: row 0 = hi part, row 8 = lo part (lanes 0..3) ----
   // k-step pair kp covers head dims [32kp, 32kp+32); lane tig's 8 dims
   // 32kp+8tig+{0..7} feed (k 2tig..2tig+1, k 2tig+8..2tig+9) of step 2kp and
-  // of step 2kp+1, matching the B fragments loaded below.
+  // of step 2kp+1, matching the B fragments loaded below.  All lanes load the
+  // group's rows together (lane: 8-dim chunk lane % CH of heads lane / CH,
+  // + 32 / CH, ...); the chunk sums meet in shared memory.
   uint32_t qa[KSTEPS][4];
   {
+    constexpr int CH = D / 8;                     // 8-dim chunks per row
+    constexpr int HP = kWarp / CH;                // heads per pass
+    constexpr int MAXP = 16 / HP;                 // passes for a group of up to 16 heads
     const T* qrow = static_cast<const T*>(p.q) + bat * p.q_sb + static_cast<int64_t>(i) * p.q_sn +
                     static_cast<int64_t>(h) * p.group * p.q_sh;
-    const float inv_g = 1.0f / static_cast<float>(p.group);
+    const int ch = lane % CH, h0 = lane / CH;
+    float x[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) x[u] = 0.f;
+#pragma unroll
+    for (int ps = 0; ps < MAXP; ++ps) {
+      const int gg = h0 + ps * HP;
+      if (gg < p.group) {
+        float f[8];
+        load8<T>(qrow + static_cast<int64_t>(gg) * p.q_sh + ch * 8, f);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) x[u] += f[u];
+      }
+    }
+#pragma unroll
+    for (int o = CH; o < kWarp; o <<= 1)
+#pragma unroll
+      for (int u = 0; u < 8; ++u) x[u] += __shfl_xor_sync(0xffffffffu, x[u], o);
+    float* qs = reinterpret_cast<float*>(s.hist);    // D floats; hist is free until the select
+    if (lane < CH) {
+      const float inv_g = 1.0f / static_cast<float>(p.group);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) qs[ch * 8 + u] = p.group != 1 ? x[u] * inv_g : x[u];
+    }
+    __syncwarp();
 #pragma unroll
     for (int kp = 0; kp < KSTEPS / 2; ++kp) {
       qa[2 * kp][0] = qa[2 * kp][1] = qa[2 * kp][2] = qa[2 * kp][3] = 0u;
       qa[2 * kp + 1][0] = qa[2 * kp + 1][1] = qa[2 * kp + 1][2] = qa[2 * kp + 1][3] = 0u;
       if (gid == 0) {
-        float x[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) x[u] = 0.f;
-        const int e0 = kp * 32 + 8 * tig;
-        for (int gg = 0; gg < p.group; ++gg) {
-          float f[8];
-          load8<T>(qrow + static_cast<int64_t>(gg) * p.q_sh + e0, f);
-#pragma unroll
-          for (int u = 0; u < 8; ++u) x[u] += f[u];
-        }
-        if (p.group != 1) {
-#pragma unroll
-          for (int u = 0; u < 8; ++u) x[u] *= inv_g;
-        }
-        split2<T>(x[0], x[1], qa[2 * kp][0], qa[2 * kp][1]);
-        split2<T>(x[2], x[3], qa[2 * kp][2], qa[2 * kp][3]);
-        split2<T>(x[4], x[5], qa[2 * kp + 1][0], qa[2 * kp + 1][1]);
-        split2<T>(x[6], x[7], qa[2 * kp + 1][2], qa[2 * kp + 1][3]);
+        const float* y = qs + kp * 32 + 8 * tig;
+        split2<T>(y[0], y[1], qa[2 * kp][0], qa[2 * kp][1]);
+        split2<T>(y[2], y[3], qa[2 * kp][2], qa[2 * kp][3]);
+        split2<T>(y[4], y[5], qa[2 * kp + 1][0], qa[2 * kp + 1][1]);
+        split2<T>(y[6], y[7], qa[2 * kp + 1][2], qa[2 * kp + 1][3]);
       }
     }
   }
@@ -419,7 +441,7 @@ template <typename T, int D>
 static cudaError_t launch_mma_t(const RescoreParams& p, cudaStream_t st) {
   const int64_t units = static_cast<int64_t>(p.batch) * p.n_q * p.h_kv;
   // tier 1: every unit, room for 512 candidates; overflow -> ovf list
-  constexpr int U1 = 4, C1 = 512;
+  constexpr int U1 = SSA_RS_UNITS, C1 = 512;
   const size_t smem1 = sizeof(RsMmaSmem<C1>) * U1;
   auto k1 = rescore_mma_kernel<T, D, C1, U1, false>;
   cudaError_t e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem1));

@@ -46,6 +46,10 @@ def _inputs(rng, n, h_q, h_kv, d, kk, dtype, B=1, n_keys=None):
     (96, 32, 8, 128, 33, False),
     (64, 16, 1, 256, 5, True),         # g = 16, d = 256
     (40, 4, 4, 96, 300, False),        # k > n: duplicates
+    (80, 12, 1, 128, 48, True),        # g = 12: two head tiles on the tensor-core path
+    (70, 16, 1, 64, 20, False),        # g = 16, d = 64
+    (50, 8, 1, 128, 17, True),         # g = 8: one full head tile
+    (33, 2, 2, 64, 1, True),           # g = 1, k = 1
 ])
 def test_sparse_attention_matches_oracle(n, h_q, h_kv, d, kk, causal, dtype):
     rng = np.random.default_rng(n + d + kk)
@@ -69,6 +73,20 @@ def test_sparse_attention_batched_int32_scale_and_offset():
     for bi in range(B):
         ref = O.sparse_attention(qn[bi], kn[bi], vn[bi], idx[bi], scale=3.0, causal=True, q_offset=off)
         _close(out[bi], ref, torch.float32)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_sparse_attention_batched_int32_offset_16bit(dtype):
+    rng = np.random.default_rng(15)
+    B, n, h_q, h_kv, d, kk = 2, 90, 16, 2, 128, 70
+    qn, kn, vn, idx, (q, k, v) = _inputs(rng, n, h_q, h_kv, d, kk, dtype, B=B, n_keys=400)
+    off = 250
+    idx[..., 0] = rng.integers(0, off + np.arange(n) + 1)[None, :, None]
+    it = torch.from_numpy(idx).to(DEV, torch.int32)
+    out = ssa.sparse_exact_attention(q, k, v, it, scale=5.0, is_causal=True, q_offset=off)
+    for bi in range(B):
+        ref = O.sparse_attention(qn[bi], kn[bi], vn[bi], idx[bi], scale=5.0, causal=True, q_offset=off)
+        _close(out[bi], ref, dtype)
 
 
 def test_sparse_attention_strided_inputs():
@@ -97,6 +115,16 @@ def test_out_of_range_index_raises():
     idx[3, 1, 2] = 8
     with pytest.raises(IndexError):
         ssa.sparse_exact_attention(q, k, k, idx)
+
+
+def test_out_of_range_index_raises_on_the_tensor_core_path():
+    q = torch.randn(40, 8, 128, device=DEV, dtype=torch.bfloat16)
+    k = torch.randn(40, 2, 128, device=DEV, dtype=torch.bfloat16)
+    idx = torch.zeros(40, 2, 24, dtype=torch.long, device=DEV)
+    for bad in (-1, 40):
+        idx[17, 1, 20] = bad
+        with pytest.raises(IndexError):
+            ssa.sparse_exact_attention(q, k, k, idx)
 
 
 def test_deterministic():
