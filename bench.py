@@ -51,6 +51,10 @@ UNIT = "tokens/s"
 # scatter), re-score tier 1, tier 2, general overflow pass; attention = 1.  (Two 4-byte
 # cudaMemsetAsync of the overflow counters are not kernels and not counted.)
 LAUNCHES_PER_STEP = 15
+# DRAM bytes (read + write) of one sparse-attention launch at config 3, n = 32768,
+# measured by ncu (dram__bytes_read.sum + dram__bytes_write.sum, one pass on this
+# workload; profiles/sparse_attn_mma_config3.txt).  Other n scale by the query rows.
+ATTN_DRAM_BYTES_N32768 = 920.29e6
 
 
 def parse():
@@ -205,6 +209,58 @@ def run_reference(args):
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
+def stage_rooflines(lib, rargs, q_codes, k_codes, cand, shape, ws, sptr, stream, hbm, tflops, peak_kind,
+                    reps=10):
+    """Rooflines of the two router stages, each timed with CUDA events in its
+    own loop after the timed region (the C ABI launches a stage's kernels in
+    one call, so they cannot be bracketed inside ssa_route):
+      stage 1 (keys): ssa_code_assign -- codebook scoring of the n*h_kv keys on
+        tensor cores, 2*n*h_kv*N_c*d_s useful flops (plus the projection);
+      stage 2: ssa_select_candidates -- inverted index, candidate union, re-score
+        and top-k; algorithmic bytes per unit C*(4 + 16 + 2*d) + g*d*2 + k*4 with
+        C the unique candidates of the unit (from the route's cand_counts)."""
+    import torch
+    from ssa_b200 import _lib as L
+
+    n, hkv, g, d = shape.n, shape.h_kv, shape.h_q // shape.h_kv, shape.d
+    c_sum = int(cand.sum().item())
+    units = n * hkv
+    s2_bytes = c_sum * (4 + 16 + 2 * d) + units * (g * d * 2 + shape.top_k * 4)
+    s1_flops = 2.0 * n * hkv * shape.n_codes * shape.d_s
+
+    def timed(fn):
+        for _ in range(2):
+            fn()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    kc = torch.empty_like(k_codes)
+    a1 = L.SsaRouteArgs.from_buffer_copy(rargs)
+    a1.k_codes = kc.data_ptr()
+    a1.n_q = 0
+    t1 = timed(lambda: L.check("ssa_code_assign",
+                               lib.ssa_code_assign(ctypes.byref(a1), ws.data_ptr(), ws.numel(), sptr)))
+    a2 = L.SsaRouteArgs.from_buffer_copy(rargs)
+    t2 = timed(lambda: L.check("ssa_select_candidates",
+                               lib.ssa_select_candidates(ctypes.byref(a2), ws.data_ptr(), ws.numel(), sptr)))
+    f1 = s1_flops / (t1 / 1e3) / 1e12
+    b2 = s2_bytes / (t2 / 1e3) / 1e9
+    return {
+        "stage1_keys": {"call": "ssa_code_assign", "bound": "tensor", "achieved": f1, "peak": tflops,
+                        "unit": "TFLOP/s", "frac": f1 / tflops, "peak_kind": peak_kind,
+                        "algorithmic_flops": s1_flops, "ms": t1},
+        "stage2": {"call": "ssa_select_candidates", "bound": "hbm", "achieved": b2, "peak": hbm,
+                   "unit": "GB/s", "frac": b2 / hbm, "peak_kind": peak_kind,
+                   "algorithmic_bytes": s2_bytes, "mean_unique_candidates": c_sum / units, "ms": t2},
+    }
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -232,8 +288,12 @@ def run_ours(args):
     # preallocated outputs + workspace; calls go straight through the C ABI
     idx = torch.empty((1, n, hkv, kk), dtype=torch.int32, device=dev)
     out = torch.empty_like(q)
+    q_codes = torch.empty((1, n, hkv, shape.a), dtype=torch.int32, device=dev)
+    k_codes = torch.empty((1, n, hkv, shape.b), dtype=torch.int32, device=dev)
+    cand = torch.empty((1, n, hkv), dtype=torch.int32, device=dev)
     w_qr, w_kr, cb = t["w_qr"].contiguous(), t["w_kr"].contiguous(), t["codebook"].contiguous()
-    rargs = ops.route_args(q, k, w_qr, w_kr, cb, shape.a, shape.b, kk, True, 1.0, 0, idx, False)
+    rargs = ops.route_args(q, k, w_qr, w_kr, cb, shape.a, shape.b, kk, True, 1.0, 0, idx, False,
+                           q_codes, k_codes, cand)
     ws = ops.workspace(rargs, dev)
     aargs = ops.attn_args(q, k, v, idx, out, math.sqrt(d), True, 0)
     stream = torch.cuda.current_stream(dev)
@@ -284,14 +344,19 @@ def run_ours(args):
     units = n * hkv
     attn_bytes = units * kk * (2 * d * 2) + 2 * n * hq * d * 2 + units * kk * 4
     achieved = attn_bytes / (attn_ms / 1e3) / 1e9
-    traffic = os.environ.get("SSA_ATTN_DRAM_BYTES")
-    roof = {"kernel": "sparse_attn_kernel", "bound": "hbm", "achieved": achieved, "peak": hbm,
+    roof = {"kernel": "sparse_attn_mma_kernel", "bound": "hbm", "achieved": achieved, "peak": hbm,
             "unit": "GB/s", "frac": achieved / hbm, "peak_kind": peak_kind,
-            "traffic": float(traffic) if traffic else None,
+            "traffic": ATTN_DRAM_BYTES_N32768 * n / 32768,
+            "traffic_note": "ncu DRAM bytes per launch at n=32768" + ("" if n == 32768 else ", scaled by n"),
             "algorithmic_bytes_per_launch": attn_bytes, "launch_ms": attn_ms,
             "router_ms": route_ms}
+    stages = stage_rooflines(lib, rargs, q_codes, k_codes, cand, shape, ws, sptr, stream, hbm, tflops,
+                             peak_kind)
 
-    # e2e through the public API from pinned host buffers
+    # e2e through the public API from pinned host buffers.  Every step copies
+    # its q/k/v in (host -> device) and its output back (device -> host); the
+    # copies run on two copy streams so that step s+1's inputs and step s-1's
+    # output move while step s computes (double-buffered device inputs).
     e2e = None
     if not args.no_e2e:
         os.environ.setdefault("SSA_CHECKED", "0")
@@ -302,28 +367,51 @@ def run_ours(args):
             router.W_qr.weight.copy_(w_qr)
             router.W_kr.weight.copy_(w_kr)
             router.codebook.copy_(cb)
-        hq_, hk_, hv_ = (x[0].cpu().pin_memory() for x in (q, k, v))
-        hout = torch.empty(hq_.shape, dtype=hq_.dtype).pin_memory()
+        host_in = [x[0].cpu().pin_memory() for x in (q, k, v)]
+        host_out = [torch.empty(host_in[0].shape, dtype=host_in[0].dtype).pin_memory() for _ in range(2)]
+        dev_in = [[torch.empty_like(x, device=dev) for x in host_in] for _ in range(2)]
+        h2d_stream = torch.cuda.Stream(dev)
+        d2h_stream = torch.cuda.Stream(dev)
+        in_ready = [torch.cuda.Event() for _ in range(2)]
+        in_free = [torch.cuda.Event() for _ in range(2)]
 
-        def e2e_step():
-            dq = hq_.to(dev, non_blocking=True)
-            dk = hk_.to(dev, non_blocking=True)
-            dv = hv_.to(dev, non_blocking=True)
-            with torch.no_grad():
-                ind = router(dq, dk, causal=True)
-                o = ssa.sparse_exact_attention(dq, dk, dv, ind, is_causal=True)
-            hout.copy_(o, non_blocking=True)
+        def h2d(sidx):
+            b = sidx % 2
+            h2d_stream.wait_event(in_free[b])
+            with torch.cuda.stream(h2d_stream):
+                for dst, src in zip(dev_in[b], host_in):
+                    dst.copy_(src, non_blocking=True)
+            in_ready[b].record(h2d_stream)
 
-        for _ in range(max(3, args.warmup)):
-            e2e_step()
+        def run(steps):
+            h2d(0)
+            for sidx in range(steps):
+                if sidx + 1 < steps:
+                    h2d(sidx + 1)
+                b = sidx % 2
+                stream.wait_event(in_ready[b])
+                dq, dk, dv = dev_in[b]
+                with torch.no_grad():
+                    ind = router(dq, dk, causal=True)
+                    o = ssa.sparse_exact_attention(dq, dk, dv, ind, is_causal=True)
+                in_free[b].record(stream)
+                done = torch.cuda.Event()
+                done.record(stream)
+                d2h_stream.wait_event(done)
+                with torch.cuda.stream(d2h_stream):
+                    host_out[b].copy_(o, non_blocking=True)
+                o.record_stream(d2h_stream)
+            stream.wait_stream(d2h_stream)
+
+        run(max(3, args.warmup))
         torch.cuda.synchronize(dev)
         if world > 1:
             dist.barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for _ in range(args.steps):
-            e2e_step()
+        h2d_stream.wait_event(e0)
+        run(args.steps)
         e1.record(stream)
         torch.cuda.synchronize(dev)
         e_ms = e0.elapsed_time(e1)
@@ -332,15 +420,17 @@ def run_ours(args):
             dist.all_reduce(tt, op=dist.ReduceOp.MAX)
             e_ms = float(tt.item())
         e2e = {"value": world * n / (e_ms / args.steps / 1e3), "unit": UNIT,
-               "h2d_bytes_per_step": sum(x.numel() * x.element_size() for x in (hq_, hk_, hv_)),
-               "d2h_bytes_per_step": hout.numel() * hout.element_size(),
-               "ms_per_step": e_ms / args.steps, "api": "CodebookRouter.forward + sparse_exact_attention"}
+               "h2d_bytes_per_step": sum(x.numel() * x.element_size() for x in host_in),
+               "d2h_bytes_per_step": host_out[0].numel() * host_out[0].element_size(),
+               "ms_per_step": e_ms / args.steps,
+               "api": "CodebookRouter.forward + sparse_exact_attention",
+               "copies": "pinned host buffers; h2d of step s+1 and d2h of step s overlap step s's compute"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cores = os.cpu_count() or 1
         torch.set_num_threads(cores)
-        cv, cs, sample = cpu_sample(cpu_inputs(shape, args.seed), shape, rows=1024)
+        cv, cs, sample = cpu_sample(cpu_inputs(shape, args.seed), shape, rows=min(4096, shape.n))
         cpu = {"value": cv, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample,
                "sample_seconds": cs}
 
@@ -353,7 +443,7 @@ def run_ours(args):
                            "per_rank": "one independent sequence per GPU",
                            "l2": f"inputs {in_mb:.0f} MB > 126 MB L2, no flush",
                            "parallelism": f"batch-units x{world}"},
-                "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
+                "roofline": roof, "roofline_stages": stages, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
                 "gpu_launches": LAUNCHES_PER_STEP * args.steps}
         print(json.dumps(line), flush=True)
     if world > 1:
