@@ -143,6 +143,21 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// v[j] for a run-time j in [0, 32) without indexing the register array (which
+// would move it to local memory): a binary tree of selects on the bits of j.
+__device__ __forceinline__ uint32_t select32(const uint32_t (&v)[32], int j) {
+  uint32_t w[16];
+#pragma unroll
+  for (int t = 0; t < 16; ++t) w[t] = (j & 1) ? v[2 * t + 1] : v[2 * t];
+#pragma unroll
+  for (int t = 0; t < 8; ++t) w[t] = (j & 2) ? w[2 * t + 1] : w[2 * t];
+#pragma unroll
+  for (int t = 0; t < 4; ++t) w[t] = (j & 4) ? w[2 * t + 1] : w[2 * t];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) w[t] = (j & 8) ? w[2 * t + 1] : w[2 * t];
+  return (j & 16) ? w[1] : w[0];
+}
+
 // Byte offset of element k of row r in a K-major SWIZZLE_NONE image whose K
 // groups are LBO bytes apart.
 __device__ __forceinline__ uint32_t img_off(int r, int kgroup, int lbo) {
@@ -442,14 +457,17 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
           for (int j = 0; j < 32; ++j) hit |= (__uint_as_float(v[j]) >= lb ? 1u : 0u) << j;
           if (hit) {
             if (ncand + __popc(hit) > kCand) flush();      // the only flush site: keeps code small
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if (hit & (1u << j)) {
-                const float x = __uint_as_float(v[j]);
-                cand[ncand * EPI + et] =
-                    rank_key(unit_t ? x : x * inv_t, static_cast<uint32_t>(col_base + part * 32 + j));
-                ++ncand;
-              }
+            // Hits are rare (about KMAX per row over all of its columns), so
+            // each one is taken by a bit scan and a 5-level select on its
+            // column rather than by a test of all 32 columns.
+#pragma unroll 1
+            while (hit) {
+              const int j = __ffs(hit) - 1;
+              hit &= hit - 1;
+              const float x = __uint_as_float(select32(v, j));
+              cand[ncand * EPI + et] =
+                  rank_key(unit_t ? x : x * inv_t, static_cast<uint32_t>(col_base + part * 32 + j));
+              ++ncand;
             }
           }
         }
