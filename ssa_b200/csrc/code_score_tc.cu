@@ -176,7 +176,7 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
   unsigned char* a_img = base;                                        // 2 x A_BYTES
   unsigned char* b_img = a_img + 2 * G::A_BYTES;                      // kStages x B_BYTES
   // [kCand][EPI] pass-2 candidate keys; the same bytes hold the pass-1 kept
-  // values ([64][EPI] floats) and, after the last flush, the merge lists
+  // values ([32][EPI] floats) and, after the last flush, the merge lists
   // ([kEpiWG-1][kM][KMAX] keys).
   uint64_t* cand = reinterpret_cast<uint64_t*>(b_img + kStages * G::B_BYTES);
   float* kept = reinterpret_cast<float*>(cand);
@@ -377,10 +377,10 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
       if (next < total_tiles) build_a(next, static_cast<int>((tl + 1) & 1));
       bool ok = true;
 
-      // ---- pass 1: top-2 of 32 column groups on the a_hi . c_hi scores ----
-      float m1[32], m2[32];
+      // ---- pass 1: maximum of each of 32 column groups on the a_hi . c_hi scores ----
+      float m1[32];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) { m1[j] = -INFINITY; m2[j] = -INFINITY; }
+      for (int j = 0; j < 32; ++j) m1[j] = -INFINITY;
       for (int c = 0; c < chunks && ok; ++c, ++g) {
         uint32_t taddr;
         if (!acquire(g, taddr)) { ok = false; break; }
@@ -390,28 +390,21 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
           tmem_ld32(taddr + part * 32, v);
           if (part == kColsPerWG / 32 - 1) release(g);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float x = __uint_as_float(v[j]);
-            const float lo = fminf(m1[j], x);
-            m1[j] = fmaxf(m1[j], x);
-            m2[j] = fmaxf(m2[j], lo);
-          }
+          for (int j = 0; j < 32; ++j) m1[j] = fmaxf(m1[j], __uint_as_float(v[j]));
         }
       }
       if (!ok) { fail(); break; }
-      // KMAX-th largest kept value: a lower bound (up to the dropped lo terms)
-      // on this thread's -- hence the row's -- KMAX-th largest score.
+      // KMAX-th largest group maximum: KMAX distinct scores reach it, so (up
+      // to the dropped lo terms) it is a lower bound on this thread's -- hence
+      // the row's -- KMAX-th largest score.
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        kept[j * EPI + et] = m1[j];
-        kept[(32 + j) * EPI + et] = m2[j];
-      }
+      for (int j = 0; j < 32; ++j) kept[j * EPI + et] = m1[j];
       {
         float best[KMAX];
 #pragma unroll
         for (int t = 0; t < KMAX; ++t) best[t] = -INFINITY;
 #pragma unroll 1
-        for (int u = 0; u < 64; ++u) {
+        for (int u = 0; u < 32; ++u) {
           float c = kept[u * EPI + et];
 #pragma unroll
           for (int t = 0; t < KMAX; ++t) {
@@ -550,7 +543,7 @@ template <int DS>
 size_t smem_bytes(int kmax) {
   using G = Geo<DS>;
   const size_t shared = std::max<size_t>({static_cast<size_t>(kCand) * 32 * kEpiWarps * 8,
-                                          static_cast<size_t>(64) * 32 * kEpiWarps * 4,
+                                          static_cast<size_t>(32) * 32 * kEpiWarps * 4,
                                           static_cast<size_t>(kEpiWG - 1) * kM * kmax * 8});
   return 1024 + 2 * G::A_BYTES + kStages * G::B_BYTES + shared + kEpiWG * kM * 4 + (2 * kStages + 8) * 8 + 16;
 }
