@@ -107,6 +107,37 @@ __device__ __forceinline__ void sort_and_write(const uint64_t* src, int nsel, in
   }
 }
 
+// First index in [l, u) whose key exceeds pos (u if none); keys ascend.  Each
+// round trip to memory loads eight probes that cut the range into nine parts,
+// so a bucket of a few hundred keys takes two or three round trips instead of
+// the eight of a binary search.
+__device__ __forceinline__ int first_above(const int32_t* bk, int l, int u, int pos) {
+  while (u - l > 8) {
+    const int len = u - l;
+    int pr[8], v[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) pr[t] = l + ((t + 1) * len) / 9;   // strictly increasing in (l, u)
+#pragma unroll
+    for (int t = 0; t < 8; ++t) v[t] = bk[pr[t]];
+    // the probes <= pos form a prefix: the answer lies after the last of them
+    // and at or before the first probe above pos
+    int nl = l, nu = u;
+#pragma unroll
+    for (int t = 0; t < 8; ++t) nl = v[t] <= pos ? pr[t] + 1 : nl;
+#pragma unroll
+    for (int t = 7; t >= 0; --t) nu = v[t] > pos ? pr[t] : nu;
+    l = nl;
+    u = nu;
+  }
+  int v[8];
+#pragma unroll
+  for (int t = 0; t < 8; ++t) v[t] = l + t < u ? bk[l + t] : INT_MAX;
+  int c = 0;
+#pragma unroll
+  for (int t = 0; t < 8; ++t) c += v[t] <= pos ? 1 : 0;
+  return l + c;
+}
+
 template <typename T, int D, int CAP>
 __device__ __forceinline__ void rescore_mma_unit(const RescoreParams& p, int64_t unit, RsMmaSmem<CAP>& s,
                                                  int lane, int32_t* out_list, int32_t* out_count) {
@@ -129,14 +160,7 @@ __device__ __forceinline__ void rescore_mma_unit(const RescoreParams& p, int64_t
     const int32_t* ptr = p.bucket_ptr + static_cast<int64_t>(bh) * (p.n_codes + 1);
     const int lo = ptr[c];
     int hi = ptr[c + 1];
-    if (p.causal) {
-      int l = lo, u = hi;
-      while (l < u) {
-        const int mid = (l + u) >> 1;
-        if (bk[mid] <= pos) l = mid + 1; else u = mid;
-      }
-      hi = l;
-    }
+    if (p.causal) hi = first_above(bk, lo, hi, pos);
     s.qc[lane] = c;
     s.lo[lane] = lo;
     len = hi - lo;
