@@ -18,60 +18,112 @@
 namespace ssa {
 
 // ---------------------------------------------------------------------------
-// K0: routing projection + L2 normalisation.
-// One warp per output row; lane c owns route component c (d_s <= 64, two
-// components per lane above 32).  W^T sits in shared memory as fp32 so that
-// lane c reads W^T[e][c] (consecutive addresses, conflict-free) and the
-// input row x[e] is a shared-memory broadcast.
+// K0: routing projection + L2 normalisation, in tiles of 64 rows.
+//   1. all threads load the tile's rows with 16-byte loads and form the GQA
+//      group mean in fp32 (shared memory, [64][d]);
+//   2. warp w computes rows 8w..8w+7: lane c owns route component c (and
+//      c + 32 when d_s = 64); W^T[e][c] comes from shared memory
+//      (consecutive lanes, conflict-free) and x[row][e..e+3] is a broadcast
+//      128-bit read, so 12 shared loads feed 32 FMAs;
+//   3. each row is normalised by a warp reduction of its squares.
+// Per output the FMA chain runs over e in increasing order, as a plain dot
+// product would.
 // ---------------------------------------------------------------------------
+constexpr int kRpRows = 64;        // rows per tile
+constexpr int kRpThreads = 256;    // 8 warps x 8 rows
+
 template <typename T, typename TW>
-__global__ void __launch_bounds__(256) route_project_kernel(RouteProjectParams p) {
-  extern __shared__ float smem[];
+__global__ void __launch_bounds__(kRpThreads) route_project_kernel(RouteProjectParams p) {
+  extern __shared__ __align__(16) float smem[];
   const int d = p.d, d_s = p.d_s;
   float* wt = smem;                          // [d][d_s]
-  float* xs = smem + d * d_s;                // [warps][d]
+  float* xs = smem + d * d_s;                // [kRpRows][d]
   const TW* w = static_cast<const TW*>(p.w);
   for (int t = threadIdx.x; t < d * d_s; t += blockDim.x) {
     const int c = t / d, e = t % d;          // w is [d_s][d]
     wt[e * d_s + c] = Elem<TW>::to_f(w[t]);
   }
-  __syncthreads();
   const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
-  const int warps = blockDim.x / kWarp;
-  float* x = xs + warp * d;
   const T* src = static_cast<const T*>(p.x);
   const float inv_g = 1.0f / static_cast<float>(p.group);
-  for (int64_t row = static_cast<int64_t>(blockIdx.x) * warps + warp; row < p.rows;
-       row += static_cast<int64_t>(gridDim.x) * warps) {
-    // row = ((bat * h_kv + h) * n_rows + i)
-    const int64_t i = row % p.n_rows;
-    const int64_t bh = row / p.n_rows;
-    const int h = static_cast<int>(bh % p.h_kv);
-    const int64_t bat = bh / p.h_kv;
-    const T* base = src + bat * p.stride_b + i * p.stride_n +
-                    static_cast<int64_t>(h) * p.group * p.stride_h;
-    for (int e = lane; e < d; e += kWarp) {
-      float acc = 0.f;
-      for (int gg = 0; gg < p.group; ++gg) acc += Elem<T>::to_f(base[gg * p.stride_h + e]);
-      x[e] = p.group == 1 ? acc : acc * inv_g;
-    }
-    __syncwarp();
-    float r0 = 0.f, r1 = 0.f;
-    const int c0 = lane, c1 = lane + kWarp;
-    if (c0 < d_s) {
-      for (int e = 0; e < d; ++e) r0 = fmaf(wt[e * d_s + c0], x[e], r0);
-    }
-    if (c1 < d_s) {
-      for (int e = 0; e < d; ++e) r1 = fmaf(wt[e * d_s + c1], x[e], r1);
-    }
-    float ss = r0 * r0 + r1 * r1;
+  const int chunks = d / 8;
+  const bool has0 = lane < d_s, has1 = lane + kWarp < d_s;
+  for (int64_t tile0 = static_cast<int64_t>(blockIdx.x) * kRpRows; tile0 < p.rows;
+       tile0 += static_cast<int64_t>(gridDim.x) * kRpRows) {
+    __syncthreads();                         // W^T written; the previous tile's rows consumed
+    // ---- 1. group means of the tile's rows ----
+    for (int idx = threadIdx.x; idx < kRpRows * chunks; idx += kRpThreads) {
+      const int rl = idx / chunks, ch = idx % chunks;
+      const int64_t row = tile0 + rl;        // row = ((bat * h_kv + h) * n_rows + i)
+      float x[8];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float nrm = fmaxf(sqrtf(ss), 1e-12f);
-    float* out = p.out + row * d_s;
-    if (c0 < d_s) out[c0] = r0 / nrm;
-    if (c1 < d_s) out[c1] = r1 / nrm;
-    __syncwarp();
+      for (int u = 0; u < 8; ++u) x[u] = 0.f;
+      if (row < p.rows) {
+        const int64_t i = row % p.n_rows;
+        const int64_t bh = row / p.n_rows;
+        const int h = static_cast<int>(bh % p.h_kv);
+        const int64_t bat = bh / p.h_kv;
+        const T* base = src + bat * p.stride_b + i * p.stride_n + static_cast<int64_t>(h) * p.group * p.stride_h +
+                        ch * 8;
+        for (int gg = 0; gg < p.group; ++gg) {
+          float f[8];
+          load8<T>(base + gg * p.stride_h, f);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) x[u] += f[u];
+        }
+        if (p.group != 1) {
+#pragma unroll
+          for (int u = 0; u < 8; ++u) x[u] *= inv_g;
+        }
+      }
+      float4* dst = reinterpret_cast<float4*>(xs + rl * d + ch * 8);
+      dst[0] = make_float4(x[0], x[1], x[2], x[3]);
+      dst[1] = make_float4(x[4], x[5], x[6], x[7]);
+    }
+    __syncthreads();
+    // ---- 2. projection: rows r0..r0+7 of the tile ----
+    const int r0 = warp * 8;
+    float acc0[8], acc1[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) acc0[r] = acc1[r] = 0.f;
+    for (int e = 0; e < d; e += 4) {
+      float w0[4], w1[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        w0[u] = has0 ? wt[(e + u) * d_s + lane] : 0.f;
+        w1[u] = has1 ? wt[(e + u) * d_s + lane + kWarp] : 0.f;
+      }
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const float4 xv = *reinterpret_cast<const float4*>(xs + (r0 + r) * d + e);
+        acc0[r] = fmaf(w0[0], xv.x, acc0[r]);
+        acc0[r] = fmaf(w0[1], xv.y, acc0[r]);
+        acc0[r] = fmaf(w0[2], xv.z, acc0[r]);
+        acc0[r] = fmaf(w0[3], xv.w, acc0[r]);
+        if (has1) {
+          acc1[r] = fmaf(w1[0], xv.x, acc1[r]);
+          acc1[r] = fmaf(w1[1], xv.y, acc1[r]);
+          acc1[r] = fmaf(w1[2], xv.z, acc1[r]);
+          acc1[r] = fmaf(w1[3], xv.w, acc1[r]);
+        }
+      }
+    }
+    // ---- 3. normalise and store ----
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const float v0 = has0 ? acc0[r] : 0.f;
+      const float v1 = has1 ? acc1[r] : 0.f;
+      float ss = v0 * v0 + v1 * v1;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float nrm = fmaxf(sqrtf(ss), 1e-12f);
+      const int64_t row = tile0 + r0 + r;
+      if (row < p.rows) {
+        float* out = p.out + row * d_s;
+        if (has0) out[lane] = v0 / nrm;
+        if (has1) out[lane + kWarp] = v1 / nrm;
+      }
+    }
   }
 }
 
@@ -174,10 +226,13 @@ __global__ void select_from_scores_kernel(const float* scores, int64_t rows, int
 // ---------------------------------------------------------------------------
 cudaError_t launch_route_project(const RouteProjectParams& p, ssa_dtype xt, ssa_dtype wt,
                                  cudaStream_t st) {
-  const int threads = 256;
-  const size_t smem = (static_cast<size_t>(p.d) * p.d_s + (threads / kWarp) * p.d) * sizeof(float);
-  int64_t blocks = cdiv(p.rows, threads / kWarp);
-  blocks = blocks > 148 * 16 ? 148 * 16 : blocks;
+  const int threads = kRpThreads;
+  const size_t smem = (static_cast<size_t>(p.d) * p.d_s + static_cast<size_t>(kRpRows) * p.d) * sizeof(float);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int64_t blocks = cdiv(p.rows, kRpRows);
+  blocks = blocks > static_cast<int64_t>(sms) * 4 ? static_cast<int64_t>(sms) * 4 : blocks;
   if (blocks < 1) return cudaSuccess;
 #define SSA_RP(T, TW)                                                                       \
   do {                                                                                      \
