@@ -130,49 +130,53 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------
-# CPU baseline: the reference's algorithm (oracle port), bounded sample
+# CPU baseline: the reference's forward (torch-CPU port), bounded sample
 # ---------------------------------------------------------------------------
-def cpu_sample(t_cpu, shape, rows=256):
-    """Times one KV head of the reference algorithm on the host: key codes for
-    all n keys, then query codes, the dense O(n) re-score per query (the
-    reference's full [rows, g, n] logits + candidate mask + top-k) and stage 3
-    for the last ``rows`` query rows.  Returns (tokens/s estimate, seconds, text)."""
-    import numpy as np
-    from oracle import ssa_oracle as O
+def cpu_sample(t_cpu, shape, heads=1, rows=None):
+    """Times the reference forward on the host for ``heads`` KV heads: key
+    codes of all n keys, then the last ``rows`` query rows (all rows by
+    default): query codes, the dense re-score over all n keys with the
+    candidate mask and top-k, and the gathered attention.  Returns (tokens/s
+    for the whole step, extrapolated over the rows and the h_kv heads,
+    seconds, description)."""
+    import torch
+    from oracle import ssa_port_torch as P
 
     q, k, v, w_qr, w_kr, cb = t_cpu
     n, g = shape.n, shape.h_q // shape.h_kv
-    h = 0
+    rows = n if rows is None else min(rows, n)
     i0 = n - rows
-    qh = q[i0:, h * g:(h + 1) * g]
-    kh = k[:, h:h + 1]
-    vh = v[:, h:h + 1]
+    P.attention(q[:8, :g].contiguous(), k[:, 0].contiguous(), v[:, 0].contiguous(),
+                torch.zeros((8, 4), dtype=torch.int64))            # thread-pool warm-up
     t0 = time.perf_counter()
-    _, k_route = O.route_vectors(kh[:1].repeat(g, axis=1), kh, w_qr, w_kr, dtype=np.float32)
-    k_codes = O.stable_topk(O.code_scores(k_route, cb[h:h + 1], dtype=np.float32), shape.b)
-    t1 = time.perf_counter()
-    q_route, _ = O.route_vectors(qh, kh[:rows], w_qr, w_kr, dtype=np.float32)
-    q_codes = O.stable_topk(O.code_scores(q_route, cb[h:h + 1], dtype=np.float32), shape.a)
-    idx = O.select_topk_dense(qh, kh, q_codes, k_codes, shape.top_k, causal=True, dtype=np.float32,
-                              q_block=64, q_start=i0)
-    O.sparse_attention(qh, kh, vh, idx, causal=True, q_offset=i0, dtype=np.float32)
-    t2 = time.perf_counter()
-    per_head = (t1 - t0) + (t2 - t1) * (n / rows)
+    key_s = 0.0
+    for h in range(heads):
+        qh = q[i0:, h * g:(h + 1) * g].contiguous()
+        kh, vh = k[:, h].contiguous(), v[:, h].contiguous()
+        ta = time.perf_counter()
+        kc = P.key_codes(kh, w_kr, cb[h], shape.b)
+        key_s += time.perf_counter() - ta
+        qc = P.query_codes(qh, w_qr, cb[h], shape.a)
+        idx = P.select(qh, kh, qc, kc, shape.n_codes, shape.top_k, i0, True)
+        P.attention(qh, kh, vh, idx, i0, True)
+    elapsed = time.perf_counter() - t0
+    per_head = (key_s + (elapsed - key_s) * n / rows) / heads
     seconds = per_head * shape.h_kv
-    sample = (f"1 of {shape.h_kv} KV heads: key codes for all {n} keys + last {rows} queries "
-              f"(codes, dense re-score over {n} keys, top-{shape.top_k}, attention), fp32, "
-              f"extrapolated x{n // rows} rows x{shape.h_kv} heads")
-    return n / seconds, t2 - t0, sample
+    sample = (f"{heads} of {shape.h_kv} KV heads: key codes of all {n} keys + "
+              + (f"all {n} query rows" if rows == n else f"the last {rows} query rows")
+              + f" (query codes, dense re-score over {n} keys with candidate mask, top-{shape.top_k},"
+              f" gathered attention), fp32 torch CPU port of the reference forward, extrapolated to "
+              f"{shape.h_kv} heads" + ("" if rows == n else f" and {n} rows"))
+    return n / seconds, elapsed, sample
 
 
 def cpu_inputs(shape, seed):
-    import numpy as np
     import torch
     from ssa_b200 import workloads as W
 
     t = W.make_inputs(shape, seed=seed, dtype=torch.bfloat16, device="cpu")
-    f = lambda x: x[0].float().numpy() if x.dim() == 4 else x.float().numpy()
-    return f(t["q"]), f(t["k"]), f(t["v"]), t["w_qr"].numpy(), t["w_kr"].numpy(), t["codebook"].numpy()
+    f = lambda x: (x[0] if x.dim() == 4 else x).float().contiguous()
+    return f(t["q"]), f(t["k"]), f(t["v"]), t["w_qr"].float(), t["w_kr"].float(), t["codebook"].float()
 
 
 def run_reference(args):
@@ -189,7 +193,7 @@ def run_reference(args):
     t_cpu = cpu_inputs(shape, args.seed)
     vals, secs = [], []
     for it in range(args.warmup + args.steps):
-        v, s, sample = cpu_sample(t_cpu, shape, rows=256)
+        v, s, sample = cpu_sample(t_cpu, shape, heads=1, rows=max(1, shape.n // 4))
         if it >= args.warmup:
             vals.append(v)
             secs.append(s)
@@ -430,7 +434,7 @@ def run_ours(args):
     if rank == 0 and world == 1 and not args.no_cpu:
         cores = os.cpu_count() or 1
         torch.set_num_threads(cores)
-        cv, cs, sample = cpu_sample(cpu_inputs(shape, args.seed), shape, rows=min(4096, shape.n))
+        cv, cs, sample = cpu_sample(cpu_inputs(shape, args.seed), shape, heads=2)
         cpu = {"value": cv, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample,
                "sample_seconds": cs}
 

@@ -132,3 +132,40 @@ def test_zero_padding_when_k_exceeds_n():
     for h in range(h_kv):
         for i in range(n):
             assert sorted(idx[i, h, :n].tolist()) == list(range(n))
+
+
+def test_torch_port_matches_oracle_on_tie_free_rows():
+    """The torch-CPU port timed as the CPU baseline computes the oracle's
+    result wherever the selection is well defined (rows with at least k
+    candidates; random inputs have no ties)."""
+    import torch
+
+    from oracle import ssa_port_torch as P
+
+    rng = np.random.default_rng(21)
+    n, h_q, h_kv, d, d_s, n_c, a, b, kk = 300, 8, 2, 32, 8, 64, 4, 2, 24
+    g = h_q // h_kv
+    q = rng.standard_normal((n, h_q, d))
+    k = rng.standard_normal((n, h_kv, d))
+    v = rng.standard_normal((n, h_kv, d))
+    w_qr = rng.standard_normal((d_s, d)) / np.sqrt(d)
+    w_kr = rng.standard_normal((d_s, d)) / np.sqrt(d)
+    cb = rng.standard_normal((h_kv, n_c, d_s))
+    qc_o, kc_o = O.route_codes(q, k, w_qr, w_kr, cb, a, b)
+    idx_o = O.select_topk_dense(q, k, qc_o, kc_o, kk, causal=True)
+    out_o = O.sparse_attention(q, k, v, idx_o, causal=True)
+    counts = O.candidate_mask_dense(qc_o, kc_o)
+    T = lambda x: torch.from_numpy(np.ascontiguousarray(x))
+    for h in range(h_kv):
+        qh, kh, vh = T(q[:, h * g:(h + 1) * g]), T(k[:, h]), T(v[:, h])
+        kc = P.key_codes(kh, T(w_kr), T(cb[h]), b)
+        qc = P.query_codes(qh, T(w_qr), T(cb[h]), a)
+        np.testing.assert_array_equal(kc.numpy(), kc_o[:, h])
+        np.testing.assert_array_equal(qc.numpy(), qc_o[:, h])
+        idx = P.select(qh, kh, qc, kc, n_c, kk, 0, True, block=64).numpy()
+        causal_cands = (counts[:, h, :] & (np.arange(n)[None, :] <= np.arange(n)[:, None])).sum(axis=1)
+        full = causal_cands >= kk
+        assert full.sum() > 50
+        np.testing.assert_array_equal(idx[full], idx_o[full, h])
+        out = P.attention(qh, kh, vh, T(idx_o[:, h]), 0, True, block=100).numpy()
+        np.testing.assert_allclose(out, out_o[:, h * g:(h + 1) * g], rtol=1e-10, atol=1e-10)
