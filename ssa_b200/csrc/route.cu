@@ -32,7 +32,46 @@ namespace ssa {
 constexpr int kRpRows = 64;        // rows per tile
 constexpr int kRpThreads = 256;    // 8 warps x 8 rows
 
-template <typename T, typename TW>
+// 8 consecutive elements as raw 16-byte words (two for fp32), converted later
+// so that several loads can be in flight before the first is used.
+template <typename T> struct Raw8 { uint4 a; };
+template <> struct Raw8<float> { uint4 a, b; };
+template <typename T>
+__device__ __forceinline__ void raw8_load(const T* p, Raw8<T>& r) { r.a = __ldg(reinterpret_cast<const uint4*>(p)); }
+template <>
+__device__ __forceinline__ void raw8_load<float>(const float* p, Raw8<float>& r) {
+  r.a = __ldg(reinterpret_cast<const uint4*>(p));
+  r.b = __ldg(reinterpret_cast<const uint4*>(p) + 1);
+}
+template <typename T>
+__device__ __forceinline__ void raw8_zero(Raw8<T>& r) { r.a = make_uint4(0u, 0u, 0u, 0u); }
+template <>
+__device__ __forceinline__ void raw8_zero<float>(Raw8<float>& r) { r.a = r.b = make_uint4(0u, 0u, 0u, 0u); }
+__device__ __forceinline__ void raw8_add(const Raw8<float>& r, float (&x)[8]) {
+  x[0] += __uint_as_float(r.a.x); x[1] += __uint_as_float(r.a.y);
+  x[2] += __uint_as_float(r.a.z); x[3] += __uint_as_float(r.a.w);
+  x[4] += __uint_as_float(r.b.x); x[5] += __uint_as_float(r.b.y);
+  x[6] += __uint_as_float(r.b.z); x[7] += __uint_as_float(r.b.w);
+}
+__device__ __forceinline__ void raw8_add(const Raw8<__nv_bfloat16>& r, float (&x)[8]) {
+  const uint32_t w[4] = {r.a.x, r.a.y, r.a.z, r.a.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    x[2 * i] += __uint_as_float(w[i] << 16);
+    x[2 * i + 1] += __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+__device__ __forceinline__ void raw8_add(const Raw8<__half>& r, float (&x)[8]) {
+  const uint32_t w[4] = {r.a.x, r.a.y, r.a.z, r.a.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+    x[2 * i] += t.x;
+    x[2 * i + 1] += t.y;
+  }
+}
+
+template <typename T, typename TW, bool TWO>
 __global__ void __launch_bounds__(kRpThreads) route_project_kernel(RouteProjectParams p) {
   extern __shared__ __align__(16) float smem[];
   const int d = p.d, d_s = p.d_s;
@@ -40,45 +79,69 @@ __global__ void __launch_bounds__(kRpThreads) route_project_kernel(RouteProjectP
   float* xs = smem + d * d_s;                // [kRpRows][d]
   const TW* w = static_cast<const TW*>(p.w);
   for (int t = threadIdx.x; t < d * d_s; t += blockDim.x) {
-    const int c = t / d, e = t % d;          // w is [d_s][d]
-    wt[e * d_s + c] = Elem<TW>::to_f(w[t]);
+    const int e = t / d_s, c = t % d_s;      // w is [d_s][d]; consecutive t -> consecutive banks
+    wt[t] = Elem<TW>::to_f(w[c * d + e]);
   }
   const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
   const T* src = static_cast<const T*>(p.x);
   const float inv_g = 1.0f / static_cast<float>(p.group);
   const int chunks = d / 8;
-  const bool has0 = lane < d_s, has1 = lane + kWarp < d_s;
+  const int items = kRpRows * chunks;
+  const bool has0 = lane < d_s;
   for (int64_t tile0 = static_cast<int64_t>(blockIdx.x) * kRpRows; tile0 < p.rows;
        tile0 += static_cast<int64_t>(gridDim.x) * kRpRows) {
     __syncthreads();                         // W^T written; the previous tile's rows consumed
-    // ---- 1. group means of the tile's rows ----
-    for (int idx = threadIdx.x; idx < kRpRows * chunks; idx += kRpThreads) {
-      const int rl = idx / chunks, ch = idx % chunks;
-      const int64_t row = tile0 + rl;        // row = ((bat * h_kv + h) * n_rows + i)
-      float x[8];
+    // ---- 1. group means of the tile's rows: a thread takes two 8-element
+    // items at a time and issues up to four heads' loads of both together ----
+    for (int idx0 = threadIdx.x; idx0 < items; idx0 += 2 * kRpThreads) {
+      const T* base[2];
+      bool ok[2];
+      float x[2][8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) x[u] = 0.f;
-      if (row < p.rows) {
+      for (int q = 0; q < 2; ++q) {
+        const int idx = idx0 + q * kRpThreads;
+        const int rl = idx / chunks, ch = idx % chunks;
+        const int64_t row = tile0 + rl;      // row = ((bat * h_kv + h) * n_rows + i)
+        ok[q] = idx < items && row < p.rows;
         const int64_t i = row % p.n_rows;
         const int64_t bh = row / p.n_rows;
         const int h = static_cast<int>(bh % p.h_kv);
         const int64_t bat = bh / p.h_kv;
-        const T* base = src + bat * p.stride_b + i * p.stride_n + static_cast<int64_t>(h) * p.group * p.stride_h +
-                        ch * 8;
-        for (int gg = 0; gg < p.group; ++gg) {
-          float f[8];
-          load8<T>(base + gg * p.stride_h, f);
+        base[q] = src + (ok[q] ? bat * p.stride_b + i * p.stride_n + static_cast<int64_t>(h) * p.group * p.stride_h +
+                                     ch * 8
+                               : 0);
 #pragma unroll
-          for (int u = 0; u < 8; ++u) x[u] += f[u];
-        }
-        if (p.group != 1) {
+        for (int u = 0; u < 8; ++u) x[q][u] = 0.f;
+      }
+      for (int g0 = 0; g0 < p.group; g0 += 4) {
+        Raw8<T> r[2][4];
 #pragma unroll
-          for (int u = 0; u < 8; ++u) x[u] *= inv_g;
+        for (int t = 0; t < 4; ++t)
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            if (ok[q] && g0 + t < p.group) raw8_load<T>(base[q] + (g0 + t) * p.stride_h, r[q][t]);
+            else raw8_zero<T>(r[q][t]);
+          }
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+#pragma unroll
+          for (int q = 0; q < 2; ++q)
+            if (g0 + t < p.group) raw8_add(r[q][t], x[q]);
+      }
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int idx = idx0 + q * kRpThreads;
+        if (idx < items) {
+          if (p.group != 1) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) x[q][u] *= inv_g;
+          }
+          const int rl = idx / chunks, ch = idx % chunks;
+          float4* dst = reinterpret_cast<float4*>(xs + rl * d + ch * 8);
+          dst[0] = make_float4(x[q][0], x[q][1], x[q][2], x[q][3]);
+          dst[1] = make_float4(x[q][4], x[q][5], x[q][6], x[q][7]);
         }
       }
-      float4* dst = reinterpret_cast<float4*>(xs + rl * d + ch * 8);
-      dst[0] = make_float4(x[0], x[1], x[2], x[3]);
-      dst[1] = make_float4(x[4], x[5], x[6], x[7]);
     }
     __syncthreads();
     // ---- 2. projection: rows r0..r0+7 of the tile ----
@@ -91,7 +154,7 @@ __global__ void __launch_bounds__(kRpThreads) route_project_kernel(RouteProjectP
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         w0[u] = has0 ? wt[(e + u) * d_s + lane] : 0.f;
-        w1[u] = has1 ? wt[(e + u) * d_s + lane + kWarp] : 0.f;
+        if (TWO) w1[u] = wt[(e + u) * d_s + lane + kWarp];
       }
 #pragma unroll
       for (int r = 0; r < 8; ++r) {
@@ -100,7 +163,7 @@ __global__ void __launch_bounds__(kRpThreads) route_project_kernel(RouteProjectP
         acc0[r] = fmaf(w0[1], xv.y, acc0[r]);
         acc0[r] = fmaf(w0[2], xv.z, acc0[r]);
         acc0[r] = fmaf(w0[3], xv.w, acc0[r]);
-        if (has1) {
+        if (TWO) {
           acc1[r] = fmaf(w1[0], xv.x, acc1[r]);
           acc1[r] = fmaf(w1[1], xv.y, acc1[r]);
           acc1[r] = fmaf(w1[2], xv.z, acc1[r]);
@@ -112,7 +175,7 @@ __global__ void __launch_bounds__(kRpThreads) route_project_kernel(RouteProjectP
 #pragma unroll
     for (int r = 0; r < 8; ++r) {
       const float v0 = has0 ? acc0[r] : 0.f;
-      const float v1 = has1 ? acc1[r] : 0.f;
+      const float v1 = TWO ? acc1[r] : 0.f;
       float ss = v0 * v0 + v1 * v1;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
@@ -121,7 +184,7 @@ __global__ void __launch_bounds__(kRpThreads) route_project_kernel(RouteProjectP
       if (row < p.rows) {
         float* out = p.out + row * d_s;
         if (has0) out[lane] = v0 / nrm;
-        if (has1) out[lane + kWarp] = v1 / nrm;
+        if (TWO) out[lane + kWarp] = v1 / nrm;
       }
     }
   }
@@ -236,7 +299,7 @@ cudaError_t launch_route_project(const RouteProjectParams& p, ssa_dtype xt, ssa_
   if (blocks < 1) return cudaSuccess;
 #define SSA_RP(T, TW)                                                                       \
   do {                                                                                      \
-    auto kern = route_project_kernel<T, TW>;                                                \
+    auto kern = p.d_s > kWarp ? route_project_kernel<T, TW, true> : route_project_kernel<T, TW, false>; \
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);     \
     kern<<<(unsigned)blocks, threads, smem, st>>>(p);                                       \
   } while (0)
