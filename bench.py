@@ -67,6 +67,9 @@ def parse():
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
+    p.add_argument("--workload", default="config3", choices=["config3", "config4"],
+                   help="config3: one sequence per GPU (the headline); config4: one n=131072 "
+                        "sequence split by queries over the GPUs (strong scaling)")
     return p.parse_args()
 
 
@@ -456,10 +459,94 @@ def run_ours(args):
     return 0
 
 
+def run_config4(args):
+    """Config 4: one long sequence (n = 131072, N_c = 8192, k = 512, bf16,
+    N(0,1) inputs) split by queries over the ranks (ssa_b200.shard: zig-zag
+    blocks, all-gather of K, V and key codes, routing with the gathered codes,
+    attention).  Total work is fixed: strong scaling."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import ssa_b200 as ssa
+    from ssa_b200 import shard
+    from ssa_b200 import workloads as W
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world == 1 and "MASTER_ADDR" not in os.environ:
+        import socket
+        with socket.socket() as so:
+            so.bind(("127.0.0.1", 0))
+            port = so.getsockname()[1]
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK="0", WORLD_SIZE="1")
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+    n = args.n if args.n != 32768 else W.CONFIG4.n
+    shape = W.Shape(**{**W.CONFIG4.asdict(), "n": n})
+    t = W.make_inputs(shape, seed=args.seed, dtype=torch.bfloat16, device=dev, planted=False,
+                      generate_on_device=True)
+    router = ssa.CodebookRouter(head_dim=shape.d, route_dim=shape.d_s, num_kv_heads=shape.h_kv,
+                                num_codebook=shape.n_codes, codes_per_key=shape.b, codes_per_query=shape.a,
+                                top_k=shape.top_k).to(dev)
+    with torch.no_grad():
+        router.W_qr.weight.copy_(t["w_qr"])
+        router.W_kr.weight.copy_(t["w_kr"])
+        router.codebook.copy_(t["codebook"])
+    ql, kl, vl = (shard.local_rows(t[x], world, rank) for x in ("q", "k", "v"))
+    del t
+    torch.cuda.empty_cache()
+    os.environ.setdefault("SSA_CHECKED", "0")
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        with torch.no_grad():
+            return shard.sharded_forward(router, ql, kl, vl, causal=True)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(local)
+    clocks.start()
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    clk = clocks.stop()
+    tt = torch.tensor([e0.elapsed_time(e1)], device=dev)
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    ms_step = float(tt.item()) / args.steps
+    if rank == 0:
+        line = {"metric": "SSA fwd tokens/s, one n=131072 sequence split over the GPUs (k=512, bf16)",
+                "value": n / (ms_step / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (seeded on device: Q/K/V ~ N(0,1))",
+                "config": {"workload": "config4 (long single sequence, query-split)", **shape.asdict(),
+                           "parallelism": f"query-split x{world} (zig-zag blocks, NCCL all-gather of K, V, codes)",
+                           "l2": "inputs 1.6 GB > 126 MB L2, no flush"},
+                "roofline": None, "cpu_baseline": None, "e2e": None, "clocks": clk}
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "config4":
+        return run_config4(args)
     return run_ours(args)
 
 

@@ -42,14 +42,20 @@ CONFIG3 = Shape(n=32768, h_q=32, h_kv=8, d=128, d_s=32, n_codes=4096, a=16, b=4,
 CONFIG4 = Shape(n=131072, h_q=32, h_kv=8, d=128, d_s=32, n_codes=8192, a=16, b=4, top_k=512)
 
 
-def make_inputs(shape: Shape, seed: int = 0, dtype=torch.bfloat16, device="cuda", planted: bool = True):
+def make_inputs(shape: Shape, seed: int = 0, dtype=torch.bfloat16, device="cuda", planted: bool = True,
+                generate_on_device: bool = False):
     """Returns dict(q [B,n,h_q,d], k, v [B,n,h_kv,d], w_qr, w_kr [d_s,d] fp32,
-    codebook [h_kv,N_c,d_s] fp32) generated on ``device`` from ``seed``."""
-    g = torch.Generator(device="cpu").manual_seed(seed)
+    codebook [h_kv,N_c,d_s] fp32) from ``seed``, on ``device``.
+
+    ``generate_on_device`` draws the numbers on ``device`` itself (fast for
+    long sequences; the same seed gives the same values on every GPU) instead
+    of on the host; the two give different numbers."""
+    gen_dev = device if generate_on_device else "cpu"
+    g = torch.Generator(device=gen_dev).manual_seed(seed)
     B, n = shape.batch, shape.n
 
     def randn(*s):
-        return torch.randn(*s, generator=g, dtype=torch.float32)
+        return torch.randn(*s, generator=g, dtype=torch.float32, device=gen_dev)
 
     q = randn(B, n, shape.h_q, shape.d)
     k = randn(B, n, shape.h_kv, shape.d)
@@ -59,12 +65,12 @@ def make_inputs(shape: Shape, seed: int = 0, dtype=torch.bfloat16, device="cuda"
         cent = randn(64, shape.d)
         for bi in range(B):
             for h in range(shape.h_kv):
-                rows = torch.randperm(n, generator=g)[:n_planted]
-                which = torch.randint(0, 64, (n_planted,), generator=g)
+                rows = torch.randperm(n, generator=g, device=gen_dev)[:n_planted]
+                which = torch.randint(0, 64, (n_planted,), generator=g, device=gen_dev)
                 k[bi, rows, h] = cent[which] + 0.1 * randn(n_planted, shape.d)
     bound = (6.0 / (shape.d + shape.d_s)) ** 0.5
-    w_qr = (torch.rand(shape.d_s, shape.d, generator=g) * 2 - 1) * bound
-    w_kr = (torch.rand(shape.d_s, shape.d, generator=g) * 2 - 1) * bound
+    w_qr = (torch.rand(shape.d_s, shape.d, generator=g, device=gen_dev) * 2 - 1) * bound
+    w_kr = (torch.rand(shape.d_s, shape.d, generator=g, device=gen_dev) * 2 - 1) * bound
     cb = randn(shape.h_kv, shape.n_codes, shape.d_s) / shape.d_s ** 0.5
     out = dict(q=q.to(dtype), k=k.to(dtype), v=v.to(dtype), w_qr=w_qr, w_kr=w_kr, codebook=cb)
     return {kk: t.to(device) for kk, t in out.items()}
