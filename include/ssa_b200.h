@@ -56,6 +56,9 @@ typedef enum {
 #define SSA_DEVICE_BAD_CODE 0x2    /* a caller-given code outside [0, n_codes) was
                                       read as code 0; the index and the indices are
                                       undefined                                     */
+#define SSA_DEVICE_BAD_INDEX 0x4   /* a caller-given code->key index failed its check
+                                      (a bucket or a key out of range); the indices
+                                      are written as zeros                          */
 #define SSA_DEVICE_TIMEOUT 0x100   /* route: a pipeline wait gave up (~1 s); the
                                       affected codes are undefined                  */
 
@@ -129,6 +132,19 @@ ssa_status ssa_code_assign(const SsaRouteArgs* args, void* workspace, size_t wor
  * inline (ssa/router.py:114-130); the split is this library's. */
 ssa_status ssa_route_with_key_codes(const SsaRouteArgs* args, void* workspace,
                                    size_t workspace_bytes, void* stream);
+
+/* ssa_route_with_key_codes with the code->key index given as well:
+ * bucket_ptr [B, h_kv, n_codes+1] and bucket_keys [B, h_kv, n*b] as
+ * ssa_build_index writes them from args->k_codes.  For a GPU that routes
+ * several query blocks of one sequence against the same keys: the index is
+ * built once.  The index is checked on the device first (bucket bounds
+ * non-decreasing within [0, n*b], keys in [0, n)); if the check fails,
+ * SSA_DEVICE_BAD_INDEX is set and every index row is written as zeros.  No
+ * reference counterpart of its own
+ * (ssa/router.py:151-259 computes the candidate mask inline). */
+ssa_status ssa_route_with_index(const SsaRouteArgs* args, const int32_t* bucket_ptr,
+                                const int32_t* bucket_keys, void* workspace, size_t workspace_bytes,
+                                void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Sparse exact attention (stage 3)                                          */

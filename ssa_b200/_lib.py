@@ -18,6 +18,7 @@ SSA_F32, SSA_BF16, SSA_F16 = 0, 1, 2
 SSA_I32, SSA_I64 = 0, 1
 SSA_DEVICE_INDEX_OOB = 0x1
 SSA_DEVICE_BAD_CODE = 0x2
+SSA_DEVICE_BAD_INDEX = 0x4
 SSA_DEVICE_TIMEOUT = 0x100
 STATUS_NAMES = {0: "SSA_OK", 1: "SSA_ERR_INVALID_ARG", 2: "SSA_ERR_UNSUPPORTED", 3: "SSA_ERR_WORKSPACE",
                 4: "SSA_ERR_ALIGNMENT", 5: "SSA_ERR_CUDA", 6: "SSA_ERR_DEVICE"}
@@ -69,6 +70,7 @@ SIGNATURES = {
     "ssa_build_index_noalloc": (ctypes.c_int, [ctypes.POINTER(SsaRouteArgs), _vp, _vp, _vp, _vp]),
     "ssa_select_candidates": (ctypes.c_int, [ctypes.POINTER(SsaRouteArgs), _vp, ctypes.c_size_t, _vp]),
     "ssa_route_with_key_codes": (ctypes.c_int, [ctypes.POINTER(SsaRouteArgs), _vp, ctypes.c_size_t, _vp]),
+    "ssa_route_with_index": (ctypes.c_int, [ctypes.POINTER(SsaRouteArgs), _vp, _vp, _vp, ctypes.c_size_t, _vp]),
     "ssa_status_str": (ctypes.c_char_p, [ctypes.c_int]),
     "ssa_last_error": (ctypes.c_char_p, []),
 }

@@ -51,7 +51,7 @@ int rescore_cap(int k_eff) {
 // Workspace regions for a route call.
 struct RouteLayout {
   size_t q_route, k_route, cb_norm, cb_image, q_codes, k_codes, counts, partials, bucket_ptr,
-      bucket_keys, ovf, ovf2;
+      bucket_keys, ovf, ovf2, flags;
   size_t total;
   int tiles;
   int64_t chunks;
@@ -79,6 +79,7 @@ RouteLayout route_layout(const SsaRouteArgs& a) {
   L.bucket_keys = take(static_cast<size_t>(B * hk) * a.n * a.b * 4);
   L.ovf = take((1 + static_cast<size_t>(B * hk) * a.n_q) * 4);   // overflow count + unit list
   L.ovf2 = take((1 + static_cast<size_t>(B * hk) * a.n_q) * 4);  // second-tier count + list
+  L.flags = take(4);                                               // index-validation flag
   L.total = off;
   return L;
 }
@@ -216,20 +217,19 @@ ssa::IndexParams index_params(const SsaRouteArgs& a, const RouteLayout& L, void*
   return ip;
 }
 
-ssa_status run_stage2(const SsaRouteArgs& a, const RouteLayout& L, void* ws, cudaStream_t st,
-                      const int32_t* q_codes, const int32_t* k_codes) {
+// Candidate union, re-score and top-k over a built code->key index.
+ssa_status run_rescore(const SsaRouteArgs& a, const RouteLayout& L, void* ws, cudaStream_t st,
+                       const int32_t* q_codes, const int32_t* k_codes, const int32_t* bucket_ptr,
+                       const int32_t* bucket_keys, const int32_t* index_bad) {
   using namespace ssa;
-  IndexParams ip = index_params(a, L, ws, k_codes, at<int32_t>(ws, L.bucket_ptr),
-                                at<int32_t>(ws, L.bucket_keys));
-  cudaError_t e = launch_build_index(ip, st);
-  if (e != cudaSuccess) return cuda_status(e, "build_index");
   RescoreParams rp{};
   rp.q = a.q; rp.q_sb = a.q_stride_b; rp.q_sn = a.q_stride_n; rp.q_sh = a.q_stride_h;
   rp.k = a.k; rp.k_sb = a.k_stride_b; rp.k_sn = a.k_stride_n; rp.k_sh = a.k_stride_h;
   rp.q_codes = q_codes;
   rp.k_codes = k_codes;
-  rp.bucket_ptr = ip.bucket_ptr;
-  rp.bucket_keys = ip.bucket_keys;
+  rp.bucket_ptr = bucket_ptr;
+  rp.bucket_keys = bucket_keys;
+  rp.index_bad = index_bad;
   rp.out = a.indices;
   rp.index_i64 = a.index_dtype == SSA_I64;
   rp.cand_counts = a.cand_counts;
@@ -242,8 +242,16 @@ ssa_status run_stage2(const SsaRouteArgs& a, const RouteLayout& L, void* ws, cud
   rp.ovf_list = at<int32_t>(ws, L.ovf) + 1;
   rp.ovf2_count = at<int32_t>(ws, L.ovf2);
   rp.ovf2_list = at<int32_t>(ws, L.ovf2) + 1;
-  e = launch_rescore(rp, a.dtype, st);
-  return cuda_status(e, "rescore_topk");
+  return cuda_status(launch_rescore(rp, a.dtype, st), "rescore_topk");
+}
+
+ssa_status run_stage2(const SsaRouteArgs& a, const RouteLayout& L, void* ws, cudaStream_t st,
+                      const int32_t* q_codes, const int32_t* k_codes) {
+  ssa::IndexParams ip = index_params(a, L, ws, k_codes, at<int32_t>(ws, L.bucket_ptr),
+                                     at<int32_t>(ws, L.bucket_keys));
+  cudaError_t e = ssa::launch_build_index(ip, st);
+  if (e != cudaSuccess) return cuda_status(e, "build_index");
+  return run_rescore(a, L, ws, st, q_codes, k_codes, ip.bucket_ptr, ip.bucket_keys, nullptr);
 }
 
 // ---------------------------------------------------------------------------
@@ -334,6 +342,28 @@ ssa_status ssa_route_with_key_codes(const SsaRouteArgs* args, void* workspace, s
   s = run_stage1(*args, L, workspace, st, false, true, qc, nullptr);
   if (s != SSA_OK) return s;
   return run_stage2(*args, L, workspace, st, qc, args->k_codes);
+}
+
+ssa_status ssa_route_with_index(const SsaRouteArgs* args, const int32_t* bucket_ptr, const int32_t* bucket_keys,
+                                void* workspace, size_t workspace_bytes, void* stream) {
+  ssa_status s = check_route(args, true, true);
+  if (s != SSA_OK) return s;
+  if (!args->k_codes || !bucket_ptr || !bucket_keys)
+    return fail(SSA_ERR_INVALID_ARG, "k_codes, bucket_ptr and bucket_keys are inputs here and must be set");
+  const RouteLayout L = route_layout(*args);
+  if (!workspace || workspace_bytes < L.total)
+    return fail(SSA_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", L.total, workspace_bytes);
+  if (args->batch == 0 || args->n_q == 0) return SSA_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int32_t* qc = args->q_codes ? args->q_codes : at<int32_t>(workspace, L.q_codes);
+  // the index comes from the caller: check it once, before any kernel trusts it
+  int32_t* bad = at<int32_t>(workspace, L.flags);
+  cudaError_t e = ssa::launch_validate_index(bucket_ptr, bucket_keys, static_cast<int64_t>(args->batch) * args->h_kv,
+                                             args->n_codes, args->n, args->b, bad, args->status, st);
+  if (e != cudaSuccess) return cuda_status(e, "validate_index");
+  s = run_stage1(*args, L, workspace, st, false, true, qc, nullptr);
+  if (s != SSA_OK) return s;
+  return run_rescore(*args, L, workspace, st, qc, args->k_codes, bucket_ptr, bucket_keys, bad);
 }
 
 ssa_status ssa_code_assign(const SsaRouteArgs* args, void* workspace, size_t workspace_bytes,

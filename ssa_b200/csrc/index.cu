@@ -206,6 +206,33 @@ __global__ void __launch_bounds__(kIndexThreads) index_scatter_kernel(IndexParam
   }
 }
 
+__global__ void validate_index_kernel(const int32_t* ptr, const int32_t* keys, int64_t batch_heads, int n_codes,
+                                      int n, int b, int32_t* bad, int32_t* status) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int entries = n * b;
+  bool ok = true;
+  for (int64_t t = t0; t < batch_heads * (n_codes + 1); t += stride) {
+    const int c = static_cast<int>(t % (n_codes + 1));
+    const int v = ptr[t];
+    ok &= v >= 0 && v <= entries;
+    if (c > 0) ok &= ptr[t - 1] <= v;
+  }
+  for (int64_t t = t0; t < batch_heads * entries; t += stride) ok &= static_cast<unsigned>(keys[t]) < static_cast<unsigned>(n);
+  if (!ok) {
+    atomicOr(bad, 1);
+    set_status(status, SSA_DEVICE_BAD_INDEX);
+  }
+}
+
+cudaError_t launch_validate_index(const int32_t* bucket_ptr, const int32_t* bucket_keys, int64_t batch_heads,
+                                  int n_codes, int n, int b, int32_t* bad, int32_t* status, cudaStream_t st) {
+  cudaError_t e = cudaMemsetAsync(bad, 0, sizeof(int32_t), st);
+  if (e != cudaSuccess) return e;
+  validate_index_kernel<<<592, 256, 0, st>>>(bucket_ptr, bucket_keys, batch_heads, n_codes, n, b, bad, status);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_build_index(const IndexParams& p, cudaStream_t st) {
   const int bhs = p.batch * p.h_kv;
   if (bhs == 0 || p.n == 0) return cudaSuccess;

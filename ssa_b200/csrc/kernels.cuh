@@ -57,6 +57,11 @@ constexpr int kScanChunk = 4096;
 
 inline int index_tile_keys(int b) { return kIndexSortEntries / b; }
 
+// Checks a caller-given code->key index (bucket bounds non-decreasing within
+// [0, n*b], keys in [0, n)); any violation sets *bad and SSA_DEVICE_BAD_INDEX.
+cudaError_t launch_validate_index(const int32_t* bucket_ptr, const int32_t* bucket_keys, int64_t batch_heads,
+                                  int n_codes, int n, int b, int32_t* bad, int32_t* status, cudaStream_t st);
+
 // K3: candidate union + causal filter + re-score + top-k + filler.
 struct RescoreParams {
   const void* q; int64_t q_sb, q_sn, q_sh;
@@ -68,6 +73,7 @@ struct RescoreParams {
   void* out; int index_i64;    // [B, n_q, h_kv, top_k]
   int32_t* cand_counts;        // optional [B, n_q, h_kv]
   int32_t* status;             // optional device word (SSA_DEVICE_BAD_CODE)
+  const int32_t* index_bad;    // optional: non-zero when a caller-given index failed validation
   int batch, n, n_q, q_offset, h_kv, group, d, a, b, n_codes, top_k, causal;
   int cap;                     // shared-memory candidate capacity (power of two)
   int32_t* ovf_count;          // workspace: units left to the general path ...
@@ -75,6 +81,22 @@ struct RescoreParams {
   int32_t* ovf2_count;         // workspace: units passed from the first warp tier ...
   int32_t* ovf2_list;          // ... to the second [B * n_q * h_kv]
 };
+
+// A caller-given code->key index that failed validation: the unit's indices
+// are written as zeros (and its candidate count as 0) instead of being
+// computed from the index.  Threads tid = 0 .. nthreads-1 of the unit call
+// this with the same result.
+__device__ __forceinline__ bool rescore_skip_bad_index(const RescoreParams& p, int bat, int i, int h, int tid,
+                                                      int nthreads) {
+  if (!p.index_bad || *p.index_bad == 0) return false;
+  const int64_t row = (static_cast<int64_t>(bat) * p.n_q + i) * p.h_kv + h;
+  for (int e = tid; e < p.top_k; e += nthreads) {
+    if (p.index_i64) static_cast<int64_t*>(p.out)[row * p.top_k + e] = 0;
+    else static_cast<int32_t*>(p.out)[row * p.top_k + e] = 0;
+  }
+  if (p.cand_counts && tid == 0) p.cand_counts[row] = 0;
+  return true;
+}
 
 // K4: sparse exact attention.
 struct AttnParams {

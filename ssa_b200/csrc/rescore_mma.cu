@@ -146,6 +146,7 @@ __device__ __forceinline__ void rescore_mma_unit(const RescoreParams& p, int64_t
   const int bh = static_cast<int>(unit / p.n_q);
   const int i = p.n_q - 1 - static_cast<int>(unit % p.n_q);
   const int bat = bh / p.h_kv, h = bh % p.h_kv;
+  if (rescore_skip_bad_index(p, bat, i, h, lane, kWarp)) return;
   const int pos = p.q_offset + i;
   const int a = p.a;
   const int k_eff = min(p.top_k, p.n);

@@ -190,6 +190,57 @@ def _route_with_key_codes_fake(q, k, k_codes, w_qr, w_kr, codebook, a, top_k, ca
     return q.new_empty((B, n_q, h_kv, top_k), dtype=torch.int64 if index_i64 else torch.int32)
 
 
+@torch.library.custom_op("ssa_b200::route_with_index", mutates_args=())
+def route_with_index(q: torch.Tensor, k: torch.Tensor, k_codes: torch.Tensor, bucket_ptr: torch.Tensor,
+                     bucket_keys: torch.Tensor, w_qr: torch.Tensor, w_kr: torch.Tensor, codebook: torch.Tensor,
+                     a: int, top_k: int, causal: bool, temperature: float, q_offset: int,
+                     index_i64: bool) -> torch.Tensor:
+    """:func:`route_with_key_codes` with the code->key index of ``k_codes``
+    given too (``bucket_ptr``, ``bucket_keys`` from :func:`build_index`), so
+    that several query blocks of one sequence share one index build."""
+    dev = _require_cuda(q, k, k_codes, bucket_ptr, bucket_keys, w_qr, w_kr, codebook)
+    q, k = _last_contig(q), _last_contig(k)
+    kc = k_codes.to(torch.int32).contiguous()
+    ptr = bucket_ptr.to(torch.int32).contiguous()
+    keys = bucket_keys.to(torch.int32).contiguous()
+    w_qr, w_kr, codebook = _prep_weights(w_qr, w_kr, codebook, k.dtype)
+    B, n_q, _, _ = q.shape
+    _, n, h_kv, _ = k.shape
+    if tuple(kc.shape[:3]) != (B, n, h_kv):
+        raise ValueError(f"k_codes shape {tuple(kc.shape)} does not match k {tuple(k.shape)}")
+    n_codes = codebook.shape[-2]
+    if ptr.numel() != B * h_kv * (n_codes + 1) or keys.numel() != B * h_kv * n * kc.shape[-1]:
+        raise ValueError("bucket_ptr / bucket_keys do not match k_codes and the codebook")
+    indices = torch.empty((B, n_q, h_kv, top_k), dtype=torch.int64 if index_i64 else torch.int32,
+                          device=dev)
+    args = route_args(q, k, w_qr, w_kr, codebook, a, kc.shape[-1], top_k, causal, temperature,
+                      q_offset, indices, index_i64, None, kc, None)
+    check = _checked() and not torch.cuda.is_current_stream_capturing()
+    status = torch.zeros(1, dtype=torch.int32, device=dev) if check else None
+    args.status = _ptr(status)
+    ws = workspace(args, dev)
+    with torch.cuda.device(dev):
+        L.check("ssa_route_with_index",
+                L.lib().ssa_route_with_index(ctypes.byref(args), ptr.data_ptr(), keys.data_ptr(), ws.data_ptr(),
+                                             ws.numel(), _stream(dev)))
+    if status is not None:
+        bits = int(status.item())
+        if bits & L.SSA_DEVICE_BAD_INDEX:
+            raise ValueError("ssa_route_with_index: the code->key index failed its check")
+        if bits & L.SSA_DEVICE_BAD_CODE:
+            raise ValueError(f"ssa_route_with_index: a code is outside [0, {n_codes})")
+        if bits & L.SSA_DEVICE_TIMEOUT:
+            raise RuntimeError("ssa_route_with_index: a device pipeline wait timed out")
+    return indices
+
+
+@route_with_index.register_fake
+def _route_with_index_fake(q, k, k_codes, bucket_ptr, bucket_keys, w_qr, w_kr, codebook, a, top_k, causal,
+                           temperature, q_offset, index_i64):
+    B, n_q, _, _ = q.shape
+    return q.new_empty((B, n_q, k.shape[2], top_k), dtype=torch.int64 if index_i64 else torch.int32)
+
+
 # ---------------------------------------------------------------------------
 # code_assign
 # ---------------------------------------------------------------------------

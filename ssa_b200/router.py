@@ -95,6 +95,25 @@ class CodebookRouter(nn.Module):
                                             self.top_k, bool(causal), float(self.temperature),
                                             int(q_offset), index_dtype == torch.int64)
 
+    def key_index(self, k_codes: torch.Tensor):
+        """The code->key inverted index of ``k_codes [B, n, h_kv, b]``:
+        ``(bucket_ptr [B, h_kv, N_c+1], bucket_keys [B, h_kv, n*b])``."""
+        return ops.build_index(k_codes, self.num_codebook)
+
+    def route_with_index(self, q_full: torch.Tensor, k_full: torch.Tensor, k_codes: torch.Tensor, index,
+                         causal: bool = True, q_offset: int = 0,
+                         index_dtype: torch.dtype = torch.int64) -> torch.Tensor:
+        """:meth:`route_with_key_codes` with the index of ``k_codes`` given
+        (``index`` from :meth:`key_index`), for several query blocks of one
+        sequence against the same keys."""
+        if q_full.shape[-2] % k_full.shape[-2]:
+            raise ValueError("num_q_heads must be divisible by num_kv_heads")
+        with torch.no_grad():
+            return ops.route_with_index(q_full, k_full, k_codes, index[0], index[1], self.W_qr.weight,
+                                        self.W_kr.weight, self.codebook, self.codes_per_query, self.top_k,
+                                        bool(causal), float(self.temperature), int(q_offset),
+                                        index_dtype == torch.int64)
+
     def forward(self, q_full: torch.Tensor, k_full: torch.Tensor,
                 causal_mask: Optional[torch.Tensor] = None, hard: bool = True,
                 causal: Optional[bool] = None) -> torch.Tensor:

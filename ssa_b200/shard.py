@@ -13,10 +13,12 @@ Per forward (:func:`sharded_forward`):
 1. key codes of the rank's own key rows -- the code assignment of a key
    depends on that key alone (``ssa/router.py:114-130``);
 2. the one exchange step: all-gather of K, V and the key codes into
-   full-sequence buffers;
-3. for each of its two blocks, routing of the block's queries against all
-   ``n`` keys with the gathered codes (``q_offset`` = the block's start), then
-   sparse attention over the selected keys.
+   full-sequence buffers (K and V start moving before the code assignment);
+3. the code->key index of all ``n`` keys, built once;
+4. for each of its two blocks, routing of the block's queries against all
+   ``n`` keys with the gathered codes and the index (``q_offset`` = the
+   block's start) -- V is still arriving meanwhile -- then sparse attention
+   over the selected keys.
 
 The reference has no distributed code; this follows the per-query
 independence of ``CodebookRouter.forward`` (``ssa/router.py:73-149``) and
@@ -87,19 +89,21 @@ def gather_sequence(local: torch.Tensor, world: int, group=None, async_op: bool 
 
 def sharded_forward(router, q_local: torch.Tensor, k_local: torch.Tensor, v_local: torch.Tensor,
                     group=None, causal: bool = True, scale: Optional[float] = None,
-                    code_fn: Optional[Callable] = None, route_fn: Optional[Callable] = None,
-                    attn_fn: Optional[Callable] = None) -> torch.Tensor:
+                    code_fn: Optional[Callable] = None, index_fn: Optional[Callable] = None,
+                    route_fn: Optional[Callable] = None, attn_fn: Optional[Callable] = None) -> torch.Tensor:
     """SSA forward of this rank's query rows of one sequence.
 
     ``q_local [B, 2*blk, h_q, d]``, ``k_local``/``v_local [B, 2*blk, h_kv, d]``
     are the rows of this rank's two zig-zag blocks (:func:`local_rows`);
     returns the attention output for those rows, ``[B, 2*blk, h_q, d]``.
 
-    ``code_fn(k) -> codes``, ``route_fn(q_block, k, v, codes, q_offset) ->
-    indices`` and ``attn_fn(q_block, k, v, indices, q_offset) -> out`` default
-    to the sm_100a kernels (:meth:`CodebookRouter.key_codes`,
-    :meth:`CodebookRouter.route_with_key_codes`, sparse attention); they are
-    parameters so that the exchange logic can be checked on CPU ranks."""
+    ``code_fn(k) -> codes``, ``index_fn(codes) -> index``,
+    ``route_fn(q_block, k, codes, index, q_offset) -> indices`` and
+    ``attn_fn(q_block, k, v, indices, q_offset) -> out`` default to the
+    sm_100a kernels (:meth:`CodebookRouter.key_codes`,
+    :meth:`CodebookRouter.key_index`, :meth:`CodebookRouter.route_with_index`,
+    sparse attention); they are parameters so that the exchange logic can be
+    checked on CPU ranks."""
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     rows = q_local.shape[1]
@@ -109,10 +113,12 @@ def sharded_forward(router, q_local: torch.Tensor, k_local: torch.Tensor, v_loca
         scale = math.sqrt(q_local.shape[-1])
     if code_fn is None:
         code_fn = router.key_codes
+    if index_fn is None:
+        index_fn = router.key_index
     if route_fn is None:
-        def route_fn(qb, k, v, codes, q_offset):
-            return router.route_with_key_codes(qb, k, codes, causal=causal, q_offset=q_offset,
-                                               index_dtype=torch.int32)
+        def route_fn(qb, k, codes, index, q_offset):
+            return router.route_with_index(qb, k, codes, index, causal=causal, q_offset=q_offset,
+                                           index_dtype=torch.int32)
     if attn_fn is None:
         from . import ops
 
@@ -124,13 +130,13 @@ def sharded_forward(router, q_local: torch.Tensor, k_local: torch.Tensor, v_loca
     v_work, v_finish = gather_sequence(v_local, world, group, async_op=True)
     codes_local = code_fn(k_local)
     c_work, c_finish = gather_sequence(codes_local, world, group, async_op=True)
-    for w in (k_work, v_work, c_work):
-        w.wait()
-    k_full, v_full, codes = k_finish(), v_finish(), c_finish()
-
-    outs = []
-    for which, (start, length) in enumerate(blocks):
-        qb = q_local[:, which * length:(which + 1) * length]
-        idx = route_fn(qb, k_full, v_full, codes, start)
-        outs.append(attn_fn(qb, k_full, v_full, idx, start))
+    k_work.wait()
+    c_work.wait()
+    k_full, codes = k_finish(), c_finish()
+    index = index_fn(codes)
+    qbs = [q_local[:, which * length:(which + 1) * length] for which, (start, length) in enumerate(blocks)]
+    idxs = [route_fn(qb, k_full, codes, index, start) for qb, (start, _) in zip(qbs, blocks)]
+    v_work.wait()
+    v_full = v_finish()
+    outs = [attn_fn(qb, k_full, v_full, idx, start) for qb, idx, (start, _) in zip(qbs, idxs, blocks)]
     return torch.cat(outs, dim=1)

@@ -224,3 +224,37 @@ def test_route_with_key_codes_refuses_unaligned_codes():
     shifted.copy_(codes)
     with pytest.raises(SSAError, match="aligned"):
         r.route_with_key_codes(q, k, shifted, causal=True)
+
+
+def test_route_with_index_matches_route_on_query_shards():
+    r = _random_router()
+    g = torch.Generator(device="cpu").manual_seed(6)
+    n = 2500
+    q = torch.randn((2, n, 8, 128), generator=g).to(DEV, torch.bfloat16)
+    k = torch.randn((2, n, 2, 128), generator=g).to(DEV, torch.bfloat16)
+    full, _, _, _ = r.route(q, k, causal=True)
+    codes = r.key_codes(k)
+    index = r.key_index(codes)
+    for start, length in [(0, 900), (900, 1600), (2499, 1)]:
+        got = r.route_with_index(q[:, start:start + length], k, codes, index, causal=True, q_offset=start)
+        assert torch.equal(got, full[:, start:start + length]), (start, length)
+
+
+def test_route_with_index_refuses_a_corrupt_index():
+    r = _random_router(n_c=512)
+    q = torch.randn((1, 700, 8, 128), device=DEV, dtype=torch.bfloat16)
+    k = torch.randn((1, 700, 2, 128), device=DEV, dtype=torch.bfloat16)
+    codes = r.key_codes(k)
+    ptr, keys = r.key_index(codes)
+    good = r.route_with_index(q, k, codes, (ptr, keys), causal=True)
+    bad_key = keys.clone()
+    bad_key[0, 1, 33] = 700
+    bad_order = ptr.clone()
+    bad_order[0, 0, 100] = bad_order[0, 0, 102] + 1
+    bad_end = ptr.clone()
+    bad_end[0, 1, -1] = 700 * 4 + 1
+    for index in [(ptr, bad_key), (bad_order, keys), (bad_end, keys)]:
+        with pytest.raises(ValueError, match="index"):
+            r.route_with_index(q, k, codes, index, causal=True)
+    # a valid index still gives the same result afterwards
+    assert torch.equal(r.route_with_index(q, k, codes, (ptr, keys), causal=True), good)

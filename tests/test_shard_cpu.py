@@ -55,7 +55,7 @@ def _oracle_fns(p):
         _, k_route = O.route_vectors(np.zeros((kl.shape[0], HQ, D)), kl, w_qr, w_kr)
         return torch.from_numpy(O.stable_topk(O.code_scores(k_route, cb), B).astype(np.int32))[None]
 
-    def route_fn(qb, k, v, codes, q_offset):
+    def route_fn(qb, k, codes, index, q_offset):
         qn = qb[0].numpy()
         q_route, _ = O.route_vectors(qn, k[0].numpy()[:qn.shape[0]], w_qr, w_kr)
         qc = O.stable_topk(O.code_scores(q_route, cb), A)
@@ -86,8 +86,8 @@ def _worker(rank, world, port, task, result_dir):
             q, k, v = (torch.from_numpy(x)[None] for x in p[:3])
             ql, kl, vl = (shard.local_rows(x, world, rank) for x in (q, k, v))
             code_fn, route_fn, attn_fn = _oracle_fns(p)
-            out = shard.sharded_forward(None, ql, kl, vl, code_fn=code_fn, route_fn=route_fn,
-                                        attn_fn=attn_fn)
+            out = shard.sharded_forward(None, ql, kl, vl, code_fn=code_fn, index_fn=lambda c: None,
+                                        route_fn=route_fn, attn_fn=attn_fn)
             want = shard.local_rows(torch.from_numpy(_oracle_full(p))[None], world, rank)
             ok = out.shape == want.shape and torch.allclose(out, want, rtol=0, atol=1e-12)
         with open(os.path.join(result_dir, f"rank{rank}"), "w") as f:
