@@ -24,6 +24,8 @@
  *                             ssa/router.py:151-259)
  *  - ssa_code_assign       CodebookRouter.get_code_assignment ssa/router.py:261-275
  *  - ssa_sparse_attn       sparse_exact_attention            ssa/attention.py:12-115
+ *  - ssa_sparse_attn_backward  its gradient (the reference differentiates
+ *                          its gather + einsum with autograd)
  *  - ssa_select_from_scores, ssa_build_index, ssa_select_candidates
  *                          test hooks exposing the stage-1 selection
  *                          (ssa/router.py:129-141), the code->key index and the
@@ -168,6 +170,16 @@ typedef struct {
 /* sparse_exact_attention(q, k, v, indices, scale) (ssa/attention.py:12-115)
  * with the per-KV-head gather k[idx, h].  Online softmax in fp32. */
 ssa_status ssa_sparse_attn(const SsaAttnArgs* args, void* stream);
+
+/* Gradients of ssa_sparse_attn (the backward of sparse_exact_attention,
+ * ssa/attention.py:12-115, which the reference differentiates with autograd).
+ * args are the forward's, with args->out = the forward output (read only).
+ * d_out has the strides of out; d_q is written with the strides of q (dtype
+ * of q); d_k and d_v are fp32 [B, n, h_kv, d] contiguous and are zeroed
+ * here, then accumulated with atomic adds (their rounding depends on the
+ * order of the adds).  Indices receive no gradient. */
+ssa_status ssa_sparse_attn_backward(const SsaAttnArgs* args, const void* d_out, void* d_q, float* d_k,
+                                    float* d_v, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Test hooks (bit-exact parity on caller-provided inputs)                   */

@@ -71,6 +71,7 @@ SIGNATURES = {
     "ssa_select_candidates": (ctypes.c_int, [ctypes.POINTER(SsaRouteArgs), _vp, ctypes.c_size_t, _vp]),
     "ssa_route_with_key_codes": (ctypes.c_int, [ctypes.POINTER(SsaRouteArgs), _vp, ctypes.c_size_t, _vp]),
     "ssa_route_with_index": (ctypes.c_int, [ctypes.POINTER(SsaRouteArgs), _vp, _vp, _vp, ctypes.c_size_t, _vp]),
+    "ssa_sparse_attn_backward": (ctypes.c_int, [ctypes.POINTER(SsaAttnArgs), _vp, _vp, _vp, _vp, _vp]),
     "ssa_status_str": (ctypes.c_char_p, [ctypes.c_int]),
     "ssa_last_error": (ctypes.c_char_p, []),
 }

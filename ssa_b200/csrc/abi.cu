@@ -289,6 +289,37 @@ ssa_status noalloc_scratch(void** out) {
   return SSA_OK;
 }
 
+// Validation shared by the attention entry points; fills the kernel params.
+ssa_status attn_params(const SsaAttnArgs* a, ssa::AttnParams& p) {
+  if (!a) return fail(SSA_ERR_INVALID_ARG, "args is NULL");
+  if (a->batch < 0 || a->n_q < 0 || a->n < 1 || a->q_offset < 0 || a->top_k < 1)
+    return fail(SSA_ERR_INVALID_ARG, "bad sizes");
+  if (a->h_kv < 1 || a->h_q % a->h_kv != 0)
+    return fail(SSA_ERR_INVALID_ARG, "num_q_heads (%d) must be a multiple of num_kv_heads (%d)", a->h_q, a->h_kv);
+  if (a->h_q / a->h_kv > 16) return fail(SSA_ERR_UNSUPPORTED, "GQA group size %d > 16", a->h_q / a->h_kv);
+  if (a->d < 8 || a->d > 256 || a->d % 8 != 0)
+    return fail(SSA_ERR_UNSUPPORTED, "head_dim %d: need a multiple of 8 in [8, 256]", a->d);
+  if (!valid_dtype(a->dtype)) return fail(SSA_ERR_INVALID_ARG, "bad dtype");
+  if (a->index_dtype != SSA_I32 && a->index_dtype != SSA_I64) return fail(SSA_ERR_INVALID_ARG, "bad index dtype");
+  if (!a->q || !a->k || !a->v || !a->indices || !a->out) return fail(SSA_ERR_INVALID_ARG, "NULL pointer");
+  if (!(a->scale != 0.f)) return fail(SSA_ERR_INVALID_ARG, "scale must be non-zero");
+  if (!aligned16(a->k) || !stride16(a->k_stride_n, a->dtype) || !stride16(a->k_stride_h, a->dtype) ||
+      !stride16(a->k_stride_b, a->dtype))
+    return fail(SSA_ERR_ALIGNMENT, "k must be 16-byte aligned with 16-byte strides");
+  p.q = a->q; p.q_sb = a->q_stride_b; p.q_sn = a->q_stride_n; p.q_sh = a->q_stride_h;
+  p.k = a->k; p.k_sb = a->k_stride_b; p.k_sn = a->k_stride_n; p.k_sh = a->k_stride_h;
+  p.v = a->v; p.v_sb = a->v_stride_b; p.v_sn = a->v_stride_n; p.v_sh = a->v_stride_h;
+  p.idx = a->indices; p.i_sb = a->idx_stride_b; p.i_sn = a->idx_stride_n; p.i_sh = a->idx_stride_h;
+  p.index_i64 = a->index_dtype == SSA_I64;
+  p.out = a->out; p.o_sb = a->out_stride_b; p.o_sn = a->out_stride_n; p.o_sh = a->out_stride_h;
+  p.status = a->status;
+  p.batch = a->batch; p.n_q = a->n_q; p.n = a->n; p.q_offset = a->q_offset;
+  p.h_kv = a->h_kv; p.group = a->h_q / a->h_kv; p.d = a->d; p.top_k = a->top_k;
+  p.causal = a->causal ? 1 : 0;
+  p.inv_scale = 1.0f / a->scale;
+  return SSA_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -443,36 +474,31 @@ ssa_status ssa_select_candidates(const SsaRouteArgs* args, void* workspace, size
 }
 
 ssa_status ssa_sparse_attn(const SsaAttnArgs* a, void* stream) {
-  if (!a) return fail(SSA_ERR_INVALID_ARG, "args is NULL");
-  if (a->batch < 0 || a->n_q < 0 || a->n < 1 || a->q_offset < 0 || a->top_k < 1)
-    return fail(SSA_ERR_INVALID_ARG, "bad sizes");
-  if (a->h_kv < 1 || a->h_q % a->h_kv != 0)
-    return fail(SSA_ERR_INVALID_ARG, "num_q_heads (%d) must be a multiple of num_kv_heads (%d)", a->h_q, a->h_kv);
-  if (a->h_q / a->h_kv > 16) return fail(SSA_ERR_UNSUPPORTED, "GQA group size %d > 16", a->h_q / a->h_kv);
-  if (a->d < 8 || a->d > 256 || a->d % 8 != 0)
-    return fail(SSA_ERR_UNSUPPORTED, "head_dim %d: need a multiple of 8 in [8, 256]", a->d);
-  if (!valid_dtype(a->dtype)) return fail(SSA_ERR_INVALID_ARG, "bad dtype");
-  if (a->index_dtype != SSA_I32 && a->index_dtype != SSA_I64) return fail(SSA_ERR_INVALID_ARG, "bad index dtype");
-  if (!a->q || !a->k || !a->v || !a->indices || !a->out) return fail(SSA_ERR_INVALID_ARG, "NULL pointer");
-  if (!(a->scale != 0.f)) return fail(SSA_ERR_INVALID_ARG, "scale must be non-zero");
-  if (!aligned16(a->k) || !stride16(a->k_stride_n, a->dtype) || !stride16(a->k_stride_h, a->dtype) ||
-      !stride16(a->k_stride_b, a->dtype))
-    return fail(SSA_ERR_ALIGNMENT, "k must be 16-byte aligned with 16-byte strides");
-  if (a->batch == 0 || a->n_q == 0) return SSA_OK;
   ssa::AttnParams p{};
-  p.q = a->q; p.q_sb = a->q_stride_b; p.q_sn = a->q_stride_n; p.q_sh = a->q_stride_h;
-  p.k = a->k; p.k_sb = a->k_stride_b; p.k_sn = a->k_stride_n; p.k_sh = a->k_stride_h;
-  p.v = a->v; p.v_sb = a->v_stride_b; p.v_sn = a->v_stride_n; p.v_sh = a->v_stride_h;
-  p.idx = a->indices; p.i_sb = a->idx_stride_b; p.i_sn = a->idx_stride_n; p.i_sh = a->idx_stride_h;
-  p.index_i64 = a->index_dtype == SSA_I64;
-  p.out = a->out; p.o_sb = a->out_stride_b; p.o_sn = a->out_stride_n; p.o_sh = a->out_stride_h;
-  p.status = a->status;
-  p.batch = a->batch; p.n_q = a->n_q; p.n = a->n; p.q_offset = a->q_offset;
-  p.h_kv = a->h_kv; p.group = a->h_q / a->h_kv; p.d = a->d; p.top_k = a->top_k;
-  p.causal = a->causal ? 1 : 0;
-  p.inv_scale = 1.0f / a->scale;
-  return cuda_status(ssa::launch_sparse_attn(p, a->dtype, static_cast<cudaStream_t>(stream)),
-                     "sparse_attn");
+  const ssa_status s = attn_params(a, p);
+  if (s != SSA_OK || a->batch == 0 || a->n_q == 0) return s;
+  return cuda_status(ssa::launch_sparse_attn(p, a->dtype, static_cast<cudaStream_t>(stream)), "sparse_attn");
+}
+
+ssa_status ssa_sparse_attn_backward(const SsaAttnArgs* a, const void* d_out, void* d_q, float* d_k, float* d_v,
+                                    void* stream) {
+  ssa::AttnBwdParams bp{};
+  const ssa_status s = attn_params(a, bp.fwd);
+  if (s != SSA_OK) return s;
+  if (!d_out || !d_q || !d_k || !d_v) return fail(SSA_ERR_INVALID_ARG, "NULL gradient pointer");
+  if (a->d > 256) return fail(SSA_ERR_UNSUPPORTED, "head_dim %d > 256", a->d);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t acc = static_cast<size_t>(a->batch) * a->n * a->h_kv * a->d * sizeof(float);
+  cudaError_t e = cudaMemsetAsync(d_k, 0, acc, st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(d_v, 0, acc, st);
+  if (e != cudaSuccess) return cuda_status(e, "zero dK / dV");
+  if (a->batch == 0 || a->n_q == 0) return SSA_OK;
+  bp.d_out = d_out;
+  bp.d_q = d_q;
+  bp.d_k = d_k;
+  bp.d_v = d_v;
+  bp.acc_sn = static_cast<int64_t>(a->h_kv) * a->d;
+  return cuda_status(ssa::launch_sparse_attn_bwd(bp, a->dtype, st), "sparse_attn_backward");
 }
 
 }  // extern "C"

@@ -110,6 +110,19 @@ struct AttnParams {
   float inv_scale;
 };
 
+// Backward of K4: the forward's arguments (with `out` = the forward output,
+// read) plus the output gradient (strides of `out`), dQ (strides of q) and
+// fp32 dK / dV accumulators [B, n, h_kv, d] (row stride acc_sn), zeroed by
+// the caller.
+struct AttnBwdParams {
+  AttnParams fwd;
+  const void* d_out;
+  void* d_q;
+  float* d_k;
+  float* d_v;
+  int64_t acc_sn;
+};
+
 cudaError_t launch_route_project(const RouteProjectParams& p, ssa_dtype xt, ssa_dtype wt,
                                  cudaStream_t st);
 cudaError_t launch_codebook_normalize(const void* cb, ssa_dtype wt, float* out, int64_t rows,
@@ -130,5 +143,6 @@ size_t rescore_smem_bytes(int cap, int top_k);
 cudaError_t launch_sparse_attn(const AttnParams& p, ssa_dtype dt, cudaStream_t st);
 bool sparse_attn_mma_supported(const AttnParams& p, ssa_dtype dt);
 cudaError_t launch_sparse_attn_mma(const AttnParams& p, ssa_dtype dt, cudaStream_t st);
+cudaError_t launch_sparse_attn_bwd(const AttnBwdParams& p, ssa_dtype dt, cudaStream_t st);
 
 }  // namespace ssa

@@ -93,6 +93,13 @@ class SSAAttention(nn.Module):
             out = sparse_exact_attention(q, k, v, idx, scale=math.sqrt(hd), is_causal=self.causal)
         return self.o_proj(out.reshape(bsz, n, self.num_q_heads * hd))
 
+    def compute_auxiliary_loss(self, hidden_states: torch.Tensor, freqs: Optional[torch.Tensor] = None):
+        """The reference's training-time routing loss (KL divergence between
+        the router's code scores and dense attention, ssa/ssa_layer.py:140-213)
+        is not part of the forward hot path this package implements."""
+        raise NotImplementedError("compute_auxiliary_loss is a router-training loss; ssa_b200 implements the "
+                                  "forward path (routing + sparse attention) and its gradient")
+
 
 class ToyTransformerBlock(nn.Module):
     """Pre-norm block: LayerNorm -> SSAAttention -> residual -> LayerNorm ->

@@ -322,6 +322,54 @@ def _sparse_attn_fake(q, k, v, indices, scale, causal, q_offset):
     return torch.empty_like(q)
 
 
+@torch.library.custom_op("ssa_b200::sparse_attn_backward", mutates_args=())
+def sparse_attn_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices: torch.Tensor,
+                         out: torch.Tensor, d_out: torch.Tensor, scale: float, causal: bool,
+                         q_offset: int) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Gradients ``(dq, dk, dv)`` of :func:`sparse_attn` at output gradient
+    ``d_out`` (``out`` is the forward output).  dK and dV are accumulated in
+    fp32 with atomic adds, so their last bits depend on the order of the adds."""
+    dev = _require_cuda(q, k, v, indices, out, d_out)
+    q = q.contiguous()
+    k, v, indices = _last_contig(k), _last_contig(v), _last_contig(indices)
+    out = out.contiguous()
+    d_out = d_out.to(out.dtype).contiguous()
+    B, n, h_kv, d = k.shape
+    dq = torch.empty_like(q)
+    dk = torch.empty((B, n, h_kv, d), dtype=torch.float32, device=dev)
+    dv = torch.empty((B, n, h_kv, d), dtype=torch.float32, device=dev)
+    check = _checked() and not torch.cuda.is_current_stream_capturing()
+    status = torch.zeros(1, dtype=torch.int32, device=dev) if check else None
+    args = attn_args(q, k, v, indices, out, scale, causal, q_offset, status)
+    with torch.cuda.device(dev):
+        L.check("ssa_sparse_attn_backward",
+                L.lib().ssa_sparse_attn_backward(ctypes.byref(args), d_out.data_ptr(), dq.data_ptr(),
+                                                 dk.data_ptr(), dv.data_ptr(), _stream(dev)))
+    if status is not None and int(status.item()) & L.SSA_DEVICE_INDEX_OOB:
+        raise IndexError(f"sparse_exact_attention backward: an index is outside [0, {n})")
+    return dq, dk.to(k.dtype), dv.to(v.dtype)
+
+
+@sparse_attn_backward.register_fake
+def _sparse_attn_backward_fake(q, k, v, indices, out, d_out, scale, causal, q_offset):
+    return torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+
+def _sparse_attn_setup(ctx, inputs, output):
+    q, k, v, indices, scale, causal, q_offset = inputs
+    ctx.save_for_backward(q, k, v, indices, output)
+    ctx.scale, ctx.causal, ctx.q_offset = scale, causal, q_offset
+
+
+def _sparse_attn_grad(ctx, d_out):
+    q, k, v, indices, out = ctx.saved_tensors
+    dq, dk, dv = sparse_attn_backward(q, k, v, indices, out, d_out, ctx.scale, ctx.causal, ctx.q_offset)
+    return dq, dk, dv, None, None, None, None
+
+
+sparse_attn.register_autograd(_sparse_attn_grad, setup_context=_sparse_attn_setup)
+
+
 # ---------------------------------------------------------------------------
 # test hooks (not custom ops): bit-exact parity of the selection stages
 # ---------------------------------------------------------------------------
