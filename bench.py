@@ -67,9 +67,12 @@ def parse():
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
-    p.add_argument("--workload", default="config3", choices=["config3", "config4"],
+    p.add_argument("--workload", default="config3", choices=["config3", "config4", "config5"],
                    help="config3: one sequence per GPU (the headline); config4: one n=131072 "
-                        "sequence split by queries over the GPUs (strong scaling)")
+                        "sequence split by queries over the GPUs (strong scaling); config5: a Qwen-style "
+                        "28-layer decoder stack with SSA attention, one batch per GPU")
+    p.add_argument("--layers", type=int, default=28, help="config5: decoder layers")
+    p.add_argument("--batch", type=int, default=4, help="config5: sequences per GPU")
     return p.parse_args()
 
 
@@ -541,12 +544,147 @@ def run_config4(args):
     return 0
 
 
+def run_config5(args):
+    """Config 5: forward of a Qwen-style decoder stack (28 layers, d_model
+    3584, 28 query / 4 KV heads of 128 -> GQA group 7, SwiGLU 18944, RMSNorm,
+    RoPE base 1e6, q/k/v biases, vocab 152064, random-init bf16 weights) with
+    every attention layer replaced by SSA (d_s 32, N_c 4096, b 4, a 16,
+    k 256): per layer CodebookRouter.route + sparse attention on the sm_100a
+    kernels, the dense projections and the MLP as cuBLAS GEMMs.  Inputs are
+    batch x n token ids uniform over the vocabulary; the LM head is not run
+    (its bf16 logits alone would take 20 GB); the step is the stack's
+    forward up to the final norm.  Each GPU runs its own batch (replicas)."""
+    import datetime
+
+    import torch
+    import torch.nn.functional as F
+
+    import ssa_b200 as ssa
+    from ssa_b200 import ops
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    H, hq, hkv, hd, inter, vocab = 3584, 28, 4, 128, 18944, 152064
+    B = args.batch
+    n = args.n if args.n != 32768 else 16384
+    dt = torch.bfloat16
+    g = torch.Generator(device=dev).manual_seed(args.seed)
+
+    def w(*shape, scale):
+        return (torch.randn(*shape, generator=g, device=dev, dtype=torch.float32) * scale).to(dt)
+
+    layers = []
+    for _ in range(args.layers):
+        r = ssa.CodebookRouter(head_dim=hd, route_dim=32, num_kv_heads=hkv, num_codebook=4096, codes_per_key=4,
+                               codes_per_query=16, top_k=256).to(dev)
+        layers.append(dict(
+            ln1=torch.ones(H, device=dev, dtype=dt), ln2=torch.ones(H, device=dev, dtype=dt),
+            wq=w(hq * hd, H, scale=H ** -0.5), bq=w(hq * hd, scale=0.02),
+            wk=w(hkv * hd, H, scale=H ** -0.5), bk=w(hkv * hd, scale=0.02),
+            wv=w(hkv * hd, H, scale=H ** -0.5), bv=w(hkv * hd, scale=0.02),
+            wo=w(H, hq * hd, scale=(hq * hd) ** -0.5),
+            wg=w(inter, H, scale=H ** -0.5), wu=w(inter, H, scale=H ** -0.5), wd=w(H, inter, scale=inter ** -0.5),
+            router=r))
+    emb = w(vocab, H, scale=0.02)
+    ln_f = torch.ones(H, device=dev, dtype=dt)
+    ids = torch.randint(0, vocab, (B, n), generator=g, device=dev)
+    inv_freq = 1.0 / (1e6 ** (torch.arange(0, hd, 2, device=dev, dtype=torch.float32) / hd))
+    ang = torch.arange(n, device=dev, dtype=torch.float32)[:, None] * inv_freq[None, :]
+    cos = torch.cat([ang.cos(), ang.cos()], dim=-1).to(dt)[None, :, None, :]
+    sin = torch.cat([ang.sin(), ang.sin()], dim=-1).to(dt)[None, :, None, :]
+
+    def rms(x, wt):
+        xf = x.float()
+        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)).to(dt) * wt
+
+    def rope(x):                                      # position-indexed rotate-half RoPE
+        x1, x2 = x[..., : hd // 2], x[..., hd // 2:]
+        return x * cos + torch.cat([-x2, x1], dim=-1) * sin
+
+    attn_ms = [0.0]
+
+    def forward(time_attn=False):
+        x = emb[ids]
+        for L in layers:
+            h = rms(x, L["ln1"])
+            q = rope(F.linear(h, L["wq"], L["bq"]).view(B, n, hq, hd))
+            k = rope(F.linear(h, L["wk"], L["bk"]).view(B, n, hkv, hd))
+            v = F.linear(h, L["wv"], L["bv"]).view(B, n, hkv, hd)
+            if time_attn:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+            idx = L["router"].route(q, k, causal=True, index_dtype=torch.int32)[0]
+            o = ops.sparse_attn(q, k, v, idx, hd ** 0.5, True, 0)
+            if time_attn:
+                e1.record()
+                torch.cuda.synchronize(dev)
+                attn_ms[0] += e0.elapsed_time(e1)
+            x = x + F.linear(o.reshape(B, n, hq * hd), L["wo"])
+            h = rms(x, L["ln2"])
+            x = x + F.linear(F.silu(F.linear(h, L["wg"])) * F.linear(h, L["wu"]), L["wd"])
+        return rms(x, ln_f)
+
+    os.environ.setdefault("SSA_CHECKED", "0")
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            forward()
+        torch.cuda.synchronize(dev)
+        clocks = ClockSampler(local)
+        clocks.start()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        stream = torch.cuda.current_stream(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            out = forward()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        clk = clocks.stop()
+        total = e0.elapsed_time(e1)
+        if dist:
+            tt = torch.tensor([total], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            total = float(tt.item())
+        forward(time_attn=True)                       # one more step, synchronised per layer: SSA share
+        finite = bool(torch.isfinite(out).all())
+    ms_step = total / args.steps
+    if rank == 0:
+        line = {"metric": "Qwen-style stack forward tokens/s with SSA attention (bf16)",
+                "value": world * B * n / (ms_step / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (random-init weights, token ids uniform over the vocabulary)",
+                "config": {"workload": "config5 (Qwen-style decoder stack, SSA in every layer)",
+                           "layers": args.layers, "d_model": H, "h_q": hq, "h_kv": hkv, "d_head": hd,
+                           "mlp": inter, "vocab": vocab, "batch_per_gpu": B, "n": n, "d_s": 32, "n_codes": 4096,
+                           "a": 16, "b": 4, "top_k": 256, "lm_head": "not run",
+                           "parallelism": f"replicas x{world}"},
+                "ssa_ms_per_step": attn_ms[0], "ssa_share": attn_ms[0] / ms_step, "output_finite": finite,
+                "roofline": None, "cpu_baseline": None, "e2e": None, "clocks": clk}
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
     if args.workload == "config4":
         return run_config4(args)
+    if args.workload == "config5":
+        return run_config5(args)
     return run_ours(args)
 
 
