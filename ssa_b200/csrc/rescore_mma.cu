@@ -52,18 +52,32 @@ struct __align__(128) RsMmaSmem {
 
 // Descending bitonic sort of 32*E keys, blocked layout: key[e] of lane l is
 // at position l*E + e, so the stages with partner distance < E compare within
-// a lane and only log2(32) of every log2(32*E) stages shuffle.
+// a lane and only log2(32) of every log2(32*E) stages shuffle.  The stage
+// loops stay rolled (run-time distances; the in-lane distances E/2 .. 1 are
+// unrolled once): the whole network is a few hundred instructions of code, so
+// the warps of a CTA do not evict one another's instructions.
 template <int E>
 __device__ __forceinline__ void sort_desc_blocked(uint64_t (&key)[E], int lane) {
   constexpr int N = 32 * E;
-#pragma unroll
+#pragma unroll 1
   for (int k2 = 2; k2 <= N; k2 <<= 1) {
+#pragma unroll 1
+    for (int j = k2 >> 1; j >= E; j >>= 1) {       // partner in lane ^ (j / E)
 #pragma unroll
-    for (int j = k2 >> 1; j > 0; j >>= 1) {
-      if (j < E) {
+      for (int e = 0; e < E; ++e) {
+        const uint64_t other = __shfl_xor_sync(0xffffffffu, key[e], j / E);
+        const int pos = lane * E + e;
+        const bool keep_max = ((pos & k2) == 0) == ((pos & j) == 0);
+        const bool gt = key[e] > other;
+        key[e] = (gt == keep_max) ? key[e] : other;
+      }
+    }
+#pragma unroll
+    for (int jj = E >> 1; jj > 0; jj >>= 1) {      // partner in the same lane
+      if (jj <= (k2 >> 1)) {
 #pragma unroll
         for (int e = 0; e < E; ++e) {
-          const int f = e ^ j;
+          const int f = e ^ jj;
           if (f > e) {
             const bool desc = ((lane * E + e) & k2) == 0;
             const uint64_t x = key[e], y = key[f];
@@ -71,15 +85,6 @@ __device__ __forceinline__ void sort_desc_blocked(uint64_t (&key)[E], int lane) 
             key[e] = swap ? y : x;
             key[f] = swap ? x : y;
           }
-        }
-      } else {
-#pragma unroll
-        for (int e = 0; e < E; ++e) {
-          const uint64_t other = __shfl_xor_sync(0xffffffffu, key[e], j / E);
-          const int pos = lane * E + e;
-          const bool keep_max = ((pos & k2) == 0) == ((pos & j) == 0);
-          const bool gt = key[e] > other;
-          key[e] = (gt == keep_max) ? key[e] : other;
         }
       }
     }
