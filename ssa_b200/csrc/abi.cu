@@ -51,7 +51,7 @@ int rescore_cap(int k_eff) {
 // Workspace regions for a route call.
 struct RouteLayout {
   size_t q_route, k_route, cb_norm, cb_image, q_codes, k_codes, counts, partials, bucket_ptr,
-      bucket_keys, ovf, ovf2, flags;
+      bucket_keys, bucket_codes, ovf, ovf2, flags;
   size_t total;
   int tiles;
   int64_t chunks;
@@ -77,6 +77,7 @@ RouteLayout route_layout(const SsaRouteArgs& a) {
   L.partials = take(static_cast<size_t>(B * hk * L.chunks) * 4);
   L.bucket_ptr = take(static_cast<size_t>(B * hk) * (a.n_codes + 1) * 4);
   L.bucket_keys = take(static_cast<size_t>(B * hk) * a.n * a.b * 4);
+  L.bucket_codes = take(a.b == 4 ? static_cast<size_t>(B * hk) * a.n * 4 * 16 : 0);   // int4 per entry
   L.ovf = take((1 + static_cast<size_t>(B * hk) * a.n_q) * 4);   // overflow count + unit list
   L.ovf2 = take((1 + static_cast<size_t>(B * hk) * a.n_q) * 4);  // second-tier count + list
   L.flags = take(4);                                               // index-validation flag
@@ -230,6 +231,13 @@ ssa_status run_rescore(const SsaRouteArgs& a, const RouteLayout& L, void* ws, cu
   rp.bucket_ptr = bucket_ptr;
   rp.bucket_keys = bucket_keys;
   rp.index_bad = index_bad;
+  if (a.b == 4) {
+    int4* bc = at<int4>(ws, L.bucket_codes);
+    const cudaError_t ec = launch_index_codes(bucket_keys, k_codes, bc, static_cast<int64_t>(a.batch) * a.h_kv, a.n,
+                                              a.h_kv, st);
+    if (ec != cudaSuccess) return cuda_status(ec, "index_codes");
+    rp.bucket_codes = bc;
+  }
   rp.out = a.indices;
   rp.index_i64 = a.index_dtype == SSA_I64;
   rp.cand_counts = a.cand_counts;

@@ -225,6 +225,31 @@ __global__ void validate_index_kernel(const int32_t* ptr, const int32_t* keys, i
   }
 }
 
+__global__ void index_codes_kernel(const int32_t* keys, const int32_t* k_codes, int4* out, int64_t batch_heads,
+                                   int n, int h_kv) {
+  const int64_t total = batch_heads * n * 4;
+  for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t bh = e / (static_cast<int64_t>(n) * 4);
+    const int64_t bat = bh / h_kv;
+    const int h = static_cast<int>(bh % h_kv);
+    const int j = keys[e];
+    out[e] = static_cast<unsigned>(j) < static_cast<unsigned>(n)
+                 ? *reinterpret_cast<const int4*>(k_codes + ((bat * n + j) * h_kv + h) * 4)
+                 : make_int4(-1, -1, -1, -1);
+  }
+}
+
+cudaError_t launch_index_codes(const int32_t* bucket_keys, const int32_t* k_codes, int4* bucket_codes,
+                               int64_t batch_heads, int n, int h_kv, cudaStream_t st) {
+  const int64_t total = batch_heads * n * 4;
+  if (total == 0) return cudaSuccess;
+  const int64_t blocks = cdiv(total, 256) < 148 * 8 ? cdiv(total, 256) : 148 * 8;
+  index_codes_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(bucket_keys, k_codes, bucket_codes,
+                                                                  batch_heads, n, h_kv);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_validate_index(const int32_t* bucket_ptr, const int32_t* bucket_keys, int64_t batch_heads,
                                   int n_codes, int n, int b, int32_t* bad, int32_t* status, cudaStream_t st) {
   cudaError_t e = cudaMemsetAsync(bad, 0, sizeof(int32_t), st);

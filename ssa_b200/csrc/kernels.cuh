@@ -59,6 +59,11 @@ inline int index_tile_keys(int b) { return kIndexSortEntries / b; }
 
 // Checks a caller-given code->key index (bucket bounds non-decreasing within
 // [0, n*b], keys in [0, n)); any violation sets *bad and SSA_DEVICE_BAD_INDEX.
+// bucket_codes[e] = the 4 codes of key bucket_keys[e] (b == 4), so that a walk
+// over the index reads an entry's key and its codes side by side; an entry
+// outside [0, n) gets codes -1.
+cudaError_t launch_index_codes(const int32_t* bucket_keys, const int32_t* k_codes, int4* bucket_codes,
+                               int64_t batch_heads, int n, int h_kv, cudaStream_t st);
 cudaError_t launch_validate_index(const int32_t* bucket_ptr, const int32_t* bucket_keys, int64_t batch_heads,
                                   int n_codes, int n, int b, int32_t* bad, int32_t* status, cudaStream_t st);
 
@@ -74,6 +79,7 @@ struct RescoreParams {
   int32_t* cand_counts;        // optional [B, n_q, h_kv]
   int32_t* status;             // optional device word (SSA_DEVICE_BAD_CODE)
   const int32_t* index_bad;    // optional: non-zero when a caller-given index failed validation
+  const int4* bucket_codes;    // optional (b == 4): the codes of each index entry's key, [B*h_kv, n*4]
   int batch, n, n_q, q_offset, h_kv, group, d, a, b, n_codes, top_k, causal;
   int cap;                     // shared-memory candidate capacity (power of two)
   int32_t* ovf_count;          // workspace: units left to the general path ...

@@ -237,30 +237,38 @@ __device__ __forceinline__ void rescore_mma_unit(const RescoreParams& p, int64_t
   // ---- 1b. walk the buckets: first-match dedupe, compact kept key indices ----
   const int32_t* kcodes = p.k_codes + static_cast<int64_t>(bat) * p.n * p.h_kv * p.b;
   int32_t* jlist = reinterpret_cast<int32_t*>(s.sel);
+  // with b == 4 the index carries each entry's key codes beside it: key and
+  // codes of an entry are loaded in the same round trip
+  const int4* bcodes = p.bucket_codes ? p.bucket_codes + static_cast<int64_t>(bh) * p.n * 4 : nullptr;
   int count = 0;
   int t = 0;
   for (int m0 = 0; m0 < total; m0 += kWalk * kWarp) {
     int32_t j[kWalk];
     int tt[kWalk];
     bool keep[kWalk];
+    int4 c4[kWalk];
 #pragma unroll
     for (int w = 0; w < kWalk; ++w) {          // key indices of the group (coalesced within a bucket)
       const int m = m0 + w * kWarp + lane;
       keep[w] = m < total;
       j[w] = 0;
+      c4[w] = make_int4(-1, -1, -1, -1);
       if (keep[w]) {
         while (s.pre[t + 1] <= m) ++t;
-        j[w] = bk[s.lo[t] + (m - s.pre[t])];
+        const int e = s.lo[t] + (m - s.pre[t]);
+        j[w] = bk[e];
+        if (bcodes && t > 0) c4[w] = bcodes[e];
       }
       tt[w] = t;
     }
     if (p.b == 4) {
-      int4 c4[kWalk];
+      if (!bcodes) {
 #pragma unroll
-      for (int w = 0; w < kWalk; ++w)          // the keys' codes, all loads in flight together
-        c4[w] = keep[w] && tt[w] > 0
-                    ? *reinterpret_cast<const int4*>(kcodes + (static_cast<int64_t>(j[w]) * p.h_kv + h) * 4)
-                    : make_int4(-1, -1, -1, -1);
+        for (int w = 0; w < kWalk; ++w)        // the keys' codes, all loads in flight together
+          c4[w] = keep[w] && tt[w] > 0
+                      ? *reinterpret_cast<const int4*>(kcodes + (static_cast<int64_t>(j[w]) * p.h_kv + h) * 4)
+                      : make_int4(-1, -1, -1, -1);
+      }
 #pragma unroll
       for (int w = 0; w < kWalk; ++w)
         for (int u = 0; u < tt[w]; ++u) {
