@@ -24,7 +24,7 @@
 //      written in order; filler and zero padding follow.
 // Two tiers: every unit first runs with room for 512 candidates (4 warps per
 // CTA); units with more go to an overflow list that a second launch runs with
-// room for 2048 (2 warps per CTA, persistent over the list).  Units beyond
+// room for 1024 (4 warps per CTA, persistent over the list).  Units beyond
 // that, or with k > 512, go to the CTA-wide path.
 #include "common.cuh"
 #include "kernels.cuh"
@@ -488,8 +488,9 @@ static cudaError_t launch_mma_t(const RescoreParams& p, cudaStream_t st) {
   if (e != cudaSuccess) return e;
   k1<<<static_cast<unsigned>(cdiv(units, U1)), U1 * kWarp, smem1, st>>>(p, nullptr, nullptr, p.ovf2_list,
                                                                        p.ovf2_count);
-  // tier 2: the overflow units, room for 2048; overflow -> the CTA-wide path
-  constexpr int U2 = 2, C2 = 2048;
+  // tier 2: the overflow units, room for 1024 (4 warps per CTA, three CTAs per
+  // SM); overflow -> the CTA-wide path
+  constexpr int U2 = 4, C2 = 1024;
   const size_t smem2 = sizeof(RsMmaSmem<C2>) * U2;
   auto k2 = rescore_mma_kernel<T, D, C2, U2, true>;
   e = cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem2));
