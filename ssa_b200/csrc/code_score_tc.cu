@@ -48,6 +48,7 @@ constexpr int kEpiWG = 2;
 constexpr int kEpiWarps = 4 * kEpiWG;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kColsPerWG = kN / kEpiWG;
+static_assert((kColsPerWG / 32) % 2 == 0, "pass 1 reads two 32-column parts per step");
 constexpr uint64_t kWaitNs = 1000000000ull;   // 1 s
 
 template <int DS>
@@ -129,7 +130,9 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
 __device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+// 32 consecutive accumulator columns of this thread's TMEM lane; the values
+// are usable after tmem_wait().
+__device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t (&v)[32]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
       "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -140,7 +143,14 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
         "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]),
         "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
       : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Three-input maximum (one instruction on sm_100; NaN inputs are ignored as by fmaxf).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
 }
 
 // v[j] for a run-time j in [0, 32) without indexing the register array (which
@@ -385,12 +395,14 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
         uint32_t taddr;
         if (!acquire(g, taddr)) { ok = false; break; }
 #pragma unroll 1
-        for (int part = 0; part < kColsPerWG / 32; ++part) {
-          uint32_t v[32];
-          tmem_ld32(taddr + part * 32, v);
-          if (part == kColsPerWG / 32 - 1) release(g);
+        for (int part = 0; part < kColsPerWG / 32; part += 2) {
+          uint32_t v[32], w[32];
+          tmem_ld32_async(taddr + part * 32, v);
+          tmem_ld32_async(taddr + part * 32 + 32, w);
+          tmem_wait();
+          if (part == kColsPerWG / 32 - 2) release(g);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) m1[j] = fmaxf(m1[j], __uint_as_float(v[j]));
+          for (int j = 0; j < 32; ++j) m1[j] = fmax3(m1[j], __uint_as_float(v[j]), __uint_as_float(w[j]));
         }
       }
       if (!ok) { fail(); break; }
@@ -443,7 +455,8 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
 #pragma unroll 1
         for (int part = 0; part < kColsPerWG / 32; ++part) {
           uint32_t v[32];
-          tmem_ld32(taddr + part * 32, v);
+          tmem_ld32_async(taddr + part * 32, v);
+          tmem_wait();
           if (part == kColsPerWG / 32 - 1) release(g);
           uint32_t hit = 0;
 #pragma unroll

@@ -14,6 +14,7 @@
 // linear map, evaluated with g times fewer multiply-adds.
 #include "common.cuh"
 #include "kernels.cuh"
+#include "mma_utils.cuh"
 
 namespace ssa {
 
@@ -190,6 +191,153 @@ __global__ void __launch_bounds__(kRpThreads) route_project_kernel(RouteProjectP
   }
 }
 
+// ---------------------------------------------------------------------------
+// K0 on the tensor cores (16-bit inputs): route[r] = W . sum_g x[r, g] as an
+// mma.sync m16n8k16 GEMM with K = g * d (the group's heads one after another,
+// each against the same W) and N = d_s, then the 1/g scale and the L2
+// normalisation in the epilogue.
+//
+// W (fp32, or 16-bit) is split into three 16-bit terms of the input's type,
+// w = w0 + w1 + w2 exactly for bf16 (8 + 8 + 8 significant bits) and to
+// below 2^-24 |w| for f16, and each A fragment is multiplied by all three:
+// every product x * w is exact and only the fp32 accumulation rounds.
+//
+// K order: the dot product over e is order-free, so the k index of the MMA
+// is mapped onto e to let each thread fill its A fragments with 16-byte loads
+// straight from global memory: within a 32-element chunk c of a row, quad
+// position p loads e in [32c + 8p, 32c + 8p + 8); k step 2c + h takes
+// e = 32c + 8p + 4h + {0, 1} as fragment columns 2p, 2p + 1 and
+// e = 32c + 8p + 4h + {2, 3} as columns 2p + 8, 2p + 9.  The W image in
+// shared memory holds each thread's B fragments in that order,
+// [k step][n tile][term][lane] x 8 bytes, so a warp reads 256 contiguous bytes
+// per fragment (no bank conflicts).
+//
+// A warp owns 32 consecutive rows (two m tiles); rows are in (bat, h, i)
+// order as in the FMA version.
+// ---------------------------------------------------------------------------
+constexpr int kRmWarps = 4;
+constexpr int kRmMT = 2;           // m tiles (16 rows) per warp
+
+template <typename T, typename TW, int NT>
+__global__ void __launch_bounds__(kRmWarps * kWarp) route_project_mma_kernel(RouteProjectParams p) {
+  extern __shared__ __align__(16) uint2 wimg[];          // [d/16][NT][3][32]
+  const int d = p.d;
+  const int ksteps = d / 16;
+  const TW* w = static_cast<const TW*>(p.w);
+  for (int t = threadIdx.x; t < ksteps * NT * 3 * kWarp; t += blockDim.x) {
+    const int ln = t % kWarp, term = (t / kWarp) % 3, nt = (t / (3 * kWarp)) % NT, s = t / (3 * kWarp * NT);
+    const int n = nt * 8 + ln / 4;
+    const int e0 = 32 * (s / 2) + 8 * (ln % 4) + 4 * (s % 2);
+    float part[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float x = Elem<TW>::to_f(w[static_cast<int64_t>(n) * d + e0 + u]);
+      for (int tt = 0; tt < term; ++tt) x -= Elem<T>::to_f(Elem<T>::from_f(x));
+      part[u] = x;
+    }
+    wimg[t] = make_uint2(pack2<T>(part[0], part[1]), pack2<T>(part[2], part[3]));
+  }
+  __syncthreads();
+
+  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+  const int gq = lane / 4, qp = lane % 4;
+  const T* src = static_cast<const T*>(p.x);
+  const float inv_g = 1.0f / static_cast<float>(p.group);
+  const int64_t tasks = cdiv(p.rows, 16 * kRmMT);
+  for (int64_t task = static_cast<int64_t>(blockIdx.x) * kRmWarps + warp; task < tasks;
+       task += static_cast<int64_t>(gridDim.x) * kRmWarps) {
+    // this thread's rows: m tile mt, half hh -> row task*32 + 16 mt + 8 hh + gq
+    const T* base[kRmMT][2];
+    bool ok[kRmMT][2];
+#pragma unroll
+    for (int mt = 0; mt < kRmMT; ++mt)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int64_t row = task * (16 * kRmMT) + 16 * mt + 8 * hh + gq;
+        ok[mt][hh] = row < p.rows;
+        const int64_t rr = ok[mt][hh] ? row : 0;
+        const int64_t i = rr % p.n_rows, bh = rr / p.n_rows;
+        const int h = static_cast<int>(bh % p.h_kv);
+        const int64_t bat = bh / p.h_kv;
+        base[mt][hh] = src + bat * p.stride_b + i * p.stride_n + static_cast<int64_t>(h) * p.group * p.stride_h +
+                       8 * qp;
+      }
+    float acc[kRmMT][NT][4];
+#pragma unroll
+    for (int mt = 0; mt < kRmMT; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int u = 0; u < 4; ++u) acc[mt][nt][u] = 0.f;
+
+    for (int gg = 0; gg < p.group; ++gg) {
+      for (int c0 = 0; c0 < d / 32; c0 += 4) {
+        // up to four 32-element chunks of every row in flight
+        uint4 raw[4][kRmMT][2];
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc)
+#pragma unroll
+          for (int mt = 0; mt < kRmMT; ++mt)
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              raw[cc][mt][hh] = make_uint4(0u, 0u, 0u, 0u);
+              if (ok[mt][hh] && c0 + cc < d / 32)
+                raw[cc][mt][hh] = __ldg(reinterpret_cast<const uint4*>(
+                    base[mt][hh] + static_cast<int64_t>(gg) * p.stride_h + 32 * (c0 + cc)));
+            }
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          if (c0 + cc >= d / 32) break;
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            const int s = 2 * (c0 + cc) + h2;
+            uint32_t a[kRmMT][4];
+#pragma unroll
+            for (int mt = 0; mt < kRmMT; ++mt) {
+              a[mt][0] = h2 ? raw[cc][mt][0].z : raw[cc][mt][0].x;
+              a[mt][1] = h2 ? raw[cc][mt][1].z : raw[cc][mt][1].x;
+              a[mt][2] = h2 ? raw[cc][mt][0].w : raw[cc][mt][0].y;
+              a[mt][3] = h2 ? raw[cc][mt][1].w : raw[cc][mt][1].y;
+            }
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+              for (int term = 0; term < 3; ++term) {
+                const uint2 b = wimg[((s * NT + nt) * 3 + term) * kWarp + lane];
+#pragma unroll
+                for (int mt = 0; mt < kRmMT; ++mt) mma16816<T>(acc[mt][nt], a[mt], b.x, b.y);
+              }
+          }
+        }
+      }
+    }
+    // epilogue: row (mt, hh) holds columns nt*8 + 2qp + {0,1} in acc[mt][nt][2hh + {0,1}]
+#pragma unroll
+    for (int mt = 0; mt < kRmMT; ++mt)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        float ss = 0.f;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          acc[mt][nt][2 * hh] *= inv_g;
+          acc[mt][nt][2 * hh + 1] *= inv_g;
+          ss += acc[mt][nt][2 * hh] * acc[mt][nt][2 * hh] + acc[mt][nt][2 * hh + 1] * acc[mt][nt][2 * hh + 1];
+        }
+        ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+        ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+        const float nrm = fmaxf(sqrtf(ss), 1e-12f);
+        if (ok[mt][hh]) {
+          const int64_t row = task * (16 * kRmMT) + 16 * mt + 8 * hh + gq;
+          float* out = p.out + row * (NT * 8) + 2 * qp;
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+            *reinterpret_cast<float2*>(out + nt * 8) =
+                make_float2(acc[mt][nt][2 * hh] / nrm, acc[mt][nt][2 * hh + 1] / nrm);
+        }
+      }
+  }
+}
+
 // Codebook rows -> L2-normalised fp32 copy [heads][n_codes][d_s].
 template <typename TW>
 __global__ void codebook_normalize_kernel(const TW* cb, float* out, int64_t rows, int d_s) {
@@ -287,8 +435,52 @@ __global__ void select_from_scores_kernel(const float* scores, int64_t rows, int
 // ---------------------------------------------------------------------------
 // host-side launchers
 // ---------------------------------------------------------------------------
+template <typename T, typename TW, int NT>
+static cudaError_t launch_route_project_mma_t(const RouteProjectParams& p, int sms, cudaStream_t st) {
+  auto kern = route_project_mma_kernel<T, TW, NT>;
+  const size_t smem = static_cast<size_t>(p.d / 16) * NT * 3 * kWarp * sizeof(uint2);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  int per_sm = 1;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kRmWarps * kWarp, smem);
+  if (e != cudaSuccess) return e;
+  const int64_t tasks = cdiv(p.rows, 16 * kRmMT);
+  int64_t blocks = cdiv(tasks, kRmWarps);
+  const int64_t cap = static_cast<int64_t>(sms) * (per_sm > 0 ? per_sm : 1);
+  if (blocks > cap) blocks = cap;
+  kern<<<static_cast<unsigned>(blocks), kRmWarps * kWarp, smem, st>>>(p);
+  return cudaGetLastError();
+}
+
+template <typename T, typename TW>
+static cudaError_t launch_route_project_mma_w(const RouteProjectParams& p, int sms, cudaStream_t st) {
+  switch (p.d_s) {
+    case 8: return launch_route_project_mma_t<T, TW, 1>(p, sms, st);
+    case 16: return launch_route_project_mma_t<T, TW, 2>(p, sms, st);
+    case 32: return launch_route_project_mma_t<T, TW, 4>(p, sms, st);
+    default: return launch_route_project_mma_t<T, TW, 8>(p, sms, st);
+  }
+}
+
+// The tensor-core projection takes 16-bit inputs with d a multiple of 32 and
+// d_s in {8, 16, 32, 64}; everything else runs the FMA version.
+static bool route_project_mma_ok(const RouteProjectParams& p, ssa_dtype xt) {
+  return (xt == SSA_BF16 || xt == SSA_F16) && p.d % 32 == 0 && p.d >= 32 &&
+         (p.d_s == 8 || p.d_s == 16 || p.d_s == 32 || p.d_s == 64);
+}
+
 cudaError_t launch_route_project(const RouteProjectParams& p, ssa_dtype xt, ssa_dtype wt,
                                  cudaStream_t st) {
+  if (p.rows == 0) return cudaSuccess;
+  if (route_project_mma_ok(p, xt)) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (xt == SSA_BF16 && wt == SSA_BF16) return launch_route_project_mma_w<__nv_bfloat16, __nv_bfloat16>(p, sms, st);
+    if (xt == SSA_BF16 && wt == SSA_F32) return launch_route_project_mma_w<__nv_bfloat16, float>(p, sms, st);
+    if (xt == SSA_F16 && wt == SSA_F16) return launch_route_project_mma_w<__half, __half>(p, sms, st);
+    if (xt == SSA_F16 && wt == SSA_F32) return launch_route_project_mma_w<__half, float>(p, sms, st);
+  }
   const int threads = kRpThreads;
   const size_t smem = (static_cast<size_t>(p.d) * p.d_s + static_cast<size_t>(kRpRows) * p.d) * sizeof(float);
   int dev = 0, sms = 148;
