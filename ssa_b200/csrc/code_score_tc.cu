@@ -49,6 +49,7 @@ constexpr int kEpiWarps = 4 * kEpiWG;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kColsPerWG = kN / kEpiWG;
 static_assert((kColsPerWG / 32) % 2 == 0, "pass 1 reads two 32-column parts per step");
+static_assert(kEpiWG == 2, "the bound merges exactly two lists per row");
 constexpr uint64_t kWaitNs = 1000000000ull;   // 1 s
 
 template <int DS>
@@ -191,8 +192,8 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
   uint64_t* cand = reinterpret_cast<uint64_t*>(b_img + kStages * G::B_BYTES);
   float* kept = reinterpret_cast<float*>(cand);
   uint64_t* merge_k = cand;
-  float* bound = reinterpret_cast<float*>(cand + kCand * EPI);       // [kEpiWG][kM]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(bound + kEpiWG * kM);
+  __half* lists = reinterpret_cast<__half*>(cand + kCand * EPI);     // [kEpiWG][kM][KMAX] bound lists
+  uint64_t* bars = reinterpret_cast<uint64_t*>(lists + kEpiWG * kM * KMAX);
   // barriers: b_full[kStages], b_empty[kStages], t_full[2], t_empty[2], a_ready[2], m_bar[2]
   const uint32_t b_full = smem_u32(bars);
   const uint32_t b_empty = b_full + 8 * kStages;
@@ -406,9 +407,13 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
         }
       }
       if (!ok) { fail(); break; }
-      // KMAX-th largest group maximum: KMAX distinct scores reach it, so (up
-      // to the dropped lo terms) it is a lower bound on this thread's -- hence
-      // the row's -- KMAX-th largest score.
+      // The row's 64 column groups (32 per warpgroup, disjoint) have maxima
+      // m_1 >= m_2 >= ...: KMAX distinct scores reach m_KMAX, so (up to the
+      // dropped lo terms) m_KMAX is a lower bound on the row's KMAX-th largest
+      // score.  Each thread sorts its own 32 maxima down to a top-KMAX list,
+      // the two lists of a row meet in shared memory (rounded down to f16,
+      // which only lowers the bound), and both threads take the KMAX-th
+      // largest of their union.
 #pragma unroll
       for (int j = 0; j < 32; ++j) kept[j * EPI + et] = m1[j];
       {
@@ -425,13 +430,23 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
             best[t] = hi;
           }
         }
-        bound[wg * kM + r] = best[KMAX - 1];
+        __half* mine = lists + (wg * kM + r) * KMAX;
+#pragma unroll
+        for (int t = 0; t < KMAX; ++t) mine[t] = __float2half_rd(best[t]);
       }
       if (!epi_sync(m_bar + 8 * (msync & 1), static_cast<uint32_t>((msync >> 1) & 1))) { fail(); break; }
       ++msync;
-      float lb = bound[r];
+      // KMAX-th largest of the union of two descending lists a, b:
+      // max over t of min(a[t-1], b[KMAX-1-t]), a[-1] = b[-1] = +inf.  Both
+      // warpgroups evaluate it in the same order, so they get the same value.
+      float lb;
+      {
+        const __half* la = lists + r * KMAX;
+        const __half* lo = lists + (kM + r) * KMAX;
+        lb = fmaxf(__half2float(la[KMAX - 1]), __half2float(lo[KMAX - 1]));
 #pragma unroll
-      for (int w2 = 1; w2 < kEpiWG; ++w2) lb = fmaxf(lb, bound[w2 * kM + r]);
+        for (int t = 1; t < KMAX; ++t) lb = fmaxf(lb, fminf(__half2float(la[t - 1]), __half2float(lo[KMAX - 1 - t])));
+      }
       // |a.c - a_hi.c_hi| <= 2^-10 for unit vectors a, c (f16 rounding of each
       // operand, Cauchy-Schwarz); 2^-9 leaves a margin for fp32 accumulation.
       lb -= 1.0f / 512.0f;
@@ -507,7 +522,7 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
             if (t < p.kk) out[t] = top.index(t);
         }
       }
-      // the bound and merge buffers are rewritten next tile only after every
+      // the bound lists and merge buffers are rewritten next tile only after every
       // epilogue warp is past this point
       if (!epi_sync(m_bar + 8 * (msync & 1), static_cast<uint32_t>((msync >> 1) & 1))) { fail(); break; }
       ++msync;
@@ -558,7 +573,8 @@ size_t smem_bytes(int kmax) {
   const size_t shared = std::max<size_t>({static_cast<size_t>(kCand) * 32 * kEpiWarps * 8,
                                           static_cast<size_t>(32) * 32 * kEpiWarps * 4,
                                           static_cast<size_t>(kEpiWG - 1) * kM * kmax * 8});
-  return 1024 + 2 * G::A_BYTES + kStages * G::B_BYTES + shared + kEpiWG * kM * 4 + (2 * kStages + 8) * 8 + 16;
+  return 1024 + 2 * G::A_BYTES + kStages * G::B_BYTES + shared + static_cast<size_t>(kEpiWG) * kM * kmax * 2 +
+         (2 * kStages + 8) * 8 + 16;
 }
 
 }  // namespace tc
