@@ -450,8 +450,11 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
       // |a.c - a_hi.c_hi| <= 2^-10 for unit vectors a, c (f16 rounding of each
       // operand, Cauchy-Schwarz); 2^-9 leaves a margin for fp32 accumulation.
       lb -= 1.0f / 512.0f;
+      // strictly below lb (and below +0 when lb is +0), so that the sign of
+      // v - lb_below is clear exactly when v >= lb_below
+      const float lb_below = lb - fabsf(lb) * 0x1p-20f - 0x1p-126f;
 
-      // ---- pass 2: full-precision scores; keep only those >= lb ----
+      // ---- pass 2: full-precision scores; keep those >= lb (a superset) ----
       TopList<KMAX> top;
       top.init();
       int ncand = 0;
@@ -473,9 +476,15 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
           tmem_ld32_async(taddr + part * 32, v);
           tmem_wait();
           if (part == kColsPerWG / 32 - 1) release(g);
-          uint32_t hit = 0;
+          // hit bit j <=> v[j] - lb_below >= 0: the sign bits of the 32
+          // differences, shifted into one word (two instructions a column).
+          // lb_below < lb, so the hits include every score >= lb; a NaN
+          // score may set its bit and is dropped below.
+          uint32_t miss = 0;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) hit |= (__uint_as_float(v[j]) >= lb ? 1u : 0u) << j;
+          for (int j = 31; j >= 0; --j)
+            miss = __funnelshift_l(__float_as_uint(__uint_as_float(v[j]) - lb_below), miss, 1);
+          uint32_t hit = ~miss;
           if (hit) {
             if (ncand + __popc(hit) > kCand) flush();      // the only flush site: keeps code small
             // Hits are rare (about KMAX per row over all of its columns), so
@@ -486,9 +495,11 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
               const int j = __ffs(hit) - 1;
               hit &= hit - 1;
               const float x = __uint_as_float(select32(v, j));
-              cand[ncand * EPI + et] =
-                  rank_key(unit_t ? x : x * inv_t, static_cast<uint32_t>(col_base + part * 32 + j));
-              ++ncand;
+              if (x == x) {
+                cand[ncand * EPI + et] =
+                    rank_key(unit_t ? x : x * inv_t, static_cast<uint32_t>(col_base + part * 32 + j));
+                ++ncand;
+              }
             }
           }
         }
