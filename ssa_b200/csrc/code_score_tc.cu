@@ -169,6 +169,25 @@ __device__ __forceinline__ uint32_t select32(const uint32_t (&v)[32], int j) {
   return (j & 16) ? w[1] : w[0];
 }
 
+// a[0..N) in descending order: bitonic network, fully unrolled (N a power of two).
+template <int N>
+__device__ __forceinline__ void sort_desc(float (&a)[N]) {
+#pragma unroll
+  for (int k = 2; k <= N; k <<= 1)
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1)
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        const int l = i ^ j;
+        if (l > i) {
+          const float x = a[i], y = a[l];
+          const bool desc = (i & k) == 0;
+          a[i] = desc ? fmaxf(x, y) : fminf(x, y);
+          a[l] = desc ? fminf(x, y) : fmaxf(x, y);
+        }
+      }
+}
+
 // Byte offset of element k of row r in a K-major SWIZZLE_NONE image whose K
 // groups are LBO bytes apart.
 __device__ __forceinline__ uint32_t img_off(int r, int kgroup, int lbo) {
@@ -186,11 +205,9 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   unsigned char* a_img = base;                                        // 2 x A_BYTES
   unsigned char* b_img = a_img + 2 * G::A_BYTES;                      // kStages x B_BYTES
-  // [kCand][EPI] pass-2 candidate keys; the same bytes hold the pass-1 kept
-  // values ([32][EPI] floats) and, after the last flush, the merge lists
-  // ([kEpiWG-1][kM][KMAX] keys).
+  // [kCand][EPI] pass-2 candidate keys; after the last flush the same bytes
+  // hold the merge lists ([kEpiWG-1][kM][KMAX] keys).
   uint64_t* cand = reinterpret_cast<uint64_t*>(b_img + kStages * G::B_BYTES);
-  float* kept = reinterpret_cast<float*>(cand);
   uint64_t* merge_k = cand;
   __half* lists = reinterpret_cast<__half*>(cand + kCand * EPI);     // [kEpiWG][kM][KMAX] bound lists
   uint64_t* bars = reinterpret_cast<uint64_t*>(lists + kEpiWG * kM * KMAX);
@@ -414,25 +431,29 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
       // the two lists of a row meet in shared memory (rounded down to f16,
       // which only lowers the bound), and both threads take the KMAX-th
       // largest of their union.
-#pragma unroll
-      for (int j = 0; j < 32; ++j) kept[j * EPI + et] = m1[j];
       {
-        float best[KMAX];
-#pragma unroll
-        for (int t = 0; t < KMAX; ++t) best[t] = -INFINITY;
-#pragma unroll 1
-        for (int u = 0; u < 32; ++u) {
-          float c = kept[u * EPI + et];
-#pragma unroll
-          for (int t = 0; t < KMAX; ++t) {
-            const float hi = fmaxf(best[t], c);
-            c = fminf(best[t], c);
-            best[t] = hi;
-          }
-        }
         __half* mine = lists + (wg * kM + r) * KMAX;
+        if constexpr (KMAX >= 16) {
+          sort_desc(m1);                             // in registers: 15 compare-exchange stages
 #pragma unroll
-        for (int t = 0; t < KMAX; ++t) mine[t] = __float2half_rd(best[t]);
+          for (int t = 0; t < KMAX; ++t) mine[t] = __float2half_rd(m1[t]);
+        } else {
+          float best[KMAX];
+#pragma unroll
+          for (int t = 0; t < KMAX; ++t) best[t] = -INFINITY;
+#pragma unroll
+          for (int u = 0; u < 32; ++u) {
+            float c = m1[u];
+#pragma unroll
+            for (int t = 0; t < KMAX; ++t) {
+              const float hi = fmaxf(best[t], c);
+              c = fminf(best[t], c);
+              best[t] = hi;
+            }
+          }
+#pragma unroll
+          for (int t = 0; t < KMAX; ++t) mine[t] = __float2half_rd(best[t]);
+        }
       }
       if (!epi_sync(m_bar + 8 * (msync & 1), static_cast<uint32_t>((msync >> 1) & 1))) { fail(); break; }
       ++msync;
@@ -517,11 +538,26 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
       if (!epi_sync(m_bar + 8 * (msync & 1), static_cast<uint32_t>((msync >> 1) & 1))) { fail(); break; }
       ++msync;
       if (wg == 0) {
-#pragma unroll 1
-        for (int u = 0; u < (kEpiWG - 1) * KMAX; ++u) {
-          const uint64_t kv = merge_k[((u / KMAX) * kM + r) * KMAX + (u % KMAX)];
-          if (kv > top.key[KMAX - 1]) top.insert_key(kv);
+        // top-KMAX of two descending lists of distinct keys: the larger of
+        // a[t] and b[KMAX-1-t] forms a bitonic sequence holding exactly the
+        // KMAX largest; log2(KMAX) half-cleaner stages sort it
+        const uint64_t* other = merge_k + static_cast<int64_t>(r) * KMAX;
+#pragma unroll
+        for (int t = 0; t < KMAX; ++t) {
+          const uint64_t b = other[KMAX - 1 - t];
+          top.key[t] = top.key[t] > b ? top.key[t] : b;
         }
+#pragma unroll
+        for (int j = KMAX / 2; j > 0; j >>= 1)
+#pragma unroll
+          for (int t = 0; t < KMAX; ++t) {
+            const int l = t ^ j;
+            if (l > t) {
+              const uint64_t x = top.key[t], y = top.key[l];
+              top.key[t] = x > y ? x : y;
+              top.key[l] = x > y ? y : x;
+            }
+          }
         const int64_t bh = tile / p.tiles_per_head;
         const int64_t i = (tile % p.tiles_per_head) * kM + r;
         if (i < p.n_rows) {
@@ -581,9 +617,8 @@ __global__ void codebook_image_kernel(const float* cbn, unsigned char* img, int6
 template <int DS>
 size_t smem_bytes(int kmax) {
   using G = Geo<DS>;
-  const size_t shared = std::max<size_t>({static_cast<size_t>(kCand) * 32 * kEpiWarps * 8,
-                                          static_cast<size_t>(32) * 32 * kEpiWarps * 4,
-                                          static_cast<size_t>(kEpiWG - 1) * kM * kmax * 8});
+  const size_t shared = std::max<size_t>(static_cast<size_t>(kCand) * 32 * kEpiWarps * 8,
+                                         static_cast<size_t>(kEpiWG - 1) * kM * kmax * 8);
   return 1024 + 2 * G::A_BYTES + kStages * G::B_BYTES + shared + static_cast<size_t>(kEpiWG) * kM * kmax * 2 +
          (2 * kStages + 8) * 8 + 16;
 }
