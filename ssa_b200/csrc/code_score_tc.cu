@@ -43,6 +43,7 @@ namespace tc {
 constexpr int kM = 128;
 constexpr int kN = 256;
 constexpr int kStages = 2;
+constexpr int kBufs = 512 / kN;   // TMEM accumulator buffers (all 512 columns)
 constexpr int kCand = 32;          // pass-2 candidates buffered per thread (one full batch)
 constexpr int kEpiWG = 2;
 constexpr int kEpiWarps = 4 * kEpiWG;
@@ -211,14 +212,14 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
   uint64_t* merge_k = cand;
   __half* lists = reinterpret_cast<__half*>(cand + kCand * EPI);     // [kEpiWG][kM][KMAX] bound lists
   uint64_t* bars = reinterpret_cast<uint64_t*>(lists + kEpiWG * kM * KMAX);
-  // barriers: b_full[kStages], b_empty[kStages], t_full[2], t_empty[2], a_ready[2], m_bar[2]
+  // barriers: b_full[kStages], b_empty[kStages], t_full[kBufs], t_empty[kBufs], a_ready[2], m_bar[2]
   const uint32_t b_full = smem_u32(bars);
   const uint32_t b_empty = b_full + 8 * kStages;
   const uint32_t t_full = b_empty + 8 * kStages;
-  const uint32_t t_empty = t_full + 16;
-  const uint32_t a_ready = t_empty + 16;
+  const uint32_t t_empty = t_full + 8 * kBufs;
+  const uint32_t a_ready = t_empty + 8 * kBufs;
   const uint32_t m_bar = a_ready + 16;           // epilogue-only barriers
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 8);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 2 * kBufs + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
@@ -230,9 +231,11 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
       mbar_init(b_full + 8 * s, 1);
       mbar_init(b_empty + 8 * s, 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kBufs; ++b) {
       mbar_init(t_full + 8 * b, 1);
       mbar_init(t_empty + 8 * b, kEpiWarps);
+    }
+    for (int b = 0; b < 2; ++b) {
       mbar_init(a_ready + 8 * b, kEpiWarps);
       mbar_init(m_bar + 8 * b, kEpiWarps);
     }
@@ -241,7 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(2 * kN));
+                 "r"(kBufs * kN));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   fence_before();
@@ -302,9 +305,9 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
           const int ksteps = pass == 0 ? HI_KSTEPS : G::KSTEPS;
           for (int c = 0; c < chunks; ++c, ++g) {
             const int s = static_cast<int>(g % kStages);
-            const int buf = static_cast<int>(g & 1);
+            const int buf = static_cast<int>(g % kBufs);
             if (*abort_flag || !mbar_wait(b_full + 8 * s, static_cast<uint32_t>((g / kStages) & 1)) ||
-                !mbar_wait(t_empty + 8 * buf, static_cast<uint32_t>(((g >> 1) & 1) ^ 1))) {
+                !mbar_wait(t_empty + 8 * buf, static_cast<uint32_t>(((g / kBufs) & 1) ^ 1))) {
               fail();
               stop = true;
               break;
@@ -325,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
       }
       if (issued) {   // the last commit covers every MMA issued: wait before TMEM is freed
         const int64_t r = g - 1;
-        mbar_wait(t_full + 8 * (r & 1), static_cast<uint32_t>((r >> 1) & 1));
+        mbar_wait(t_full + 8 * (r % kBufs), static_cast<uint32_t>((r / kBufs) & 1));
       }
     }
   } else {
@@ -383,8 +386,8 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
 
     // wait for accumulator chunk g and return its TMEM address for this thread
     auto acquire = [&](int64_t gg, uint32_t& taddr) -> bool {
-      const int buf = static_cast<int>(gg & 1);
-      if (*abort_flag || !mbar_wait(t_full + 8 * buf, static_cast<uint32_t>((gg >> 1) & 1))) return false;
+      const int buf = static_cast<int>(gg % kBufs);
+      if (*abort_flag || !mbar_wait(t_full + 8 * buf, static_cast<uint32_t>((gg / kBufs) & 1))) return false;
       fence_after();
       taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
               static_cast<uint32_t>(buf * kN + wg * kColsPerWG);
@@ -393,7 +396,7 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
     auto release = [&](int64_t gg) {
       fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(t_empty + 8 * (gg & 1));
+      if (lane == 0) mbar_arrive(t_empty + 8 * (gg % kBufs));
     };
 
     int64_t g = 0, tl = 0;
@@ -580,7 +583,7 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
   __syncthreads();
   if (warp == 1) {
     fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(2 * kN));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kBufs * kN));
   }
 }
 
@@ -620,7 +623,7 @@ size_t smem_bytes(int kmax) {
   const size_t shared = std::max<size_t>(static_cast<size_t>(kCand) * 32 * kEpiWarps * 8,
                                          static_cast<size_t>(kEpiWG - 1) * kM * kmax * 8);
   return 1024 + 2 * G::A_BYTES + kStages * G::B_BYTES + shared + static_cast<size_t>(kEpiWG) * kM * kmax * 2 +
-         (2 * kStages + 8) * 8 + 16;
+         (2 * kStages + 2 * kBufs + 4) * 8 + 16;
 }
 
 }  // namespace tc
