@@ -207,10 +207,10 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
   unsigned char* a_img = base;                                        // 2 x A_BYTES
   unsigned char* b_img = a_img + 2 * G::A_BYTES;                      // kStages x B_BYTES
   // [kCand][EPI] pass-2 candidate keys; after the last flush the same bytes
-  // hold the merge lists ([kEpiWG-1][kM][KMAX] keys).
+  // hold the merge lists ([kEpiWG-1][KMAX][kM] keys, row-minor: conflict-free).
   uint64_t* cand = reinterpret_cast<uint64_t*>(b_img + kStages * G::B_BYTES);
   uint64_t* merge_k = cand;
-  __half* lists = reinterpret_cast<__half*>(cand + kCand * EPI);     // [kEpiWG][kM][KMAX] bound lists
+  __half* lists = reinterpret_cast<__half*>(cand + kCand * EPI);     // [kEpiWG][KMAX][kM] bound lists
   uint64_t* bars = reinterpret_cast<uint64_t*>(lists + kEpiWG * kM * KMAX);
   // barriers: b_full[kStages], b_empty[kStages], t_full[kBufs], t_empty[kBufs], a_ready[2], m_bar[2]
   const uint32_t b_full = smem_u32(bars);
@@ -435,11 +435,11 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
       // which only lowers the bound), and both threads take the KMAX-th
       // largest of their union.
       {
-        __half* mine = lists + (wg * kM + r) * KMAX;
+        __half* mine = lists + wg * KMAX * kM + r;     // element t at mine[t * kM]
         if constexpr (KMAX >= 16) {
           sort_desc(m1);                             // in registers: 15 compare-exchange stages
 #pragma unroll
-          for (int t = 0; t < KMAX; ++t) mine[t] = __float2half_rd(m1[t]);
+          for (int t = 0; t < KMAX; ++t) mine[t * kM] = __float2half_rd(m1[t]);
         } else {
           float best[KMAX];
 #pragma unroll
@@ -455,7 +455,7 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
             }
           }
 #pragma unroll
-          for (int t = 0; t < KMAX; ++t) mine[t] = __float2half_rd(best[t]);
+          for (int t = 0; t < KMAX; ++t) mine[t * kM] = __float2half_rd(best[t]);
         }
       }
       if (!epi_sync(m_bar + 8 * (msync & 1), static_cast<uint32_t>((msync >> 1) & 1))) { fail(); break; }
@@ -465,11 +465,12 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
       // warpgroups evaluate it in the same order, so they get the same value.
       float lb;
       {
-        const __half* la = lists + r * KMAX;
-        const __half* lo = lists + (kM + r) * KMAX;
-        lb = fmaxf(__half2float(la[KMAX - 1]), __half2float(lo[KMAX - 1]));
+        const __half* la = lists + r;
+        const __half* lo = lists + KMAX * kM + r;
+        lb = fmaxf(__half2float(la[(KMAX - 1) * kM]), __half2float(lo[(KMAX - 1) * kM]));
 #pragma unroll
-        for (int t = 1; t < KMAX; ++t) lb = fmaxf(lb, fminf(__half2float(la[t - 1]), __half2float(lo[KMAX - 1 - t])));
+        for (int t = 1; t < KMAX; ++t)
+          lb = fmaxf(lb, fminf(__half2float(la[(t - 1) * kM]), __half2float(lo[(KMAX - 1 - t) * kM])));
       }
       // |a.c - a_hi.c_hi| <= 2^-10 for unit vectors a, c (f16 rounding of each
       // operand, Cauchy-Schwarz); 2^-9 leaves a margin for fp32 accumulation.
@@ -536,7 +537,7 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
       // merge the warpgroups' lists (ranking keys are unique: plain key inserts)
       if (wg > 0) {
 #pragma unroll
-        for (int t = 0; t < KMAX; ++t) merge_k[((wg - 1) * kM + r) * KMAX + t] = top.key[t];
+        for (int t = 0; t < KMAX; ++t) merge_k[((wg - 1) * KMAX + t) * kM + r] = top.key[t];
       }
       if (!epi_sync(m_bar + 8 * (msync & 1), static_cast<uint32_t>((msync >> 1) & 1))) { fail(); break; }
       ++msync;
@@ -544,10 +545,10 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
         // top-KMAX of two descending lists of distinct keys: the larger of
         // a[t] and b[KMAX-1-t] forms a bitonic sequence holding exactly the
         // KMAX largest; log2(KMAX) half-cleaner stages sort it
-        const uint64_t* other = merge_k + static_cast<int64_t>(r) * KMAX;
+        const uint64_t* other = merge_k + r;
 #pragma unroll
         for (int t = 0; t < KMAX; ++t) {
-          const uint64_t b = other[KMAX - 1 - t];
+          const uint64_t b = other[(KMAX - 1 - t) * kM];
           top.key[t] = top.key[t] > b ? top.key[t] : b;
         }
 #pragma unroll

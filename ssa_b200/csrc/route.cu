@@ -224,18 +224,23 @@ __global__ void __launch_bounds__(kRmWarps * kWarp) route_project_mma_kernel(Rou
   const int d = p.d;
   const int ksteps = d / 16;
   const TW* w = static_cast<const TW*>(p.w);
-  for (int t = threadIdx.x; t < ksteps * NT * 3 * kWarp; t += blockDim.x) {
-    const int ln = t % kWarp, term = (t / kWarp) % 3, nt = (t / (3 * kWarp)) % NT, s = t / (3 * kWarp * NT);
+  for (int t = threadIdx.x; t < ksteps * NT * kWarp; t += blockDim.x) {
+    const int ln = t % kWarp, nt = (t / kWarp) % NT, s = t / (kWarp * NT);
     const int n = nt * 8 + ln / 4;
     const int e0 = 32 * (s / 2) + 8 * (ln % 4) + 4 * (s % 2);
-    float part[4];
+    float x[4];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      float x = Elem<TW>::to_f(w[static_cast<int64_t>(n) * d + e0 + u]);
-      for (int tt = 0; tt < term; ++tt) x -= Elem<T>::to_f(Elem<T>::from_f(x));
-      part[u] = x;
+    for (int u = 0; u < 4; ++u) x[u] = Elem<TW>::to_f(w[static_cast<int64_t>(n) * d + e0 + u]);
+#pragma unroll
+    for (int term = 0; term < 3; ++term) {
+      float tv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        tv[u] = Elem<T>::to_f(Elem<T>::from_f(x[u]));     // this term
+        x[u] -= tv[u];                                    // what the next terms carry
+      }
+      wimg[((s * NT + nt) * 3 + term) * kWarp + ln] = make_uint2(pack2<T>(tv[0], tv[1]), pack2<T>(tv[2], tv[3]));
     }
-    wimg[t] = make_uint2(pack2<T>(part[0], part[1]), pack2<T>(part[2], part[3]));
   }
   __syncthreads();
 
