@@ -549,7 +549,8 @@ def run_config5(args):
     3584, 28 query / 4 KV heads of 128 -> GQA group 7, SwiGLU 18944, RMSNorm,
     RoPE base 1e6, q/k/v biases, vocab 152064, random-init bf16 weights) with
     every attention layer replaced by SSA (d_s 32, N_c 4096, b 4, a 16,
-    k 256): per layer CodebookRouter.route + sparse attention on the sm_100a
+    k 256): per layer RoPE + CodebookRouter.route in one call
+    (CodebookRouter.route_rope) and the sparse attention on the sm_100a
     kernels, the dense projections and the MLP as cuBLAS GEMMs.  Inputs are
     batch x n token ids uniform over the vocabulary; the LM head is not run
     (its bf16 logits alone would take 20 GB); the step is the stack's
@@ -604,23 +605,20 @@ def run_config5(args):
         xf = x.float()
         return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)).to(dt) * wt
 
-    def rope(x):                                      # position-indexed rotate-half RoPE
-        x1, x2 = x[..., : hd // 2], x[..., hd // 2:]
-        return x * cos + torch.cat([-x2, x1], dim=-1) * sin
-
     attn_ms = [0.0]
 
     def forward(time_attn=False):
         x = emb[ids]
         for L in layers:
             h = rms(x, L["ln1"])
-            q = rope(F.linear(h, L["wq"], L["bq"]).view(B, n, hq, hd))
-            k = rope(F.linear(h, L["wk"], L["bk"]).view(B, n, hkv, hd))
+            q = F.linear(h, L["wq"], L["bq"]).view(B, n, hq, hd)
+            k = F.linear(h, L["wk"], L["bk"]).view(B, n, hkv, hd)
             v = F.linear(h, L["wv"], L["bv"]).view(B, n, hkv, hd)
             if time_attn:
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record()
-            idx = L["router"].route(q, k, causal=True, index_dtype=torch.int32)[0]
+            # position-indexed rotate-half RoPE, applied by the routing projection
+            idx, q, k = L["router"].route_rope(q, k, cos, sin, causal=True, index_dtype=torch.int32)
             o = ops.sparse_attn(q, k, v, idx, hd ** 0.5, True, 0)
             if time_attn:
                 e1.record()

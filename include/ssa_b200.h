@@ -22,6 +22,8 @@
  *  - ssa_route             CodebookRouter.forward            ssa/router.py:73-149
  *                          (+ _select_candidates / _build_candidate_mask,
  *                             ssa/router.py:151-259)
+ *  - ssa_route_rope        apply_rotary_pos_emb + CodebookRouter.forward
+ *                          (training/train_qwen.py:134-135, ssa/router.py:73-149)
  *  - ssa_code_assign       CodebookRouter.get_code_assignment ssa/router.py:261-275
  *  - ssa_sparse_attn       sparse_exact_attention            ssa/attention.py:12-115
  *  - ssa_sparse_attn_backward  its gradient (the reference differentiates
@@ -147,6 +149,35 @@ ssa_status ssa_route_with_key_codes(const SsaRouteArgs* args, void* workspace,
 ssa_status ssa_route_with_index(const SsaRouteArgs* args, const int32_t* bucket_ptr,
                                 const int32_t* bucket_keys, void* workspace, size_t workspace_bytes,
                                 void* stream);
+
+/* Rotary position embedding applied on load by ssa_route_rope: the
+ * rotate-half form of the Qwen2 path of the reference
+ * (training/train_qwen.py:134-135, transformers' apply_rotary_pos_emb):
+ *   x_rot = x * cos + rotate_half(x) * sin,  rotate_half(x) = [-x2, x1],
+ * evaluated elementwise in the dtype of q and k (each product and the sum
+ * rounded to it, as the PyTorch expression does).  Row i of q (of k) uses
+ * table row q_offset + i (row i). */
+typedef struct {
+  const void* cos;          /* [*, positions, d], dtype of q and k, last dim contiguous */
+  const void* sin;          /* same layout as cos                          */
+  int64_t table_stride_b;   /* elements between sequences; 0 shares one table */
+  int64_t table_stride_n;   /* elements between positions                   */
+  void* q_out;  int64_t q_out_stride_b, q_out_stride_n, q_out_stride_h; /* rotated q [B,n_q,h_q,d] */
+  void* k_out;  int64_t k_out_stride_b, k_out_stride_n, k_out_stride_h; /* rotated k [B,n,h_kv,d]  */
+} SsaRopeArgs;
+
+/* RoPE + CodebookRouter.forward in one call: q and k in `args` are the
+ * projections before RoPE; the routing projection rotates each row as it
+ * loads it, writes the rotated rows to q_out / k_out, and stages 1-2 run on
+ * the rotated tensors, so the result equals ssa_route on the rotated q and k
+ * (bit for bit, with q_out / k_out equal to the PyTorch RoPE expression).
+ * Pass q_out / k_out to ssa_sparse_attn afterwards.  Replaces the separate
+ * apply_rotary_pos_emb of training/train_qwen.py:134-135 ahead of
+ * CodebookRouter.forward (ssa/router.py:73-149).  16-bit q/k with
+ * d in {64, 128} and d_s in {8, 16, 32, 64}; other shapes return
+ * SSA_ERR_UNSUPPORTED.  Workspace: ssa_route_workspace_size(args). */
+ssa_status ssa_route_rope(const SsaRouteArgs* args, const SsaRopeArgs* rope, void* workspace,
+                          size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Sparse exact attention (stage 3)                                          */

@@ -58,6 +58,14 @@ class SsaAttnArgs(ctypes.Structure):
     ]
 
 
+class SsaRopeArgs(ctypes.Structure):
+    _fields_ = [
+        ("cos", _vp), ("sin", _vp), ("table_stride_b", _c_i64), ("table_stride_n", _c_i64),
+        ("q_out", _vp), ("q_out_stride_b", _c_i64), ("q_out_stride_n", _c_i64), ("q_out_stride_h", _c_i64),
+        ("k_out", _vp), ("k_out_stride_b", _c_i64), ("k_out_stride_n", _c_i64), ("k_out_stride_h", _c_i64),
+    ]
+
+
 # exported symbol -> (restype, argtypes)
 SIGNATURES = {
     "ssa_route_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(SsaRouteArgs)]),
@@ -71,6 +79,8 @@ SIGNATURES = {
     "ssa_select_candidates": (ctypes.c_int, [ctypes.POINTER(SsaRouteArgs), _vp, ctypes.c_size_t, _vp]),
     "ssa_route_with_key_codes": (ctypes.c_int, [ctypes.POINTER(SsaRouteArgs), _vp, ctypes.c_size_t, _vp]),
     "ssa_route_with_index": (ctypes.c_int, [ctypes.POINTER(SsaRouteArgs), _vp, _vp, _vp, ctypes.c_size_t, _vp]),
+    "ssa_route_rope": (ctypes.c_int, [ctypes.POINTER(SsaRouteArgs), ctypes.POINTER(SsaRopeArgs), _vp,
+                                      ctypes.c_size_t, _vp]),
     "ssa_sparse_attn_backward": (ctypes.c_int, [ctypes.POINTER(SsaAttnArgs), _vp, _vp, _vp, _vp, _vp]),
     "ssa_status_str": (ctypes.c_char_p, [ctypes.c_int]),
     "ssa_last_error": (ctypes.c_char_p, []),

@@ -166,8 +166,11 @@ cudaError_t score_and_select(const SsaRouteArgs& a, const RouteLayout& L, void* 
   return launch_code_select(sp, st);
 }
 
+// `rope` (optional): rotate q and k on load and write the rotated rows to its
+// q_out / k_out (ssa_route_rope).
 ssa_status run_stage1(const SsaRouteArgs& a, const RouteLayout& L, void* ws, cudaStream_t st,
-                      bool keys, bool queries, int32_t* q_codes, int32_t* k_codes) {
+                      bool keys, bool queries, int32_t* q_codes, int32_t* k_codes,
+                      const SsaRopeArgs* rope = nullptr) {
   using namespace ssa;
   cudaError_t e = launch_codebook_normalize(a.codebook, a.w_dtype, at<float>(ws, L.cb_norm),
                                             static_cast<int64_t>(a.codebook_heads) * a.n_codes, a.d_s, st);
@@ -181,6 +184,12 @@ ssa_status run_stage1(const SsaRouteArgs& a, const RouteLayout& L, void* ws, cud
     RouteProjectParams kp{a.k, a.k_stride_b, a.k_stride_n, a.k_stride_h, a.w_kr,
                           at<float>(ws, L.k_route), static_cast<int64_t>(a.batch) * a.h_kv * a.n, a.n,
                           a.h_kv, 1, a.d, a.d_s};
+    if (rope) {
+      kp.rope_cos = rope->cos; kp.rope_sin = rope->sin;
+      kp.rope_sb = rope->table_stride_b; kp.rope_sn = rope->table_stride_n; kp.pos_offset = 0;
+      kp.x_out = rope->k_out;
+      kp.out_sb = rope->k_out_stride_b; kp.out_sn = rope->k_out_stride_n; kp.out_sh = rope->k_out_stride_h;
+    }
     e = launch_route_project(kp, a.dtype, a.w_dtype, st);
     if (e != cudaSuccess) return cuda_status(e, "route_project(k)");
     e = score_and_select(a, L, ws, at<float>(ws, L.k_route), a.n, a.b, k_codes, st);
@@ -190,6 +199,12 @@ ssa_status run_stage1(const SsaRouteArgs& a, const RouteLayout& L, void* ws, cud
     RouteProjectParams qp{a.q, a.q_stride_b, a.q_stride_n, a.q_stride_h, a.w_qr,
                           at<float>(ws, L.q_route), static_cast<int64_t>(a.batch) * a.h_kv * a.n_q,
                           a.n_q, a.h_kv, a.h_q / a.h_kv, a.d, a.d_s};
+    if (rope) {
+      qp.rope_cos = rope->cos; qp.rope_sin = rope->sin;
+      qp.rope_sb = rope->table_stride_b; qp.rope_sn = rope->table_stride_n; qp.pos_offset = a.q_offset;
+      qp.x_out = rope->q_out;
+      qp.out_sb = rope->q_out_stride_b; qp.out_sn = rope->q_out_stride_n; qp.out_sh = rope->q_out_stride_h;
+    }
     e = launch_route_project(qp, a.dtype, a.w_dtype, st);
     if (e != cudaSuccess) return cuda_status(e, "route_project(q)");
     e = score_and_select(a, L, ws, at<float>(ws, L.q_route), a.n_q, a.a, q_codes, st);
@@ -365,6 +380,43 @@ ssa_status ssa_route(const SsaRouteArgs* args, void* workspace, size_t workspace
   s = run_stage1(*args, L, workspace, st, true, true, qc, kc);
   if (s != SSA_OK) return s;
   return run_stage2(*args, L, workspace, st, qc, kc);
+}
+
+ssa_status ssa_route_rope(const SsaRouteArgs* args, const SsaRopeArgs* rope, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+  ssa_status s = check_route(args, true, true);
+  if (s != SSA_OK) return s;
+  if (!rope) return fail(SSA_ERR_INVALID_ARG, "rope is NULL");
+  if (!ssa::route_project_rope_supported(args->d, args->d_s, args->dtype))
+    return fail(SSA_ERR_UNSUPPORTED, "route_rope needs 16-bit q/k, head_dim 64 or 128 and route_dim 8/16/32/64");
+  if (!rope->cos || !rope->sin || !rope->q_out || !rope->k_out)
+    return fail(SSA_ERR_INVALID_ARG, "cos / sin / q_out / k_out is NULL");
+  if (rope->table_stride_b < 0 || rope->table_stride_n < args->d)
+    return fail(SSA_ERR_INVALID_ARG, "bad RoPE table strides");
+  if (!aligned16(rope->cos) || !aligned16(rope->sin) || !stride16(rope->table_stride_b, args->dtype) ||
+      !stride16(rope->table_stride_n, args->dtype))
+    return fail(SSA_ERR_ALIGNMENT, "RoPE tables must be 16-byte aligned with 16-byte strides");
+  if (!aligned16(rope->q_out) || !aligned16(rope->k_out) || !stride16(rope->q_out_stride_b, args->dtype) ||
+      !stride16(rope->q_out_stride_n, args->dtype) || !stride16(rope->q_out_stride_h, args->dtype) ||
+      !stride16(rope->k_out_stride_b, args->dtype) || !stride16(rope->k_out_stride_n, args->dtype) ||
+      !stride16(rope->k_out_stride_h, args->dtype))
+    return fail(SSA_ERR_ALIGNMENT, "q_out / k_out must be 16-byte aligned with 16-byte strides");
+  const RouteLayout L = route_layout(*args);
+  if (!workspace || workspace_bytes < L.total)
+    return fail(SSA_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", L.total, workspace_bytes);
+  if (args->batch == 0 || args->n_q == 0) return SSA_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int32_t* qc = args->q_codes ? args->q_codes : at<int32_t>(workspace, L.q_codes);
+  int32_t* kc = args->k_codes ? args->k_codes : at<int32_t>(workspace, L.k_codes);
+  s = run_stage1(*args, L, workspace, st, true, true, qc, kc, rope);
+  if (s != SSA_OK) return s;
+  // stage 2 re-scores with the rotated rows
+  SsaRouteArgs r = *args;
+  r.q = rope->q_out;
+  r.q_stride_b = rope->q_out_stride_b; r.q_stride_n = rope->q_out_stride_n; r.q_stride_h = rope->q_out_stride_h;
+  r.k = rope->k_out;
+  r.k_stride_b = rope->k_out_stride_b; r.k_stride_n = rope->k_out_stride_n; r.k_stride_h = rope->k_out_stride_h;
+  return run_stage2(r, L, workspace, st, qc, kc);
 }
 
 ssa_status ssa_route_with_key_codes(const SsaRouteArgs* args, void* workspace, size_t workspace_bytes,

@@ -17,7 +17,16 @@ struct RouteProjectParams {
   float* out;              // [rows, d_s] L2-normalised route vectors
   int64_t rows, n_rows;
   int h_kv, group, d, d_s;
+  // Optional rotate-half RoPE on load (tensor-core path only): row i of x is
+  // rotated with table row pos_offset + i of rope_cos / rope_sin (dtype of x)
+  // and written to x_out before it is projected.
+  const void* rope_cos = nullptr;
+  const void* rope_sin = nullptr;
+  int64_t rope_sb = 0, rope_sn = 0, pos_offset = 0;
+  void* x_out = nullptr;
+  int64_t out_sb = 0, out_sn = 0, out_sh = 0;
 };
+bool route_project_rope_supported(int d, int d_s, ssa_dtype xt);
 
 // K1: codebook scoring + top-kk selection.  Route rows in (bat, h, i) order.
 struct CodeSelectParams {

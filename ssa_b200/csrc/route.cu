@@ -218,7 +218,43 @@ __global__ void __launch_bounds__(kRpThreads) route_project_kernel(RouteProjectP
 constexpr int kRmWarps = 4;
 constexpr int kRmMT = 2;           // m tiles (16 rows) per warp
 
-template <typename T, typename TW, int NT>
+// Rotate-half RoPE of 8 elements of the first half (lo) and their partners
+// d/2 further on (hi), evaluated as the PyTorch expression
+// x * cos + cat(-x2, x1) * sin in the 16-bit dtype T: each product and the sum
+// rounded to T.
+template <typename T>
+__device__ __forceinline__ void rope8(uint4& lo, uint4& hi, const uint4 c_lo, const uint4 c_hi, const uint4 s_lo,
+                                      const uint4 s_hi) {
+  auto r = [](float x) { return Elem<T>::to_f(Elem<T>::from_f(x)); };
+  auto unpack = [](const uint4 v, float (&f)[8]) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const T* h = reinterpret_cast<const T*>(&w[i]);
+      f[2 * i] = Elem<T>::to_f(h[0]);
+      f[2 * i + 1] = Elem<T>::to_f(h[1]);
+    }
+  };
+  float a[8], b[8], cl[8], ch[8], sl[8], sh[8];
+  unpack(lo, a); unpack(hi, b); unpack(c_lo, cl); unpack(c_hi, ch); unpack(s_lo, sl); unpack(s_hi, sh);
+  uint32_t ol[4], oh[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float xl[2], xh[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int e = 2 * i + u;
+      xl[u] = r(r(a[e] * cl[e]) + r(-b[e] * sl[e]));
+      xh[u] = r(r(b[e] * ch[e]) + r(a[e] * sh[e]));
+    }
+    ol[i] = pack2<T>(xl[0], xl[1]);
+    oh[i] = pack2<T>(xh[0], xh[1]);
+  }
+  lo = make_uint4(ol[0], ol[1], ol[2], ol[3]);
+  hi = make_uint4(oh[0], oh[1], oh[2], oh[3]);
+}
+
+template <typename T, typename TW, int NT, bool ROPE>
 __global__ void __launch_bounds__(kRmWarps * kWarp) route_project_mma_kernel(RouteProjectParams p) {
   extern __shared__ __align__(16) uint2 wimg[];          // [d/16][NT][3][32]
   const int d = p.d;
@@ -253,6 +289,7 @@ __global__ void __launch_bounds__(kRmWarps * kWarp) route_project_mma_kernel(Rou
        task += static_cast<int64_t>(gridDim.x) * kRmWarps) {
     // this thread's rows: m tile mt, half hh -> row task*32 + 16 mt + 8 hh + gq
     const T* base[kRmMT][2];
+    int64_t tab[kRmMT][2], obase[kRmMT][2];      // RoPE table row and output row offsets
     bool ok[kRmMT][2];
 #pragma unroll
     for (int mt = 0; mt < kRmMT; ++mt)
@@ -266,6 +303,10 @@ __global__ void __launch_bounds__(kRmWarps * kWarp) route_project_mma_kernel(Rou
         const int64_t bat = bh / p.h_kv;
         base[mt][hh] = src + bat * p.stride_b + i * p.stride_n + static_cast<int64_t>(h) * p.group * p.stride_h +
                        8 * qp;
+        if constexpr (ROPE) {
+          tab[mt][hh] = bat * p.rope_sb + (p.pos_offset + i) * p.rope_sn + 8 * qp;
+          obase[mt][hh] = bat * p.out_sb + i * p.out_sn + static_cast<int64_t>(h) * p.group * p.out_sh + 8 * qp;
+        }
       }
     float acc[kRmMT][NT][4];
 #pragma unroll
@@ -290,6 +331,37 @@ __global__ void __launch_bounds__(kRmWarps * kWarp) route_project_mma_kernel(Rou
                 raw[cc][mt][hh] = __ldg(reinterpret_cast<const uint4*>(
                     base[mt][hh] + static_cast<int64_t>(gg) * p.stride_h + 32 * (c0 + cc)));
             }
+        if constexpr (ROPE) {
+          // d is 64 or 128 here, so this pass holds every chunk of the rows:
+          // chunk cc pairs with chunk cc + d/64 (elements e and e + d/2)
+          const T* tcos = static_cast<const T*>(p.rope_cos);
+          const T* tsin = static_cast<const T*>(p.rope_sin);
+          T* xo = static_cast<T*>(p.x_out);
+#pragma unroll
+          for (int mt = 0; mt < kRmMT; ++mt)
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              if (!ok[mt][hh]) continue;
+              const T* cr = tcos + tab[mt][hh];
+              const T* sr = tsin + tab[mt][hh];
+              T* orow = xo + obase[mt][hh] + static_cast<int64_t>(gg) * p.out_sh;
+              auto pair = [&](uint4& lo, uint4& hi, int clo, int chi) {
+                const uint4 c_lo = __ldg(reinterpret_cast<const uint4*>(cr + 32 * clo));
+                const uint4 c_hi = __ldg(reinterpret_cast<const uint4*>(cr + 32 * chi));
+                const uint4 s_lo = __ldg(reinterpret_cast<const uint4*>(sr + 32 * clo));
+                const uint4 s_hi = __ldg(reinterpret_cast<const uint4*>(sr + 32 * chi));
+                rope8<T>(lo, hi, c_lo, c_hi, s_lo, s_hi);
+                *reinterpret_cast<uint4*>(orow + 32 * clo) = lo;
+                *reinterpret_cast<uint4*>(orow + 32 * chi) = hi;
+              };
+              if (d == 128) {
+                pair(raw[0][mt][hh], raw[2][mt][hh], 0, 2);
+                pair(raw[1][mt][hh], raw[3][mt][hh], 1, 3);
+              } else {
+                pair(raw[0][mt][hh], raw[1][mt][hh], 0, 1);
+              }
+            }
+        }
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc) {
           if (c0 + cc >= d / 32) break;
@@ -442,7 +514,7 @@ __global__ void select_from_scores_kernel(const float* scores, int64_t rows, int
 // ---------------------------------------------------------------------------
 template <typename T, typename TW, int NT>
 static cudaError_t launch_route_project_mma_t(const RouteProjectParams& p, int sms, cudaStream_t st) {
-  auto kern = route_project_mma_kernel<T, TW, NT>;
+  auto kern = p.rope_cos ? route_project_mma_kernel<T, TW, NT, true> : route_project_mma_kernel<T, TW, NT, false>;
   const size_t smem = static_cast<size_t>(p.d / 16) * NT * 3 * kWarp * sizeof(uint2);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
@@ -474,9 +546,17 @@ static bool route_project_mma_ok(const RouteProjectParams& p, ssa_dtype xt) {
          (p.d_s == 8 || p.d_s == 16 || p.d_s == 32 || p.d_s == 64);
 }
 
+// RoPE on load: the tensor-core projection with all of a row's chunks in one
+// pass (d = 64 or 128).
+bool route_project_rope_supported(int d, int d_s, ssa_dtype xt) {
+  return (xt == SSA_BF16 || xt == SSA_F16) && (d == 64 || d == 128) &&
+         (d_s == 8 || d_s == 16 || d_s == 32 || d_s == 64);
+}
+
 cudaError_t launch_route_project(const RouteProjectParams& p, ssa_dtype xt, ssa_dtype wt,
                                  cudaStream_t st) {
   if (p.rows == 0) return cudaSuccess;
+  if (p.rope_cos && !route_project_rope_supported(p.d, p.d_s, xt)) return cudaErrorInvalidValue;
   if (route_project_mma_ok(p, xt)) {
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);

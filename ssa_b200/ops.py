@@ -144,6 +144,90 @@ def _route_fake(q, k, w_qr, w_kr, codebook, a, b, top_k, causal, temperature, q_
 
 
 # ---------------------------------------------------------------------------
+# route_rope: rotate-half RoPE fused into the routing projection
+# ---------------------------------------------------------------------------
+def _rope_table(t: torch.Tensor, B: int, d: int) -> torch.Tensor:
+    """``cos`` / ``sin`` as ``[1 or B, positions, d]`` with a contiguous last
+    dimension; accepts ``[positions, d]``, ``[1|B, positions, d]`` and the
+    head-broadcast forms ``[1|B, positions, 1, d]`` / ``[1|B, 1, positions, d]``."""
+    if t.dim() == 4:
+        if t.shape[2] == 1:
+            t = t[:, :, 0]
+        elif t.shape[1] == 1:
+            t = t[:, 0]
+        else:
+            raise ValueError(f"RoPE table of shape {tuple(t.shape)} is not broadcast over heads")
+    if t.dim() == 2:
+        t = t.unsqueeze(0)
+    if t.dim() != 3 or t.shape[-1] != d or t.shape[0] not in (1, B):
+        raise ValueError(f"RoPE table of shape {tuple(t.shape)} does not fit batch {B}, head_dim {d}")
+    return _last_contig(t)
+
+
+@torch.library.custom_op("ssa_b200::route_rope", mutates_args=())
+def route_rope(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, w_qr: torch.Tensor,
+               w_kr: torch.Tensor, codebook: torch.Tensor, a: int, b: int, top_k: int, causal: bool,
+               temperature: float, q_offset: int, index_i64: bool
+               ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """RoPE (rotate-half, ``x * cos + cat(-x2, x1) * sin`` in the dtype of q/k)
+    applied to ``q [B, n_q, h_q, d]`` and ``k [B, n, h_kv, d]`` inside the
+    routing projection, then stages 1-2 on the rotated rows.  Query row i uses
+    table position ``q_offset + i``.  Returns ``(indices, q_codes, k_codes,
+    cand_counts, q_rot, k_rot)``."""
+    dev = _require_cuda(q, k, cos, sin, w_qr, w_kr, codebook)
+    q, k = _last_contig(q), _last_contig(k)
+    if cos.dtype != q.dtype or sin.dtype != q.dtype:
+        raise ValueError("cos / sin must have the dtype of q and k")
+    B, n_q, _, d = q.shape
+    _, n, h_kv, _ = k.shape
+    cos, sin = _rope_table(cos, B, d), _rope_table(sin, B, d)
+    if cos.shape != sin.shape or cos.stride() != sin.stride():
+        raise ValueError("cos and sin must have the same shape and strides")
+    if cos.shape[1] < max(n, q_offset + n_q):
+        raise ValueError(f"RoPE tables cover {cos.shape[1]} positions, {max(n, q_offset + n_q)} needed")
+    w_qr, w_kr, codebook = _prep_weights(w_qr, w_kr, codebook, k.dtype)
+    indices = torch.empty((B, n_q, h_kv, top_k), dtype=torch.int64 if index_i64 else torch.int32,
+                          device=dev)
+    q_codes = torch.empty((B, n_q, h_kv, a), dtype=torch.int32, device=dev)
+    k_codes = torch.empty((B, n, h_kv, b), dtype=torch.int32, device=dev)
+    counts = torch.empty((B, n_q, h_kv), dtype=torch.int32, device=dev)
+    q_rot, k_rot = torch.empty_like(q, memory_format=torch.contiguous_format), \
+        torch.empty_like(k, memory_format=torch.contiguous_format)
+    args = route_args(q, k, w_qr, w_kr, codebook, a, b, top_k, causal, temperature, q_offset,
+                      indices, index_i64, q_codes, k_codes, counts)
+    rope = L.SsaRopeArgs()
+    rope.cos, rope.sin = cos.data_ptr(), sin.data_ptr()
+    rope.table_stride_b = cos.stride(0) if cos.shape[0] > 1 else 0
+    rope.table_stride_n = cos.stride(1)
+    rope.q_out = q_rot.data_ptr()
+    rope.q_out_stride_b, rope.q_out_stride_n, rope.q_out_stride_h = q_rot.stride(0), q_rot.stride(1), q_rot.stride(2)
+    rope.k_out = k_rot.data_ptr()
+    rope.k_out_stride_b, rope.k_out_stride_n, rope.k_out_stride_h = k_rot.stride(0), k_rot.stride(1), k_rot.stride(2)
+    check = _checked() and not torch.cuda.is_current_stream_capturing()
+    status = torch.zeros(1, dtype=torch.int32, device=dev) if check else None
+    args.status = _ptr(status)
+    ws = workspace(args, dev)
+    with torch.cuda.device(dev):
+        L.check("ssa_route_rope", L.lib().ssa_route_rope(ctypes.byref(args), ctypes.byref(rope), ws.data_ptr(),
+                                                         ws.numel(), _stream(dev)))
+    if status is not None and int(status.item()) & L.SSA_DEVICE_TIMEOUT:
+        raise RuntimeError("ssa_route_rope: a device pipeline wait timed out; results are undefined")
+    return indices, q_codes, k_codes, counts, q_rot, k_rot
+
+
+@route_rope.register_fake
+def _route_rope_fake(q, k, cos, sin, w_qr, w_kr, codebook, a, b, top_k, causal, temperature, q_offset, index_i64):
+    B, n_q, _, _ = q.shape
+    _, n, h_kv, _ = k.shape
+    return (q.new_empty((B, n_q, h_kv, top_k), dtype=torch.int64 if index_i64 else torch.int32),
+            q.new_empty((B, n_q, h_kv, a), dtype=torch.int32),
+            q.new_empty((B, n, h_kv, b), dtype=torch.int32),
+            q.new_empty((B, n_q, h_kv), dtype=torch.int32),
+            torch.empty_like(q, memory_format=torch.contiguous_format),
+            torch.empty_like(k, memory_format=torch.contiguous_format))
+
+
+# ---------------------------------------------------------------------------
 # route_with_key_codes
 # ---------------------------------------------------------------------------
 @torch.library.custom_op("ssa_b200::route_with_key_codes", mutates_args=())

@@ -74,6 +74,27 @@ class CodebookRouter(nn.Module):
                              self.codes_per_query, self.codes_per_key, self.top_k, bool(causal),
                              float(self.temperature), int(q_offset), index_dtype == torch.int64)
 
+    def route_rope(self, q_full: torch.Tensor, k_full: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                   causal: bool = True, q_offset: int = 0, index_dtype: torch.dtype = torch.int64):
+        """RoPE + routing in one call, for the Qwen2 path of the reference
+        (``training/train_qwen.py:134-135`` rotates with
+        ``apply_rotary_pos_emb`` before the router): ``q [B, n_q, h_q, d]`` and
+        ``k [B, n, h_kv, d]`` before RoPE, ``cos`` / ``sin`` the position
+        tables (``[positions, d]``, ``[1|B, positions, d]`` or head-broadcast
+        4-D forms, dtype of q/k).  The routing projection rotates each row as it
+        loads it (``x * cos + rotate_half(x) * sin``, rounded as that PyTorch
+        expression rounds) and writes the rotated rows out ->
+        ``(indices [B, n_q, h_kv, k], q_rot, k_rot)``; attend with
+        ``q_rot`` / ``k_rot``.  16-bit q/k, head_dim 64 or 128."""
+        if q_full.shape[-2] % k_full.shape[-2]:
+            raise ValueError("num_q_heads must be divisible by num_kv_heads")
+        with torch.no_grad():
+            idx, _, _, _, q_rot, k_rot = ops.route_rope(
+                q_full, k_full, cos, sin, self.W_qr.weight, self.W_kr.weight, self.codebook,
+                self.codes_per_query, self.codes_per_key, self.top_k, bool(causal), float(self.temperature),
+                int(q_offset), index_dtype == torch.int64)
+        return idx, q_rot, k_rot
+
     def key_codes(self, k_full: torch.Tensor) -> torch.Tensor:
         """Batched key codes ``[B, n, h_kv, b]`` int32 of ``k [B, n, h_kv, d]``
         (the input :meth:`route_with_key_codes` takes)."""

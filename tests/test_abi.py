@@ -59,7 +59,8 @@ def _c_layout(struct: str, fields):
     return vals[0], vals[1:]
 
 
-@pytest.mark.parametrize("cls,name", [(L.SsaRouteArgs, "SsaRouteArgs"), (L.SsaAttnArgs, "SsaAttnArgs")])
+@pytest.mark.parametrize("cls,name", [(L.SsaRouteArgs, "SsaRouteArgs"), (L.SsaAttnArgs, "SsaAttnArgs"),
+                                      (L.SsaRopeArgs, "SsaRopeArgs")])
 def test_ctypes_structs_match_c_layout(cls, name):
     fields = [f for f, _ in cls._fields_]
     size, offsets = _c_layout(name, fields)
@@ -134,3 +135,34 @@ def test_select_from_scores_argument_errors(lib):
 def test_status_strings(lib):
     for code in range(7):
         assert lib.ssa_status_str(code)
+
+
+def _rope_args(**over):
+    r = L.SsaRopeArgs()
+    vals = dict(cos=0x7000, sin=0x8000, table_stride_b=0, table_stride_n=64,
+                q_out=0x9000, q_out_stride_b=64 * 8 * 64, q_out_stride_n=8 * 64, q_out_stride_h=64,
+                k_out=0xa000, k_out_stride_b=64 * 2 * 64, k_out_stride_n=2 * 64, k_out_stride_h=64)
+    vals.update(over)
+    for kk, v in vals.items():
+        setattr(r, kk, v)
+    return r
+
+
+@pytest.mark.parametrize("route_over,rope_over,code", [
+    ({"dtype": L.SSA_F32}, {}, 2),          # fp32 q/k: no tensor-core projection
+    ({"d": 96, "q_stride_h": 96, "k_stride_h": 96}, {}, 2),   # head_dim not 64/128
+    ({}, {"cos": 0}, 1),
+    ({}, {"k_out": 0}, 1),
+    ({}, {"table_stride_n": 32}, 1),       # rows of the table overlap
+    ({}, {"q_out": 0x9008}, 4),
+    ({}, {"table_stride_n": 68}, 4),
+])
+def test_route_rope_argument_errors(lib, route_over, rope_over, code):
+    a = _route_args(**route_over)
+    r = _rope_args(**rope_over)
+    assert lib.ssa_route_rope(ctypes.byref(a), ctypes.byref(r), None, 0, None) == code
+
+
+def test_route_rope_null_rope_is_an_argument_error(lib):
+    a = _route_args()
+    assert lib.ssa_route_rope(ctypes.byref(a), None, None, 0, None) == 1
