@@ -189,6 +189,22 @@ __device__ __forceinline__ void sort_desc(float (&a)[N]) {
       }
 }
 
+// Insert kv into the descending list key[0..K) (its last entry drops out).
+// Every position is computed from the old list, key'[t] = max(key[t],
+// min(kv, key[t-1])) with key[-1] = +inf, so the dependency depth is two
+// compare-selects rather than a chain through all K positions.
+template <int K>
+__device__ __forceinline__ void insert_desc(uint64_t (&key)[K], uint64_t kv) {
+  uint64_t prev = ~0ull;
+#pragma unroll
+  for (int t = 0; t < K; ++t) {
+    const uint64_t cur = key[t];
+    const uint64_t m = kv < prev ? kv : prev;
+    key[t] = cur > m ? cur : m;
+    prev = cur;
+  }
+}
+
 // Byte offset of element k of row r in a K-major SWIZZLE_NONE image whose K
 // groups are LBO bytes apart.
 __device__ __forceinline__ uint32_t img_off(int r, int kgroup, int lbo) {
@@ -436,27 +452,11 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
       // largest of their union.
       {
         __half* mine = lists + wg * KMAX * kM + r;     // element t at mine[t * kM]
-        if constexpr (KMAX >= 16) {
-          sort_desc(m1);                             // in registers: 15 compare-exchange stages
+        // in registers: 15 stages of independent compare-exchanges (an
+        // insertion of the 32 maxima into a KMAX-list would chain 32 * KMAX)
+        sort_desc(m1);
 #pragma unroll
-          for (int t = 0; t < KMAX; ++t) mine[t * kM] = __float2half_rd(m1[t]);
-        } else {
-          float best[KMAX];
-#pragma unroll
-          for (int t = 0; t < KMAX; ++t) best[t] = -INFINITY;
-#pragma unroll
-          for (int u = 0; u < 32; ++u) {
-            float c = m1[u];
-#pragma unroll
-            for (int t = 0; t < KMAX; ++t) {
-              const float hi = fmaxf(best[t], c);
-              c = fminf(best[t], c);
-              best[t] = hi;
-            }
-          }
-#pragma unroll
-          for (int t = 0; t < KMAX; ++t) mine[t * kM] = __float2half_rd(best[t]);
-        }
+        for (int t = 0; t < KMAX; ++t) mine[t * kM] = __float2half_rd(m1[t]);
       }
       if (!epi_sync(m_bar + 8 * (msync & 1), static_cast<uint32_t>((msync >> 1) & 1))) { fail(); break; }
       ++msync;
@@ -487,7 +487,7 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
 #pragma unroll 1
         for (int t = 0; t < ncand; ++t) {
           const uint64_t kv = cand[t * EPI + et];
-          if (kv > top.key[KMAX - 1]) top.insert_key(kv);
+          if (kv > top.key[KMAX - 1]) insert_desc(top.key, kv);
         }
         ncand = 0;
       };
@@ -503,12 +503,17 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
           if (part == kColsPerWG / 32 - 1) release(g);
           // hit bit j <=> v[j] - lb_below >= 0: the sign bits of the 32
           // differences, shifted into one word (two instructions a column).
-          // lb_below < lb, so the hits include every score >= lb; a NaN
-          // score may set its bit and is dropped below.
-          uint32_t miss = 0;
+          // Four independent 8-bit chains, joined at the end, keep the
+          // dependency depth at 8 shifts instead of 32.  lb_below < lb, so
+          // the hits include every score >= lb; a NaN score may set its bit
+          // and is dropped below.
+          uint32_t mb[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-          for (int j = 31; j >= 0; --j)
-            miss = __funnelshift_l(__float_as_uint(__uint_as_float(v[j]) - lb_below), miss, 1);
+          for (int j = 7; j >= 0; --j)
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              mb[q] = __funnelshift_l(__float_as_uint(__uint_as_float(v[8 * q + j]) - lb_below), mb[q], 1);
+          const uint32_t miss = mb[0] | (mb[1] << 8) | (mb[2] << 16) | (mb[3] << 24);
           uint32_t hit = ~miss;
           if (hit) {
             if (ncand + __popc(hit) > kCand) flush();      // the only flush site: keeps code small

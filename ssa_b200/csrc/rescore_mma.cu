@@ -52,42 +52,59 @@ struct __align__(128) RsMmaSmem {
 
 // Descending bitonic sort of 32*E keys, blocked layout: key[e] of lane l is
 // at position l*E + e, so the stages with partner distance < E compare within
-// a lane and only log2(32) of every log2(32*E) stages shuffle.  The stage
-// loops stay rolled (run-time distances; the in-lane distances E/2 .. 1 are
-// unrolled once): the whole network is a few hundred instructions of code, so
-// the warps of a CTA do not evict one another's instructions.
+// a lane and only log2(32) of every log2(32*E) stages shuffle.  The merge
+// direction of a stage, (position & k2) == 0, depends only on e while
+// k2 < E and only on the lane from k2 = E on, so it is computed once per
+// stage (not per element) and every compare-exchange is one 64-bit compare
+// and two 64-bit selects.  The stage loops from k2 = 2E on stay rolled
+// (run-time distances): the whole network is a few hundred instructions of
+// code, so the warps of a CTA do not evict one another's instructions.
+template <int E>
+__device__ __forceinline__ void cx_desc(uint64_t (&key)[E], int e, int f, bool desc) {
+  const uint64_t x = key[e], y = key[f];
+  const bool sw = (x > y) != desc;           // equal keys: either order
+  key[e] = sw ? y : x;
+  key[f] = sw ? x : y;
+}
+
 template <int E>
 __device__ __forceinline__ void sort_desc_blocked(uint64_t (&key)[E], int lane) {
   constexpr int N = 32 * E;
+  // k2 < E: within each lane, direction fixed by e
+#pragma unroll
+  for (int k2 = 2; k2 < E; k2 <<= 1)
+#pragma unroll
+    for (int jj = k2 >> 1; jj > 0; jj >>= 1)
+#pragma unroll
+      for (int e = 0; e < E; ++e)
+        if ((e ^ jj) > e) cx_desc<E>(key, e, e ^ jj, (e & k2) == 0);
+  // k2 = E: each lane's E keys in the direction of the lane's parity
+  {
+    const bool desc = (lane & 1) == 0;
+#pragma unroll
+    for (int jj = E >> 1; jj > 0; jj >>= 1)
+#pragma unroll
+      for (int e = 0; e < E; ++e)
+        if ((e ^ jj) > e) cx_desc<E>(key, e, e ^ jj, desc);
+  }
+  const int lk = lane * E;
 #pragma unroll 1
-  for (int k2 = 2; k2 <= N; k2 <<= 1) {
+  for (int k2 = 2 * E; k2 <= N; k2 <<= 1) {
+    const bool desc = (lk & k2) == 0;
 #pragma unroll 1
     for (int j = k2 >> 1; j >= E; j >>= 1) {       // partner in lane ^ (j / E)
+      const bool keep_max = desc == ((lk & j) == 0);
 #pragma unroll
       for (int e = 0; e < E; ++e) {
         const uint64_t other = __shfl_xor_sync(0xffffffffu, key[e], j / E);
-        const int pos = lane * E + e;
-        const bool keep_max = ((pos & k2) == 0) == ((pos & j) == 0);
-        const bool gt = key[e] > other;
-        key[e] = (gt == keep_max) ? key[e] : other;
+        key[e] = ((key[e] > other) == keep_max) ? key[e] : other;
       }
     }
 #pragma unroll
-    for (int jj = E >> 1; jj > 0; jj >>= 1) {      // partner in the same lane
-      if (jj <= (k2 >> 1)) {
+    for (int jj = E >> 1; jj > 0; jj >>= 1)        // partner in the same lane
 #pragma unroll
-        for (int e = 0; e < E; ++e) {
-          const int f = e ^ jj;
-          if (f > e) {
-            const bool desc = ((lane * E + e) & k2) == 0;
-            const uint64_t x = key[e], y = key[f];
-            const bool swap = desc ? (x < y) : (x > y);
-            key[e] = swap ? y : x;
-            key[f] = swap ? x : y;
-          }
-        }
-      }
-    }
+      for (int e = 0; e < E; ++e)
+        if ((e ^ jj) > e) cx_desc<E>(key, e, e ^ jj, desc);
   }
 }
 
