@@ -79,7 +79,7 @@ RouteLayout route_layout(const SsaRouteArgs& a) {
   L.bucket_keys = take(static_cast<size_t>(B * hk) * a.n * a.b * 4);
   L.bucket_codes = take(a.b == 4 ? static_cast<size_t>(B * hk) * a.n * 4 * 16 : 0);   // int4 per entry
   L.ovf = take((1 + static_cast<size_t>(B * hk) * a.n_q) * 4);   // overflow count + unit list
-  L.ovf2 = take((1 + static_cast<size_t>(B * hk) * a.n_q) * 4);  // second-tier count + list
+  L.ovf2 = take((2 + static_cast<size_t>(B * hk) * a.n_q) * 4);  // second-tier count, claim counter, list
   L.flags = take(4);                                               // index-validation flag
   L.total = off;
   return L;
@@ -264,7 +264,8 @@ ssa_status run_rescore(const SsaRouteArgs& a, const RouteLayout& L, void* ws, cu
   rp.ovf_count = at<int32_t>(ws, L.ovf);
   rp.ovf_list = at<int32_t>(ws, L.ovf) + 1;
   rp.ovf2_count = at<int32_t>(ws, L.ovf2);
-  rp.ovf2_list = at<int32_t>(ws, L.ovf2) + 1;
+  rp.ovf2_next = at<int32_t>(ws, L.ovf2) + 1;
+  rp.ovf2_list = at<int32_t>(ws, L.ovf2) + 2;
   return cuda_status(launch_rescore(rp, a.dtype, st), "rescore_topk");
 }
 

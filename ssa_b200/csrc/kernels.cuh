@@ -94,7 +94,8 @@ struct RescoreParams {
   int32_t* ovf_count;          // workspace: units left to the general path ...
   int32_t* ovf_list;           // ... and their indices [B * n_q * h_kv]
   int32_t* ovf2_count;         // workspace: units passed from the first warp tier ...
-  int32_t* ovf2_list;          // ... to the second [B * n_q * h_kv]
+  int32_t* ovf2_next;          // ... the next of them a second-tier warp claims ...
+  int32_t* ovf2_list;          // ... and their indices [B * n_q * h_kv]
 };
 
 // A caller-given code->key index that failed validation: the unit's indices

@@ -24,8 +24,9 @@
 //      written in order; filler and zero padding follow.
 // Two tiers: every unit first runs with room for 512 candidates (4 warps per
 // CTA); units with more go to an overflow list that a second launch runs with
-// room for 1024 (4 warps per CTA, persistent over the list).  Units beyond
-// that, or with k > 512, go to the CTA-wide path.
+// room for 1024 (4 warps per CTA, persistent, each warp claiming the next
+// unit of the list).  Units beyond that, or with k > 512, go to the CTA-wide
+// path.
 #include "common.cuh"
 #include "kernels.cuh"
 #include "mma_utils.cuh"
@@ -42,7 +43,8 @@ constexpr int kWalk = 4;            // bucket-walk iterations whose loads are is
 template <int CAP>
 struct __align__(128) RsMmaSmem {
   uint64_t keys[CAP];                          // ranking keys of all candidates
-  uint64_t sel[CAP];                           // kept key indices, then the selected keys
+  // kept key indices (CAP int32), then the selected keys (k <= kMaxSel)
+  uint64_t sel[CAP / 2 > kMaxSel ? CAP / 2 : kMaxSel];
   uint32_t hist[256];
   int32_t qc[32];
   int32_t lo[32];
@@ -311,6 +313,7 @@ __device__ __forceinline__ void rescore_mma_unit(const RescoreParams& p, int64_t
       if (keep[w] && slot < CAP) jlist[slot] = j[w];
       count += __popc(bal);
     }
+    if (count > CAP) break;                     // overflows this tier: no need to walk further
   }
   if (count > CAP || k_eff > kMaxSel) {
     if (lane == 0) out_list[atomicAdd(out_count, 1)] = static_cast<int32_t>(unit);
@@ -467,11 +470,11 @@ __device__ __forceinline__ void rescore_mma_unit(const RescoreParams& p, int64_t
 }
 
 // All units (LIST false) or the units of a list (count read on the device;
-// warps stride over it).
+// each warp claims the next unclaimed unit through a counter).
 template <typename T, int D, int CAP, int UNITS, bool LIST>
 __global__ void __launch_bounds__(UNITS * kWarp) rescore_mma_kernel(RescoreParams p, const int32_t* in_list,
-                                                                    const int32_t* in_count, int32_t* out_list,
-                                                                    int32_t* out_count) {
+                                                                    const int32_t* in_count, int32_t* in_next,
+                                                                    int32_t* out_list, int32_t* out_count) {
   extern __shared__ __align__(128) unsigned char dyn[];
   const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
   RsMmaSmem<CAP>& s = reinterpret_cast<RsMmaSmem<CAP>*>(dyn)[warp];
@@ -480,8 +483,15 @@ __global__ void __launch_bounds__(UNITS * kWarp) rescore_mma_kernel(RescoreParam
     const int64_t units = static_cast<int64_t>(p.batch) * p.n_q * p.h_kv;
     if (wi < units) rescore_mma_unit<T, D, CAP>(p, wi, s, lane, out_list, out_count);
   } else {
-    const int64_t n = *in_count;
-    for (int64_t it = wi; it < n; it += static_cast<int64_t>(gridDim.x) * UNITS) {
+    // units differ in cost by several times: each warp claims the next unit
+    // of the list when it is free (a fixed stride leaves the launch waiting
+    // on the warps that drew the heaviest units)
+    const int n = *in_count;
+    while (true) {
+      int it = 0;
+      if (lane == 0) it = atomicAdd(in_next, 1);
+      it = __shfl_sync(0xffffffffu, it, 0);
+      if (it >= n) break;
       rescore_mma_unit<T, D, CAP>(p, in_list[it], s, lane, out_list, out_count);
       __syncwarp();
     }
@@ -503,20 +513,25 @@ static cudaError_t launch_mma_t(const RescoreParams& p, cudaStream_t st) {
   if (e != cudaSuccess) return e;
   e = cudaMemsetAsync(p.ovf2_count, 0, sizeof(int32_t), st);
   if (e != cudaSuccess) return e;
-  k1<<<static_cast<unsigned>(cdiv(units, U1)), U1 * kWarp, smem1, st>>>(p, nullptr, nullptr, p.ovf2_list,
-                                                                       p.ovf2_count);
-  // tier 2: the overflow units, room for 1024 (4 warps per CTA, three CTAs per
-  // SM); overflow -> the CTA-wide path
+  e = cudaMemsetAsync(p.ovf2_next, 0, sizeof(int32_t), st);
+  if (e != cudaSuccess) return e;
+  k1<<<static_cast<unsigned>(cdiv(units, U1)), U1 * kWarp, smem1, st>>>(p, nullptr, nullptr, nullptr,
+                                                                       p.ovf2_list, p.ovf2_count);
+  // tier 2: the overflow units, room for 1024 (4 warps per CTA, as many CTAs
+  // per SM as fit, warps claiming units from the list); overflow -> the
+  // CTA-wide path
   constexpr int U2 = 4, C2 = 1024;
   const size_t smem2 = sizeof(RsMmaSmem<C2>) * U2;
   auto k2 = rescore_mma_kernel<T, D, C2, U2, true>;
   e = cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem2));
   if (e != cudaSuccess) return e;
-  int dev = 0, sms = 148;
+  int dev = 0, sms = 148, per_sm = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  k2<<<static_cast<unsigned>(sms * 3), U2 * kWarp, smem2, st>>>(p, p.ovf2_list, p.ovf2_count, p.ovf_list,
-                                                                p.ovf_count);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k2, U2 * kWarp, smem2);
+  if (e != cudaSuccess) return e;
+  k2<<<static_cast<unsigned>(sms * (per_sm > 0 ? per_sm : 1)), U2 * kWarp, smem2, st>>>(p, p.ovf2_list, p.ovf2_count, p.ovf2_next,
+                                                                p.ovf_list, p.ovf_count);
   return cudaGetLastError();
 }
 
