@@ -44,8 +44,9 @@ template <int CAP>
 struct __align__(128) RsMmaSmem {
   uint64_t keys[CAP];                          // ranking keys of all candidates
   // kept key indices (CAP int32), then the selected keys (k <= kMaxSel)
+  // (its last 1 KB doubles as the radix-select histogram, and before the walk
+  // as the group-mean query: neither overlaps a live use of sel)
   uint64_t sel[CAP / 2 > kMaxSel ? CAP / 2 : kMaxSel];
-  uint32_t hist[256];
   int32_t qc[32];
   int32_t lo[32];
   int32_t pre[33];
@@ -176,6 +177,7 @@ __device__ __forceinline__ void rescore_mma_unit(const RescoreParams& p, int64_t
   const int k_eff = min(p.top_k, p.n);
   const int32_t* bk = p.bucket_keys + static_cast<int64_t>(bh) * p.n * p.b;
   const int gid = lane >> 2, tig = lane & 3;
+  uint32_t* hist = reinterpret_cast<uint32_t*>(s.sel) + (sizeof(s.sel) / 4 - 256);
 
   // ---- 1a. the query's buckets (causal prefix of each) ----
   int len = 0;
@@ -231,7 +233,7 @@ __device__ __forceinline__ void rescore_mma_unit(const RescoreParams& p, int64_t
     for (int o = CH; o < kWarp; o <<= 1)
 #pragma unroll
       for (int u = 0; u < 8; ++u) x[u] += __shfl_xor_sync(0xffffffffu, x[u], o);
-    float* qs = reinterpret_cast<float*>(s.hist);    // D floats; hist is free until the select
+    float* qs = reinterpret_cast<float*>(hist);      // D floats; sel is free until the walk
     if (lane < CH) {
       const float inv_g = 1.0f / static_cast<float>(p.group);
 #pragma unroll
@@ -365,11 +367,11 @@ __device__ __forceinline__ void rescore_mma_unit(const RescoreParams& p, int64_t
     uint64_t prefix = 0ull, mask = 0ull;
     int need = k_eff;
     for (int shift = 56; shift >= 0; shift -= 8) {
-      for (int b = lane; b < 256; b += kWarp) s.hist[b] = 0u;
+      for (int b = lane; b < 256; b += kWarp) hist[b] = 0u;
       __syncwarp();
       for (int idx = lane; idx < count; idx += kWarp) {
         const uint64_t kv = s.keys[idx];
-        if ((kv & mask) == prefix) atomicAdd(&s.hist[(kv >> shift) & 255u], 1u);
+        if ((kv & mask) == prefix) atomicAdd(&hist[(kv >> shift) & 255u], 1u);
       }
       __syncwarp();
       // lane l owns digits 255-8l .. 248-8l (descending)
@@ -377,7 +379,7 @@ __device__ __forceinline__ void rescore_mma_unit(const RescoreParams& p, int64_t
       uint32_t local = 0;
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
-        cnt[q] = s.hist[255 - 8 * lane - q];
+        cnt[q] = hist[255 - 8 * lane - q];
         local += cnt[q];
       }
       uint32_t inc = local;
@@ -470,9 +472,11 @@ __device__ __forceinline__ void rescore_mma_unit(const RescoreParams& p, int64_t
 }
 
 // All units (LIST false) or the units of a list (count read on the device;
-// each warp claims the next unclaimed unit through a counter).
+// each warp claims the next unclaimed unit through a counter).  Register caps:
+// six CTAs of the first tier per SM (8.5 KB of shared memory per warp; the
+// few bytes it spills cost less than the warps gained), four of the second.
 template <typename T, int D, int CAP, int UNITS, bool LIST>
-__global__ void __launch_bounds__(UNITS * kWarp) rescore_mma_kernel(RescoreParams p, const int32_t* in_list,
+__global__ void __launch_bounds__(UNITS * kWarp, LIST ? 4 : 6) rescore_mma_kernel(RescoreParams p, const int32_t* in_list,
                                                                     const int32_t* in_count, int32_t* in_next,
                                                                     int32_t* out_list, int32_t* out_count) {
   extern __shared__ __align__(128) unsigned char dyn[];
