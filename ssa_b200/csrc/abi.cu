@@ -78,7 +78,7 @@ RouteLayout route_layout(const SsaRouteArgs& a) {
   L.bucket_ptr = take(static_cast<size_t>(B * hk) * (a.n_codes + 1) * 4);
   L.bucket_keys = take(static_cast<size_t>(B * hk) * a.n * a.b * 4);
   L.bucket_codes = take(a.b == 4 ? static_cast<size_t>(B * hk) * a.n * 4 * 16 : 0);   // int4 per entry
-  L.ovf = take((1 + static_cast<size_t>(B * hk) * a.n_q) * 4);   // overflow count + unit list
+  L.ovf = take((2 + static_cast<size_t>(B * hk) * a.n_q) * 4);   // overflow count, claim counter, unit list
   L.ovf2 = take((2 + static_cast<size_t>(B * hk) * a.n_q) * 4);  // second-tier count, claim counter, list
   L.flags = take(4);                                               // index-validation flag
   L.total = off;
@@ -262,7 +262,8 @@ ssa_status run_rescore(const SsaRouteArgs& a, const RouteLayout& L, void* ws, cu
   rp.n_codes = a.n_codes; rp.top_k = a.top_k; rp.causal = a.causal ? 1 : 0;
   rp.cap = rescore_cap(std::min(a.top_k, a.n));
   rp.ovf_count = at<int32_t>(ws, L.ovf);
-  rp.ovf_list = at<int32_t>(ws, L.ovf) + 1;
+  rp.ovf_next = at<int32_t>(ws, L.ovf) + 1;
+  rp.ovf_list = at<int32_t>(ws, L.ovf) + 2;
   rp.ovf2_count = at<int32_t>(ws, L.ovf2);
   rp.ovf2_next = at<int32_t>(ws, L.ovf2) + 1;
   rp.ovf2_list = at<int32_t>(ws, L.ovf2) + 2;

@@ -92,6 +92,7 @@ struct RescoreParams {
   int batch, n, n_q, q_offset, h_kv, group, d, a, b, n_codes, top_k, causal;
   int cap;                     // shared-memory candidate capacity (power of two)
   int32_t* ovf_count;          // workspace: units left to the general path ...
+  int32_t* ovf_next;           // ... the next of them a general-path CTA claims ...
   int32_t* ovf_list;           // ... and their indices [B * n_q * h_kv]
   int32_t* ovf2_count;         // workspace: units passed from the first warp tier ...
   int32_t* ovf2_next;          // ... the next of them a second-tier warp claims ...

@@ -312,17 +312,30 @@ __device__ void rescore_unit_block(const RescoreParams& p, int64_t unit, RsStati
   __syncthreads();   // shared state is reused by the CTA's next unit
 }
 
-// General path: every unit (list == nullptr) or the units listed by the warp
-// kernel (count read on the device).
+// General path: every unit (list == nullptr, one CTA each) or the units
+// listed by the warp kernels (count read on the device; a persistent grid
+// whose CTAs claim the next unclaimed unit through a counter, since the
+// listed units differ in cost by several times).
 template <typename T>
 __global__ void __launch_bounds__(kRsThreads) rescore_block_kernel(RescoreParams p, const int32_t* list,
-                                                                  const int32_t* list_count) {
+                                                                  const int32_t* list_count, int32_t* list_next) {
   __shared__ RsStatic s;
+  __shared__ int claimed;
   extern __shared__ __align__(16) unsigned char dyn[];
-  const int64_t n = list ? static_cast<int64_t>(*list_count)
-                         : static_cast<int64_t>(p.batch) * p.n_q * p.h_kv;
-  for (int64_t it = blockIdx.x; it < n; it += gridDim.x)
-    rescore_unit_block<T>(p, list ? static_cast<int64_t>(list[it]) : it, s, dyn);
+  if (!list) {
+    const int64_t n = static_cast<int64_t>(p.batch) * p.n_q * p.h_kv;
+    for (int64_t it = blockIdx.x; it < n; it += gridDim.x) rescore_unit_block<T>(p, it, s, dyn);
+    return;
+  }
+  const int n = *list_count;
+  while (true) {
+    if (threadIdx.x == 0) claimed = atomicAdd(list_next, 1);
+    __syncthreads();
+    const int it = claimed;
+    __syncthreads();                               // read before thread 0 claims again
+    if (it >= n) break;
+    rescore_unit_block<T>(p, static_cast<int64_t>(list[it]), s, dyn);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -579,10 +592,12 @@ static cudaError_t launch_rescore_t(const RescoreParams& p, cudaStream_t st) {
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   if (std::min(p.top_k, p.n) > kWarpCap || p.ovf_list == nullptr) {
-    rescore_block_kernel<T><<<static_cast<unsigned>(units), kRsThreads, smem, st>>>(p, nullptr, nullptr);
+    rescore_block_kernel<T><<<static_cast<unsigned>(units), kRsThreads, smem, st>>>(p, nullptr, nullptr, nullptr);
     return cudaGetLastError();
   }
   e = cudaMemsetAsync(p.ovf_count, 0, sizeof(int32_t), st);
+  if (e != cudaSuccess) return e;
+  e = cudaMemsetAsync(p.ovf_next, 0, sizeof(int32_t), st);
   if (e != cudaSuccess) return e;
   const ssa_dtype dt = sizeof(T) == 4 ? SSA_F32 : (std::is_same<T, __half>::value ? SSA_F16 : SSA_BF16);
   if (rescore_mma_supported(p, dt)) {
@@ -591,11 +606,14 @@ static cudaError_t launch_rescore_t(const RescoreParams& p, cudaStream_t st) {
   } else {
     rescore_warp_kernel<T><<<static_cast<unsigned>(cdiv(units, kWarpUnits)), kWarpUnits * kWarp, 0, st>>>(p);
   }
-  int dev = 0, sms = 148;
+  int dev = 0, sms = 148, per_sm = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t grid = std::min<int64_t>(units, static_cast<int64_t>(sms) * 4);
-  rescore_block_kernel<T><<<static_cast<unsigned>(grid), kRsThreads, smem, st>>>(p, p.ovf_list, p.ovf_count);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rescore_block_kernel<T>, kRsThreads, smem);
+  if (e != cudaSuccess) return e;
+  const int64_t grid = std::min<int64_t>(units, static_cast<int64_t>(sms) * (per_sm > 0 ? per_sm : 1));
+  rescore_block_kernel<T><<<static_cast<unsigned>(grid), kRsThreads, smem, st>>>(p, p.ovf_list, p.ovf_count,
+                                                                                  p.ovf_next);
   return cudaGetLastError();
 }
 

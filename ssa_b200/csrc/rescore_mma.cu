@@ -430,7 +430,10 @@ __device__ __forceinline__ void rescore_mma_unit(const RescoreParams& p, int64_t
   }
 
   // ---- 4. sort the selected keys, write them; filler; padding ----
-  if (nsel <= 32 * 8) sort_and_write<8>(src, nsel, lane, p, obase);
+  // the network for the smallest power of two >= nsel (4 keys a lane for the
+  // early queries of a causal head, which have few candidates)
+  if (nsel <= 32 * 4) sort_and_write<4>(src, nsel, lane, p, obase);
+  else if (nsel <= 32 * 8) sort_and_write<8>(src, nsel, lane, p, obase);
   else sort_and_write<16>(src, nsel, lane, p, obase);
   auto put = [&](int slot, int32_t jj) {
     if (p.index_i64) static_cast<int64_t*>(p.out)[obase + slot] = jj;
