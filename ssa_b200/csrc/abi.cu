@@ -51,7 +51,7 @@ int rescore_cap(int k_eff) {
 // Workspace regions for a route call.
 struct RouteLayout {
   size_t q_route, k_route, cb_norm, cb_image, q_codes, k_codes, counts, partials, bucket_ptr,
-      bucket_keys, bucket_codes, ovf, ovf2, flags;
+      bucket_keys, bucket_codes, ovf, ovf2, ovf3, flags;
   size_t total;
   int tiles;
   int64_t chunks;
@@ -80,6 +80,7 @@ RouteLayout route_layout(const SsaRouteArgs& a) {
   L.bucket_codes = take(a.b == 4 ? static_cast<size_t>(B * hk) * a.n * 4 * 16 : 0);   // int4 per entry
   L.ovf = take((2 + static_cast<size_t>(B * hk) * a.n_q) * 4);   // overflow count, claim counter, unit list
   L.ovf2 = take((2 + static_cast<size_t>(B * hk) * a.n_q) * 4);  // second-tier count, claim counter, list
+  L.ovf3 = take((2 + static_cast<size_t>(B * hk) * a.n_q) * 4);  // third tier, the same
   L.flags = take(4);                                               // index-validation flag
   L.total = off;
   return L;
@@ -267,6 +268,9 @@ ssa_status run_rescore(const SsaRouteArgs& a, const RouteLayout& L, void* ws, cu
   rp.ovf2_count = at<int32_t>(ws, L.ovf2);
   rp.ovf2_next = at<int32_t>(ws, L.ovf2) + 1;
   rp.ovf2_list = at<int32_t>(ws, L.ovf2) + 2;
+  rp.ovf3_count = at<int32_t>(ws, L.ovf3);
+  rp.ovf3_next = at<int32_t>(ws, L.ovf3) + 1;
+  rp.ovf3_list = at<int32_t>(ws, L.ovf3) + 2;
   return cuda_status(launch_rescore(rp, a.dtype, st), "rescore_topk");
 }
 

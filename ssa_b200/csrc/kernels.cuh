@@ -97,6 +97,9 @@ struct RescoreParams {
   int32_t* ovf2_count;         // workspace: units passed from the first warp tier ...
   int32_t* ovf2_next;          // ... the next of them a second-tier warp claims ...
   int32_t* ovf2_list;          // ... and their indices [B * n_q * h_kv]
+  int32_t* ovf3_count;         // workspace: units passed from the second warp tier to the third,
+  int32_t* ovf3_next;          // the claim counter and
+  int32_t* ovf3_list;          // their indices [B * n_q * h_kv]
 };
 
 // A caller-given code->key index that failed validation: the unit's indices

@@ -22,11 +22,11 @@
 //      key and the top k are compacted;
 //   4. the selected keys are sorted in registers (bitonic, 32*E keys) and
 //      written in order; filler and zero padding follow.
-// Two tiers: every unit first runs with room for 512 candidates (4 warps per
+// Three tiers: every unit first runs with room for 512 candidates (4 warps per
 // CTA); units with more go to an overflow list that a second launch runs with
 // room for 1024 (4 warps per CTA, persistent, each warp claiming the next
-// unit of the list).  Units beyond that, or with k > 512, go to the CTA-wide
-// path.
+// unit of the list), and its overflow to a third with room for 2048 (2 warps
+// per CTA).  Units beyond that, or with k > 512, go to the CTA-wide path.
 #include "common.cuh"
 #include "kernels.cuh"
 #include "mma_utils.cuh"
@@ -509,37 +509,51 @@ bool rescore_mma_supported(const RescoreParams& p, ssa_dtype dt) {
   return (dt == SSA_BF16 || dt == SSA_F16) && (p.d == 64 || p.d == 128) && p.a <= 32;
 }
 
+// A persistent launch of a list tier: as many CTAs per SM as fit.
+template <typename Kern>
+static cudaError_t launch_list_tier(Kern kern, int warps, size_t smem, const RescoreParams& p, const int32_t* in_list,
+                                    const int32_t* in_count, int32_t* in_next, int32_t* out_list,
+                                    int32_t* out_count, cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  int dev = 0, sms = 148, per_sm = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, warps * kWarp, smem);
+  if (e != cudaSuccess) return e;
+  kern<<<static_cast<unsigned>(sms * (per_sm > 0 ? per_sm : 1)), warps * kWarp, smem, st>>>(
+      p, in_list, in_count, in_next, out_list, out_count);
+  return cudaGetLastError();
+}
+
 template <typename T, int D>
 static cudaError_t launch_mma_t(const RescoreParams& p, cudaStream_t st) {
   const int64_t units = static_cast<int64_t>(p.batch) * p.n_q * p.h_kv;
-  // tier 1: every unit, room for 512 candidates; overflow -> ovf list
+  for (int32_t* z : {p.ovf2_count, p.ovf2_next, p.ovf3_count, p.ovf3_next}) {
+    const cudaError_t e = cudaMemsetAsync(z, 0, sizeof(int32_t), st);
+    if (e != cudaSuccess) return e;
+  }
+  // tier 1: every unit, room for 512 candidates; overflow -> tier 2's list
   constexpr int U1 = SSA_RS_UNITS, C1 = 512;
   const size_t smem1 = sizeof(RsMmaSmem<C1>) * U1;
   auto k1 = rescore_mma_kernel<T, D, C1, U1, false>;
   cudaError_t e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem1));
   if (e != cudaSuccess) return e;
-  e = cudaMemsetAsync(p.ovf2_count, 0, sizeof(int32_t), st);
-  if (e != cudaSuccess) return e;
-  e = cudaMemsetAsync(p.ovf2_next, 0, sizeof(int32_t), st);
-  if (e != cudaSuccess) return e;
   k1<<<static_cast<unsigned>(cdiv(units, U1)), U1 * kWarp, smem1, st>>>(p, nullptr, nullptr, nullptr,
                                                                        p.ovf2_list, p.ovf2_count);
-  // tier 2: the overflow units, room for 1024 (4 warps per CTA, as many CTAs
-  // per SM as fit, warps claiming units from the list); overflow -> the
-  // CTA-wide path
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  // tier 2: room for 1024 (4 warps per CTA, warps claiming units from the
+  // list); overflow -> tier 3
   constexpr int U2 = 4, C2 = 1024;
-  const size_t smem2 = sizeof(RsMmaSmem<C2>) * U2;
-  auto k2 = rescore_mma_kernel<T, D, C2, U2, true>;
-  e = cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem2));
+  e = launch_list_tier(rescore_mma_kernel<T, D, C2, U2, true>, U2, sizeof(RsMmaSmem<C2>) * U2, p, p.ovf2_list,
+                       p.ovf2_count, p.ovf2_next, p.ovf3_list, p.ovf3_count, st);
   if (e != cudaSuccess) return e;
-  int dev = 0, sms = 148, per_sm = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k2, U2 * kWarp, smem2);
-  if (e != cudaSuccess) return e;
-  k2<<<static_cast<unsigned>(sms * (per_sm > 0 ? per_sm : 1)), U2 * kWarp, smem2, st>>>(p, p.ovf2_list, p.ovf2_count, p.ovf2_next,
-                                                                p.ovf_list, p.ovf_count);
-  return cudaGetLastError();
+  // tier 3: room for 2048 (2 warps per CTA, 25 KB of shared memory a warp);
+  // overflow -> the CTA-wide path
+  constexpr int U3 = 2, C3 = 2048;
+  return launch_list_tier(rescore_mma_kernel<T, D, C3, U3, true>, U3, sizeof(RsMmaSmem<C3>) * U3, p, p.ovf3_list,
+                          p.ovf3_count, p.ovf3_next, p.ovf_list, p.ovf_count, st);
 }
 
 cudaError_t launch_rescore_mma(const RescoreParams& p, ssa_dtype dt, cudaStream_t st) {

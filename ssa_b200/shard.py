@@ -12,9 +12,11 @@ Per forward (:func:`sharded_forward`):
 
 1. key codes of the rank's own key rows -- the code assignment of a key
    depends on that key alone (``ssa/router.py:114-130``);
-2. the one exchange step: all-gather of K, V and the key codes into
-   full-sequence buffers (K and V start moving before the code assignment);
-3. the code->key index of all ``n`` keys, built once;
+2. the one exchange step: all-gather of the key codes, K and V into
+   full-sequence buffers, in that order (collectives run in issue order, so
+   the small code gather is issued first);
+3. the code->key index of all ``n`` keys, built once as soon as the codes
+   have arrived -- K and V are still moving meanwhile;
 4. for each of its two blocks, routing of the block's queries against all
    ``n`` keys with the gathered codes and the index (``q_offset`` = the
    block's start) -- V is still arriving meanwhile -- then sparse attention
@@ -125,15 +127,18 @@ def sharded_forward(router, q_local: torch.Tensor, k_local: torch.Tensor, v_loca
         def attn_fn(qb, k, v, idx, q_offset):
             return ops.sparse_attn(qb, k, v, idx, float(scale), bool(causal), int(q_offset))
 
-    # the exchange: K and V start moving while this rank assigns its key codes
-    k_work, k_finish = gather_sequence(k_local, world, group, async_op=True)
-    v_work, v_finish = gather_sequence(v_local, world, group, async_op=True)
+    # the exchange.  The codes go first: the index built from them needs
+    # neither K nor V, so it is built while K and V are still moving (a code
+    # gather issued after them would wait for both).
     codes_local = code_fn(k_local)
     c_work, c_finish = gather_sequence(codes_local, world, group, async_op=True)
-    k_work.wait()
+    k_work, k_finish = gather_sequence(k_local, world, group, async_op=True)
+    v_work, v_finish = gather_sequence(v_local, world, group, async_op=True)
     c_work.wait()
-    k_full, codes = k_finish(), c_finish()
+    codes = c_finish()
     index = index_fn(codes)
+    k_work.wait()
+    k_full = k_finish()
     qbs = [q_local[:, which * length:(which + 1) * length] for which, (start, length) in enumerate(blocks)]
     idxs = [route_fn(qb, k_full, codes, index, start) for qb, (start, _) in zip(qbs, blocks)]
     v_work.wait()

@@ -72,7 +72,8 @@ CASES = [
     (700, 16, 2, 128, 64, 16, 4, 256, True),
     (1500, 4, 1, 64, 32, 4, 2, 300, True),      # 257..512 candidates: 16-per-lane warp sort
     (600, 8, 2, 64, 16, 4, 2, 600, True),       # k > 512: every unit on the CTA-wide path
-    (400, 4, 1, 64, 64, 32, 4, 32, True),       # a = 32 query codes: the hashed first-match test rarely applies
+    (400, 4, 1, 64, 64, 32, 4, 32, True),       # a = 32 query codes
+    (3000, 4, 1, 64, 16, 4, 4, 64, True),       # up to ~2200 candidates: every warp tier, then the CTA path
 ]
 
 
