@@ -148,6 +148,15 @@ __device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t (&v)[32
 }
 __device__ __forceinline__ void tmem_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// (hi - l, lo - l) of the fp32 pair (lo, hi) against l = (l, l) packed in 64
+// bits: one packed f32x2 subtraction, round to nearest, no flush to zero.
+__device__ __forceinline__ uint64_t sub_f32x2(uint32_t lo, uint32_t hi, uint64_t l) {
+  const uint64_t a = (static_cast<uint64_t>(hi) << 32) | lo;
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(l));
+  return d;
+}
+
 // Three-input maximum (one instruction on sm_100; NaN inputs are ignored as by fmaxf).
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float r;
@@ -478,6 +487,7 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
       // strictly below lb (and below +0 when lb is +0), so that the sign of
       // v - lb_below is clear exactly when v >= lb_below
       const float lb_below = lb - fabsf(lb) * 0x1p-20f - 0x1p-126f;
+      const uint64_t lb_pair = (static_cast<uint64_t>(__float_as_uint(lb_below)) << 32) | __float_as_uint(lb_below);
 
       // ---- pass 2: full-precision scores; keep those >= lb (a superset) ----
       TopList<KMAX> top;
@@ -507,12 +517,17 @@ __global__ void __launch_bounds__(kThreads, 1) code_score_tc_kernel(CodeScoreTcP
           // dependency depth at 8 shifts instead of 32.  lb_below < lb, so
           // the hits include every score >= lb; a NaN score may set its bit
           // and is dropped below.
+          // The subtractions run two columns per instruction (packed f32x2,
+          // round to nearest as the scalar form).
           uint32_t mb[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-          for (int j = 7; j >= 0; --j)
+          for (int j = 3; j >= 0; --j)
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
-              mb[q] = __funnelshift_l(__float_as_uint(__uint_as_float(v[8 * q + j]) - lb_below), mb[q], 1);
+            for (int q = 0; q < 4; ++q) {
+              const uint64_t d = sub_f32x2(v[8 * q + 2 * j], v[8 * q + 2 * j + 1], lb_pair);
+              mb[q] = __funnelshift_l(static_cast<uint32_t>(d >> 32), mb[q], 1);
+              mb[q] = __funnelshift_l(static_cast<uint32_t>(d), mb[q], 1);
+            }
           const uint32_t miss = mb[0] | (mb[1] << 8) | (mb[2] << 16) | (mb[3] << 24);
           uint32_t hit = ~miss;
           if (hit) {

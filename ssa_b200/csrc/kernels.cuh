@@ -91,6 +91,8 @@ struct RescoreParams {
   const int4* bucket_codes;    // optional (b == 4): the codes of each index entry's key, [B*h_kv, n*4]
   int batch, n, n_q, q_offset, h_kv, group, d, a, b, n_codes, top_k, causal;
   int cap;                     // shared-memory candidate capacity (power of two)
+  int tier1_rows;              // warp path: query rows per (bat, h) the first tier takes (the
+                               // lowest positions; 0 means all n_q)
   int32_t* ovf_count;          // workspace: units left to the general path ...
   int32_t* ovf_next;           // ... the next of them a general-path CTA claims ...
   int32_t* ovf_list;           // ... and their indices [B * n_q * h_kv]

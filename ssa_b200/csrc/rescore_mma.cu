@@ -27,6 +27,8 @@
 // room for 1024 (4 warps per CTA, persistent, each warp claiming the next
 // unit of the list), and its overflow to a third with room for 2048 (2 warps
 // per CTA).  Units beyond that, or with k > 512, go to the CTA-wide path.
+#include <cmath>
+
 #include "common.cuh"
 #include "kernels.cuh"
 #include "mma_utils.cuh"
@@ -487,8 +489,13 @@ __global__ void __launch_bounds__(UNITS * kWarp, LIST ? 4 : 6) rescore_mma_kerne
   RsMmaSmem<CAP>& s = reinterpret_cast<RsMmaSmem<CAP>*>(dyn)[warp];
   const int64_t wi = static_cast<int64_t>(blockIdx.x) * UNITS + warp;
   if constexpr (!LIST) {
-    const int64_t units = static_cast<int64_t>(p.batch) * p.n_q * p.h_kv;
-    if (wi < units) rescore_mma_unit<T, D, CAP>(p, wi, s, lane, out_list, out_count);
+    // the tier1_rows lowest positions of every (bat, h): unit numbers
+    // bh * n_q + [n_q - tier1_rows, n_q) (positions descend within a head)
+    const int rows = p.tier1_rows;
+    const int64_t units = static_cast<int64_t>(p.batch) * p.h_kv * rows;
+    if (wi < units)
+      rescore_mma_unit<T, D, CAP>(p, (wi / rows) * p.n_q + (p.n_q - rows) + wi % rows, s, lane, out_list,
+                                  out_count);
   } else {
     // units differ in cost by several times: each warp claims the next unit
     // of the list when it is free (a fixed stride leaves the launch waiting
@@ -507,6 +514,31 @@ __global__ void __launch_bounds__(UNITS * kWarp, LIST ? 4 : 6) rescore_mma_kerne
 
 bool rescore_mma_supported(const RescoreParams& p, ssa_dtype dt) {
   return (dt == SSA_BF16 || dt == SSA_F16) && (p.d == 64 || p.d == 128) && p.a <= 32;
+}
+
+// The units that start in the second tier, [bh * n_q, bh * n_q + rows) for
+// every (bat, h), as its first list entries.
+__global__ void rescore_prefill_kernel(int32_t* list, int32_t* count, int64_t heads, int n_q, int rows) {
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t total = heads * rows;
+  if (t < total) list[t] = static_cast<int32_t>((t / rows) * n_q + t % rows);
+  if (t == 0) *count = static_cast<int32_t>(total);
+}
+
+// Query rows (per (bat, h), counted from the lowest position) that start in
+// the first tier.  With uniformly used codes a query at position pos has
+// about a * b * (pos + 1) / n_codes candidates under the causal mask
+// (a * b * n / n_codes without it); a query expected to hold more than 1.25
+// times the first tier's room would nearly always overflow it after walking
+// that many entries, so it starts in the second tier.  Any split gives the
+// same results: every tier computes the same function of a unit.
+static int tier1_rows(const RescoreParams& p, int cap1) {
+  const double per_key = static_cast<double>(p.a) * p.b / p.n_codes;
+  const double limit = 1.25 * cap1;
+  if (!p.causal) return per_key * p.n > limit ? 0 : p.n_q;
+  const double first_pos = std::ceil(limit / per_key);      // expected count above limit from here on
+  const double rows = first_pos - p.q_offset;
+  return rows <= 0 ? 0 : (rows >= p.n_q ? p.n_q : static_cast<int>(rows));
 }
 
 // A persistent launch of a list tier: as many CTAs per SM as fit.
@@ -528,21 +560,35 @@ static cudaError_t launch_list_tier(Kern kern, int warps, size_t smem, const Res
 
 template <typename T, int D>
 static cudaError_t launch_mma_t(const RescoreParams& p, cudaStream_t st) {
-  const int64_t units = static_cast<int64_t>(p.batch) * p.n_q * p.h_kv;
   for (int32_t* z : {p.ovf2_count, p.ovf2_next, p.ovf3_count, p.ovf3_next}) {
     const cudaError_t e = cudaMemsetAsync(z, 0, sizeof(int32_t), st);
     if (e != cudaSuccess) return e;
   }
-  // tier 1: every unit, room for 512 candidates; overflow -> tier 2's list
+  // tier 1: room for 512 candidates, all units but those expected to need
+  // more (which go to tier 2's list first); overflow -> tier 2's list
   constexpr int U1 = SSA_RS_UNITS, C1 = 512;
-  const size_t smem1 = sizeof(RsMmaSmem<C1>) * U1;
-  auto k1 = rescore_mma_kernel<T, D, C1, U1, false>;
-  cudaError_t e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem1));
-  if (e != cudaSuccess) return e;
-  k1<<<static_cast<unsigned>(cdiv(units, U1)), U1 * kWarp, smem1, st>>>(p, nullptr, nullptr, nullptr,
-                                                                       p.ovf2_list, p.ovf2_count);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
+  RescoreParams p1 = p;
+  p1.tier1_rows = tier1_rows(p, C1);
+  const int64_t heads = static_cast<int64_t>(p.batch) * p.h_kv;
+  cudaError_t e = cudaSuccess;
+  if (p1.tier1_rows < p.n_q) {
+    const int64_t pre = heads * (p.n_q - p1.tier1_rows);
+    rescore_prefill_kernel<<<static_cast<unsigned>(cdiv(pre, 256)), 256, 0, st>>>(p.ovf2_list, p.ovf2_count, heads,
+                                                                                p.n_q, p.n_q - p1.tier1_rows);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  if (p1.tier1_rows > 0) {
+    const size_t smem1 = sizeof(RsMmaSmem<C1>) * U1;
+    auto k1 = rescore_mma_kernel<T, D, C1, U1, false>;
+    e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem1));
+    if (e != cudaSuccess) return e;
+    const int64_t units1 = heads * p1.tier1_rows;
+    k1<<<static_cast<unsigned>(cdiv(units1, U1)), U1 * kWarp, smem1, st>>>(p1, nullptr, nullptr, nullptr,
+                                                                          p.ovf2_list, p.ovf2_count);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
   // tier 2: room for 1024 (4 warps per CTA, warps claiming units from the
   // list); overflow -> tier 3
   constexpr int U2 = 4, C2 = 1024;
