@@ -451,24 +451,17 @@ __device__ __forceinline__ void rescore_mma_unit(const RescoreParams& p, int64_t
       if (jj < static_cast<uint32_t>(k_eff)) atomicOr(&s.bitmap[jj >> 5], 1u << (jj & 31));
     }
     __syncwarp();
-    uint32_t free_bits = 0;
-    if (lane < words) {
-      free_bits = ~s.bitmap[lane];
-      if (lane == words - 1 && (k_eff & 31)) free_bits &= (1u << (k_eff & 31)) - 1u;
-    }
-    const int nfree = __popc(free_bits);
-    int fin = nfree;
-#pragma unroll
-    for (int o = 1; o < kWarp; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, fin, o);
-      if (lane >= o) fin += y;
-    }
-    int rank = fin - nfree;
-    while (free_bits && rank < need) {
-      const int bit = __ffs(free_bits) - 1;
-      free_bits &= free_bits - 1;
-      put(count + rank, lane * 32 + bit);
-      ++rank;
+    // the lowest `need` free indices, in order: 32 indices per step, ranked
+    // by a ballot (coalesced stores; the loop ends once `need` are placed)
+    int base = 0;
+#pragma unroll 1
+    for (int w0 = 0; w0 < k_eff && base < need; w0 += kWarp) {
+      const int jj = w0 + lane;
+      const bool fr = jj < k_eff && !((s.bitmap[jj >> 5] >> (jj & 31)) & 1u);
+      const unsigned bal = __ballot_sync(0xffffffffu, fr);
+      const int rank = base + __popc(bal & ((1u << lane) - 1u));
+      if (fr && rank < need) put(count + rank, jj);
+      base += __popc(bal);
     }
   }
   for (int e = k_eff + lane; e < p.top_k; e += kWarp) put(e, 0);
@@ -493,9 +486,11 @@ __global__ void __launch_bounds__(UNITS * kWarp, LIST ? 4 : 6) rescore_mma_kerne
     // bh * n_q + [n_q - tier1_rows, n_q) (positions descend within a head)
     const int rows = p.tier1_rows;
     const int64_t units = static_cast<int64_t>(p.batch) * p.h_kv * rows;
-    if (wi < units)
-      rescore_mma_unit<T, D, CAP>(p, (wi / rows) * p.n_q + (p.n_q - rows) + wi % rows, s, lane, out_list,
-                                  out_count);
+    if (wi < units) {
+      const int w = static_cast<int>(wi), bh = w / rows;        // unit numbers fit 32 bits (list entries)
+      const int unit = rows == p.n_q ? w : bh * p.n_q + (p.n_q - rows) + (w - bh * rows);
+      rescore_mma_unit<T, D, CAP>(p, unit, s, lane, out_list, out_count);
+    }
   } else {
     // units differ in cost by several times: each warp claims the next unit
     // of the list when it is free (a fixed stride leaves the launch waiting
