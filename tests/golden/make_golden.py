@@ -1,9 +1,10 @@
 """Generate the golden fixtures that pin the CPU oracle to the reference.
 
-Run in the build container, where the reference implementation is importable
-(default location ``/root/reference``; override with ``SSA_REFERENCE_PATH``):
+Run where the reference implementation's source tree is available, with
+``SSA_REFERENCE_PATH`` set to its root (the directory holding the ``ssa``
+package):
 
-    python tests/golden/make_golden.py
+    SSA_REFERENCE_PATH=<reference checkout> python tests/golden/make_golden.py
 
 Each fixture stores seeded inputs together with the outputs of the
 *unmodified* reference code (chenxingqiang/SSA, pure PyTorch, fp32, CPU):
@@ -35,10 +36,12 @@ import sys
 
 sys.dont_write_bytecode = True
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("SSA_REFERENCE_PATH", "/root/reference")
+REF = os.environ.get("SSA_REFERENCE_PATH", "")
 
 
 def _import_reference():
+    if not REF or not os.path.isdir(os.path.join(REF, "ssa")):
+        raise SystemExit("set SSA_REFERENCE_PATH to the reference checkout (the directory holding `ssa/`)")
     sys.path.insert(0, REF)
     import ssa  # noqa: F401  (the reference package)
     assert os.path.realpath(os.path.dirname(ssa.__file__)).startswith(os.path.realpath(REF))
