@@ -5,7 +5,7 @@
 // candidates = keys sharing a code with the query, j <= i when causal;
 // ranked by qbar . k_j with the lower key index first among equal scores;
 // canonical filler; zero padding).  Steps, all inside one warp:
-//   1. the query's a buckets are located (causal cut by binary search) and
+//   1. the query's a buckets are located (causal cut by an 8-probe search) and
 //      walked 128 keys at a time (all loads of a group issued together); the
 //      first-match rule drops keys reached through an earlier code; kept key
 //      indices are compacted with ballots;
@@ -27,6 +27,8 @@
 // room for 1024 (4 warps per CTA, persistent, each warp claiming the next
 // unit of the list), and its overflow to a third with room for 2048 (2 warps
 // per CTA).  Units beyond that, or with k > 512, go to the CTA-wide path.
+// Queries expected to hold far more candidates than the first tier's room
+// (long sequences only) start in the second tier.
 #include <cmath>
 
 #include "common.cuh"
