@@ -88,6 +88,17 @@ def test_workspace_size_is_host_only_and_positive(lib):
     assert lib.ssa_route_workspace_size(None) == 0
 
 
+def test_workspace_grows_with_the_query_units(lib):
+    # every (query, KV head) unit needs its routed vector (d_s fp32), its a
+    # codes and one slot in each of the three overflow lists of the re-score
+    # tiers; regions are 256-byte aligned, hence the slack
+    small = lib.ssa_route_workspace_size(ctypes.byref(_route_args(n=4096, n_q=1024)))
+    large = lib.ssa_route_workspace_size(ctypes.byref(_route_args(n=4096, n_q=4096)))
+    units = (4096 - 1024) * 2
+    per_unit = 32 * 4 + 8 * 4 + 3 * 4
+    assert large - small >= units * per_unit - 32 * 256
+
+
 @pytest.mark.parametrize("over,code", [
     (dict(h_q=7), 1),                 # not a multiple of h_kv
     (dict(d=60), 2),                  # head_dim not a multiple of 8
