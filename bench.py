@@ -16,16 +16,26 @@ attention over the selected keys.
   (``CodebookRouter`` -> ``sparse_exact_attention``) from pinned HOST
   buffers: host->device copies of q/k/v and the device->host copy of the
   output are inside the timed region.
-* ``roofline``: the sparse-attention kernel (the largest share of the step),
-  algorithmic bytes per launch / its CUDA-event duration, against the measured
-  HBM copy bandwidth.
+* ``roofline``: the sparse-attention kernel (the largest share of the step):
+  its compulsory HBM bytes (q, out, K, V, indices once) per launch / its
+  CUDA-event duration against the measured HBM copy bandwidth, the ncu DRAM
+  traffic of a launch beside them, and in ``l2`` the logical bytes (every
+  gathered K/V row) against the L2 read peak measured in the same run -- the
+  gathers are served from L2, so that fraction is the one that binds.
+  ``roofline_stages``: stage 1 (codebook scoring, tensor) and stage 2
+  (index + re-score + top-k, DRAM and L2 as above).
+* ``parity``: the timed step's own codes, indices and output against the CPU
+  oracle on a sample (one KV head, ~580 query rows), outside the timed region.
 * ``cpu_baseline``: the reference algorithm (CPU oracle port, O(n^2) dense
   re-score as the reference computes it) on a bounded sample, rank 0 only.
+* ``config4``: config 4 (one n = 131072 sequence split by queries over the
+  ranks, NCCL all-gathers of K, V and key codes) timed in the same process
+  group: its strong-scaling curve over the driver's N = 1, 2, 4, 8 runs.
 
-Multi-GPU (torchrun, one process per GPU): each rank runs its own
-independent sequence (batch x KV-head units need no exchange) -> weak scaling.
-``--impl reference`` times the reference's CPU algorithm (oracle port) on the
-host cores instead.
+Multi-GPU (torchrun, one process per GPU): for the headline each rank runs its
+own independent sequence (batch x KV-head units need no exchange) -> weak
+scaling.  ``--impl reference`` times the reference's CPU algorithm (oracle
+port) on the host cores instead.
 """
 
 from __future__ import annotations
@@ -56,6 +66,10 @@ LAUNCHES_PER_STEP = 17
 # measured by ncu (dram__bytes_read.sum + dram__bytes_write.sum, one pass on this
 # workload; profiles/sparse_attn_mma_config3.txt).  Other n scale by the query rows.
 ATTN_DRAM_BYTES_N32768 = 920.29e6
+# DRAM bytes of stage 2 (ssa_select_candidates: index build, entry codes, re-score
+# tiers) per call at n = 32768, from the ncu DRAM counters of its kernels
+# (profiles/rescore_mma_config3.txt).
+RESCORE_DRAM_BYTES_N32768 = 2 * 289.7e6
 
 
 def parse():
@@ -68,6 +82,8 @@ def parse():
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
+    p.add_argument("--no-config4", action="store_true",
+                   help="skip the config-4 (query-split n=131072) record of the default run")
     p.add_argument("--workload", default="config3", choices=["config3", "config4", "config5"],
                    help="config3: one sequence per GPU (the headline); config4: one n=131072 "
                         "sequence split by queries over the GPUs (strong scaling); config5: a Qwen-style "
@@ -131,9 +147,10 @@ class ClockSampler:
         mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
-        under = sorted(sm)[len(sm) // 2:] if sm else []
-        return {"sm_mhz": statistics.median(under) if under else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+        # every sample taken while the timed region ran (no filtering)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_mhz_min": min(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows),
+                "interval_ms": 100}
 
 
 # ---------------------------------------------------------------------------
@@ -186,7 +203,23 @@ def cpu_inputs(shape, seed):
     return f(t["q"]), f(t["k"]), f(t["v"]), t["w_qr"].float(), t["w_kr"].float(), t["codebook"].float()
 
 
+def bench_config(shape, world):
+    """The ``config`` dict of the config-3 line; both arms print the same one."""
+    mb = shape.n * (shape.h_q + 2 * shape.h_kv) * shape.d * 2 / 1e6
+    return {"workload": f"config3 (op-level sweep at n={shape.n})", **shape.asdict(),
+            "per_rank": "one independent sequence per GPU",
+            "l2": f"inputs {mb:.0f} MB {'>' if mb > 126 else '<'} 126 MB L2, no flush",
+            "parallelism": f"batch-units x{world}"}
+
+
 def run_reference(args):
+    """The reference's CPU algorithm (oracle port) on the host cores.  Each
+    step is a bounded sample of the config-3 forward: one KV head, key codes
+    of all n keys, then the last n/4 query rows (query codes, dense masked
+    re-score over all n keys, top-k, gathered attention).  ``ms_per_step`` is
+    the measured time of that sampled step; ``value`` is the tokens/s of the
+    full forward extrapolated from it (the key codes once per head, the rows
+    by n / rows, the h_kv heads by h_kv)."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
@@ -198,18 +231,26 @@ def run_reference(args):
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
     t_cpu = cpu_inputs(shape, args.seed)
+    rows = max(1, shape.n // 4)
     vals, secs = [], []
+    t0 = time.perf_counter()
     for it in range(args.warmup + args.steps):
-        v, s, sample = cpu_sample(t_cpu, shape, heads=1, rows=max(1, shape.n // 4))
+        v, s, sample = cpu_sample(t_cpu, shape, heads=1, rows=rows)
         if it >= args.warmup:
             vals.append(v)
             secs.append(s)
+    wall = time.perf_counter() - t0
     value = statistics.median(vals)
+    ms_step = 1e3 * statistics.median(secs)
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * shape.n / value,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded planted-cluster config-3 inputs)",
-            "config": {"workload": "config3", **shape.asdict()},
+            "data": "synthetic (seeded: Q/K ~ N(0,1), 5% planted keys around 64 centroids, V ~ N(0,1))",
+            "config": bench_config(shape, world),
+            "work_per_step": {"kv_heads": 1, "of_kv_heads": shape.h_kv, "keys_coded": shape.n,
+                              "query_rows": rows, "of_query_rows": shape.n},
+            "ms_per_full_forward_extrapolated": 1e3 * shape.n / value,
+            "wall_s": wall,
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
                              "sample": sample, "sample_seconds": statistics.median(secs)},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -220,8 +261,65 @@ def run_reference(args):
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
+def measure_l2_read_peak(dev, reps=40):
+    """Read bandwidth of an L2-resident buffer (outside the timed region):
+    ``torch.sum`` over an fp32 tensor of 16 / 32 / 48 MiB that a warm-up pass
+    left in the 126 MB L2, timed with CUDA events; the best of the sizes.
+    The denominator of the ``l2`` fractions below."""
+    import torch
+
+    best = 0.0
+    for mib in (16, 32, 48):
+        x = torch.ones(mib * 2 ** 20 // 4, device=dev)
+        for _ in range(5):
+            x.sum()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            x.sum()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        best = max(best, mib * 2 ** 20 * reps / (e0.elapsed_time(e1) / 1e3) / 1e9)
+        del x
+    return best
+
+
+def bench_parity(t, shape, idx, q_codes, k_codes, out, head=1, n_rows=512, seed=7):
+    """Sampled parity of the measured step's own outputs against the CPU
+    oracle (outside the timed region): one KV head, ``n_rows`` query rows
+    spread over the sequence plus the last 64.  Reports the fraction of key
+    and query code rows equal to the oracle's, the candidate-set overlap with
+    the oracle's selection and the relative L2 error of the attention output
+    against the float64 oracle on the GPU's own selection (
+    >= 0.999, >= 0.999, <= 2e-3)."""
+    import numpy as np
+    import torch
+    from oracle import ssa_oracle as O
+
+    t0 = time.perf_counter()
+    n, g = shape.n, shape.h_q // shape.h_kv
+    rng = np.random.default_rng(seed)
+    rows = np.unique(np.concatenate([rng.choice(n, size=n_rows, replace=False), np.arange(n - 64, n)]))
+    rt = torch.from_numpy(rows).to(idx.device)
+    f64 = lambda x: x.double().cpu().numpy()
+    q_rows = f64(t["q"][0, rt, head * g:(head + 1) * g])
+    k_h, v_h = f64(t["k"][0, :, head]), f64(t["v"][0, :, head])
+    kc, qc, ref_idx = O.route_rows_one_head(q_rows, rows, k_h, f64(t["w_qr"]), f64(t["w_kr"]),
+                                            f64(t["codebook"][head]), shape.a, shape.b, shape.top_k, causal=True)
+    same = lambda a, b: float((np.sort(a, -1) == np.sort(b, -1)).all(-1).mean())
+    gi = idx[0, rt, head].long().cpu().numpy()
+    sa, sb = np.sort(gi, 1), np.sort(ref_idx, 1)
+    overlap = sum(np.intersect1d(x, y).size for x, y in zip(sa, sb)) / gi.size
+    ref_out = O.sparse_attention(q_rows, k_h[:, None], v_h[:, None], gi[:, None], causal=True, positions=rows)
+    got = f64(out[0, rt, head * g:(head + 1) * g])
+    rel = float(np.linalg.norm(got - ref_out) / np.linalg.norm(ref_out))
+    return {"kv_head": head, "query_rows": int(rows.size), "key_code_rows_equal": same(k_codes[0, :, head].cpu().numpy(), kc),
+            "query_code_rows_equal": same(q_codes[0, rt, head].cpu().numpy(), qc),
+            "candidate_overlap": overlap, "output_rel_l2_err": rel,
+            "oracle": "oracle/ssa_oracle.py route_rows_one_head + sparse_attention (float64)",
+            "seconds": time.perf_counter() - t0}
 def stage_rooflines(lib, rargs, q_codes, k_codes, cand, shape, ws, sptr, stream, hbm, tflops, peak_kind,
-                    reps=10):
+                    l2_peak, reps=10):
     """Rooflines of the two router stages, each timed with CUDA events in its
     own loop after the timed region (the C ABI launches a stage's kernels in
     one call, so they cannot be bracketed inside ssa_route):
@@ -261,14 +359,20 @@ def stage_rooflines(lib, rargs, q_codes, k_codes, cand, shape, ws, sptr, stream,
     t2 = timed(lambda: L.check("ssa_select_candidates",
                                lib.ssa_select_candidates(ctypes.byref(a2), ws.data_ptr(), ws.numel(), sptr)))
     f1 = s1_flops / (t1 / 1e3) / 1e12
-    b2 = s2_bytes / (t2 / 1e3) / 1e9
+    dram2 = RESCORE_DRAM_BYTES_N32768 * n / 32768
     return {
         "stage1_keys": {"call": "ssa_code_assign", "bound": "tensor", "achieved": f1, "peak": tflops,
                         "unit": "TFLOP/s", "frac": f1 / tflops, "peak_kind": peak_kind,
                         "algorithmic_flops": s1_flops, "ms": t1},
-        "stage2": {"call": "ssa_select_candidates", "bound": "hbm", "achieved": b2, "peak": hbm,
-                   "unit": "GB/s", "frac": b2 / hbm, "peak_kind": peak_kind,
-                   "algorithmic_bytes": s2_bytes, "mean_unique_candidates": c_sum / units, "ms": t2},
+        # stage 2's gathers (key rows of the candidates) are served from L2 like
+        # the attention's: fractions of the DRAM copy peak (ncu DRAM bytes of the
+        # stage's kernels) and of the measured L2 read peak (logical bytes)
+        "stage2": {"call": "ssa_select_candidates", "bound": "hbm", "unit": "GB/s", "ms": t2,
+                   "achieved": dram2 / (t2 / 1e3) / 1e9, "peak": hbm, "peak_kind": peak_kind,
+                   "frac": dram2 / (t2 / 1e3) / 1e9 / hbm, "traffic": dram2,
+                   "l2": {"achieved": s2_bytes / (t2 / 1e3) / 1e9, "peak": l2_peak,
+                          "frac": s2_bytes / (t2 / 1e3) / 1e9 / l2_peak, "bytes": s2_bytes},
+                   "logical_bytes": s2_bytes, "mean_unique_candidates": c_sum / units},
     }
 
 
@@ -286,9 +390,8 @@ def run_ours(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    if world > 1 or not args.no_config4:
+        init_group(dev, world, 180)
 
     shape = W.Shape(**{**W.CONFIG3.asdict(), "n": args.n})
     t = W.make_inputs(shape, seed=args.seed + rank, dtype=torch.bfloat16, device=dev)
@@ -350,27 +453,44 @@ def run_ours(args):
     value = world * n / (ms_step / 1e3)
     in_mb = sum(x.numel() * x.element_size() for x in (q, k, v)) / 1e6
 
-    # roofline of the sparse-attention kernel (one launch per step)
+    # roofline of the sparse-attention kernel (one launch per step).  Its
+    # algorithmic HBM bytes are the compulsory ones (q and out once, K and V
+    # once, the int32 indices once); its k gathered K/V rows per (query, head)
+    # -- the logical bytes -- come from L2 (head-major order keeps a head's K/V
+    # resident), so the L2 read rate against the measured L2 read peak is the
+    # fraction that binds it.
     hbm, tflops, peak_kind = load_peaks()
+    l2_peak = measure_l2_read_peak(dev)
     units = n * hkv
-    attn_bytes = units * kk * (2 * d * 2) + 2 * n * hq * d * 2 + units * kk * 4
-    achieved = attn_bytes / (attn_ms / 1e3) / 1e9
-    roof = {"kernel": "sparse_attn_mma_kernel", "bound": "hbm", "achieved": achieved, "peak": hbm,
-            "unit": "GB/s", "frac": achieved / hbm, "peak_kind": peak_kind,
-            "traffic": ATTN_DRAM_BYTES_N32768 * n / 32768,
-            "traffic_note": "ncu DRAM bytes per launch at n=32768" + ("" if n == 32768 else ", scaled by n"),
-            "algorithmic_bytes_per_launch": attn_bytes, "launch_ms": attn_ms,
-            "router_ms": route_ms}
+    attn_logical = units * kk * (2 * d * 2) + 2 * n * hq * d * 2 + units * kk * 4
+    attn_compulsory = 2 * n * hq * d * 2 + 2 * n * hkv * d * 2 + units * kk * 4
+    attn_s = attn_ms / 1e3
+    traffic = ATTN_DRAM_BYTES_N32768 * n / 32768
+    roof = {"kernel": "sparse_attn_mma_kernel", "bound": "hbm", "unit": "GB/s",
+            "achieved": attn_compulsory / attn_s / 1e9, "peak": hbm, "peak_kind": peak_kind,
+            "frac": attn_compulsory / attn_s / 1e9 / hbm,
+            "traffic": traffic,
+            "traffic_note": "ncu DRAM read + write bytes per launch at n=32768"
+                            + ("" if n == 32768 else ", scaled by n"),
+            "algorithmic_bytes_per_launch": attn_compulsory,
+            "dram_frac": traffic / attn_s / 1e9 / hbm,
+            "l2": {"achieved": attn_logical / attn_s / 1e9, "peak": l2_peak, "unit": "GB/s",
+                   "frac": attn_logical / attn_s / 1e9 / l2_peak, "bytes": attn_logical,
+                   "peak_kind": "measured in this run: torch.sum over an L2-resident buffer"},
+            "binding": "l2 (k gathered K/V rows per query and head, served from L2)",
+            "logical_bytes_per_launch": attn_logical, "launch_ms": attn_ms, "router_ms": route_ms}
+    # parity of the timed steps' own outputs, before anything rewrites them
+    parity = bench_parity(t, shape, idx, q_codes, k_codes, out) if rank == 0 else None
     stages = stage_rooflines(lib, rargs, q_codes, k_codes, cand, shape, ws, sptr, stream, hbm, tflops,
-                             peak_kind)
+                             peak_kind, l2_peak)
 
-    # e2e through the public API from pinned host buffers.  Every step copies
-    # its q/k/v in (host -> device) and its output back (device -> host); the
-    # copies run on two copy streams so that step s+1's inputs and step s-1's
-    # output move while step s computes (double-buffered device inputs).
+    # e2e through the public API from pinned host buffers, with the API's
+    # default device-status checking (read back lazily, no host stall).  Every
+    # step copies its q/k/v in (host -> device) and its output back (device ->
+    # host); the copies run on two copy streams so that step s+1's inputs and
+    # step s-1's output move while step s computes (double-buffered inputs).
     e2e = None
     if not args.no_e2e:
-        os.environ.setdefault("SSA_CHECKED", "0")
         router = ssa.CodebookRouter(head_dim=d, route_dim=shape.d_s, num_kv_heads=hkv,
                                     num_codebook=shape.n_codes, codes_per_key=shape.b,
                                     codes_per_query=shape.a, top_k=kk).to(dev)
@@ -425,6 +545,7 @@ def run_ours(args):
         run(args.steps)
         e1.record(stream)
         torch.cuda.synchronize(dev)
+        ssa.check_errors(dev)                     # the steps' device status words: all clear
         e_ms = e0.elapsed_time(e1)
         if world > 1:
             tt = torch.tensor([e_ms], device=dev)
@@ -434,8 +555,19 @@ def run_ours(args):
                "h2d_bytes_per_step": sum(x.numel() * x.element_size() for x in host_in),
                "d2h_bytes_per_step": host_out[0].numel() * host_out[0].element_size(),
                "ms_per_step": e_ms / args.steps,
-               "api": "CodebookRouter.forward + sparse_exact_attention",
+               "api": "CodebookRouter.forward + sparse_exact_attention (default SSA_CHECKED: lazy status)",
                "copies": "pinned host buffers; h2d of step s+1 and d2h of step s overlap step s's compute"}
+        del host_in, host_out, dev_in
+        torch.cuda.empty_cache()
+
+    # config 4 (one n = 131072 sequence split by queries over the ranks, NCCL
+    # all-gathers) in the same process group: the driver's N = 1..8 runs of
+    # this script then record its strong-scaling curve too
+    c4 = None
+    if not args.no_config4:
+        del q, k, v, t, out, idx, ws
+        torch.cuda.empty_cache()
+        c4 = config4_timing(args, dev, world, rank, steps=max(3, min(args.steps, 10)), warmup=3)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -450,26 +582,40 @@ def run_ours(args):
                 "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
                 "data": "synthetic (seeded: Q/K ~ N(0,1), 5% planted keys around 64 centroids, V ~ N(0,1))",
-                "config": {"workload": f"config3 (op-level sweep at n={n})", **shape.asdict(),
-                           "per_rank": "one independent sequence per GPU",
-                           "l2": f"inputs {in_mb:.0f} MB > 126 MB L2, no flush",
-                           "parallelism": f"batch-units x{world}"},
-                "roofline": roof, "roofline_stages": stages, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
-                "gpu_launches": LAUNCHES_PER_STEP * args.steps}
+                "config": bench_config(shape, world),
+                "roofline": roof, "roofline_stages": stages, "parity": parity, "cpu_baseline": cpu,
+                "e2e": e2e, "clocks": clk, "gpu_launches": LAUNCHES_PER_STEP * args.steps,
+                "config4": c4}
         print(json.dumps(line), flush=True)
-    if world > 1:
+    if dist.is_initialized():
         dist.barrier()
         dist.destroy_process_group()
     return 0
 
 
-def run_config4(args):
-    """Config 4: one long sequence (n = 131072, N_c = 8192, k = 512, bf16,
-    N(0,1) inputs) split by queries over the ranks (ssa_b200.shard: zig-zag
-    blocks, all-gather of K, V and key codes, routing with the gathered codes,
-    attention).  Total work is fixed: strong scaling."""
+def init_group(dev, world, timeout_s):
+    """One NCCL process group over the ranks torchrun started (a 1-rank group
+    on 127.0.0.1 for a plain ``python bench.py``)."""
     import datetime
+    import socket
 
+    import torch.distributed as dist
+
+    if world == 1 and "MASTER_ADDR" not in os.environ:
+        with socket.socket() as so:
+            so.bind(("127.0.0.1", 0))
+            port = so.getsockname()[1]
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK="0", WORLD_SIZE="1")
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=timeout_s), device_id=dev)
+
+
+def config4_timing(args, dev, world, rank, steps, warmup):
+    """Config 4: one long sequence (n = 131072, N_c = 8192, k = 512, bf16,
+    N(0,1) inputs) split by queries over the ranks of the current process group
+    (ssa_b200.shard: zig-zag blocks, all-gather of K, V and key codes, routing
+    with the gathered codes, attention).  Total work is fixed: strong scaling.
+    Device-timed (CUDA events, barrier + synchronize on both sides, max over
+    ranks).  Returns the record rank 0 prints."""
     import torch
     import torch.distributed as dist
 
@@ -477,19 +623,7 @@ def run_config4(args):
     from ssa_b200 import shard
     from ssa_b200 import workloads as W
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world == 1 and "MASTER_ADDR" not in os.environ:
-        import socket
-        with socket.socket() as so:
-            so.bind(("127.0.0.1", 0))
-            port = so.getsockname()[1]
-        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK="0", WORLD_SIZE="1")
-    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
-    n = args.n if args.n != 32768 else W.CONFIG4.n
+    n = W.CONFIG4.n if args.workload != "config4" or args.n == 32768 else args.n
     shape = W.Shape(**{**W.CONFIG4.asdict(), "n": n})
     t = W.make_inputs(shape, seed=args.seed, dtype=torch.bfloat16, device=dev, planted=False,
                       generate_on_device=True)
@@ -503,43 +637,60 @@ def run_config4(args):
     ql, kl, vl = (shard.local_rows(t[x], world, rank) for x in ("q", "k", "v"))
     del t
     torch.cuda.empty_cache()
-    os.environ.setdefault("SSA_CHECKED", "0")
     stream = torch.cuda.current_stream(dev)
 
     def step():
         with torch.no_grad():
             return shard.sharded_forward(router, ql, kl, vl, causal=True)
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
     torch.cuda.synchronize(dev)
-    clocks = ClockSampler(local)
+    ssa.check_errors(dev)
+    clocks = ClockSampler(dev.index)
     clocks.start()
     dist.barrier()
     torch.cuda.synchronize(dev)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(args.steps):
+    for _ in range(steps):
         step()
     e1.record(stream)
     torch.cuda.synchronize(dev)
     dist.barrier()
     clk = clocks.stop()
+    ssa.check_errors(dev)
     tt = torch.tensor([e0.elapsed_time(e1)], device=dev)
     dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-    ms_step = float(tt.item()) / args.steps
+    ms_step = float(tt.item()) / steps
+    del ql, kl, vl
+    torch.cuda.empty_cache()
+    return {"metric": "SSA fwd tokens/s, one n=131072 sequence split over the GPUs (k=512, bf16)",
+            "value": n / (ms_step / 1e3), "unit": UNIT, "n_gpus": world, "steps": steps, "warmup": warmup,
+            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong", "dtype": "bf16",
+            "data": "synthetic (seeded on device: Q/K/V ~ N(0,1))",
+            "config": {"workload": "config4 (long single sequence, query-split)", **shape.asdict(),
+                       "parallelism": f"query-split x{world} (zig-zag blocks, NCCL all-gather of K, V, codes)",
+                       "l2": "inputs 1.6 GB > 126 MB L2, no flush"},
+            "clocks": clk}
+
+
+def run_config4(args):
+    """``--workload config4``: the config-4 record alone, as its own line."""
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    init_group(dev, world, 180)
+    rec = config4_timing(args, dev, world, rank, args.steps, args.warmup)
     if rank == 0:
-        line = {"metric": "SSA fwd tokens/s, one n=131072 sequence split over the GPUs (k=512, bf16)",
-                "value": n / (ms_step / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-                "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-                "data": "synthetic (seeded on device: Q/K/V ~ N(0,1))",
-                "config": {"workload": "config4 (long single sequence, query-split)", **shape.asdict(),
-                           "parallelism": f"query-split x{world} (zig-zag blocks, NCCL all-gather of K, V, codes)",
-                           "l2": "inputs 1.6 GB > 126 MB L2, no flush"},
-                "roofline": None, "cpu_baseline": None, "e2e": None, "clocks": clk}
-        print(json.dumps(line), flush=True)
+        print(json.dumps({**rec, "vs_baseline": None, "roofline": None, "cpu_baseline": None, "e2e": None}),
+              flush=True)
     dist.barrier()
     dist.destroy_process_group()
     return 0
@@ -630,7 +781,6 @@ def run_config5(args):
             x = x + F.linear(F.silu(F.linear(h, L["wg"])) * F.linear(h, L["wu"]), L["wd"])
         return rms(x, ln_f)
 
-    os.environ.setdefault("SSA_CHECKED", "0")
     with torch.no_grad():
         for _ in range(args.warmup):
             forward()

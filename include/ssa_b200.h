@@ -199,7 +199,10 @@ typedef struct {
 } SsaAttnArgs;
 
 /* sparse_exact_attention(q, k, v, indices, scale) (ssa/attention.py:12-115)
- * with the per-KV-head gather k[idx, h].  Online softmax in fp32. */
+ * with the per-KV-head gather k[idx, h].  Online softmax in fp32.  A query
+ * row none of whose indices is valid (with causal = 1, every index above
+ * q_offset + i) gets a zero output row; the reference never masks in this
+ * stage, and a softmax over no key would be 0/0. */
 ssa_status ssa_sparse_attn(const SsaAttnArgs* args, void* stream);
 
 /* Gradients of ssa_sparse_attn (the backward of sparse_exact_attention,
@@ -243,8 +246,11 @@ ssa_status ssa_build_index(const SsaRouteArgs* args, const int32_t* k_codes,
  * it before any stream capture.  Every call on a device uses the same array:
  * calls that overlap on the GPU (different streams, no ordering) race and
  * corrupt each other's result.  Nothing in the array needs clearing: each call
- * writes every scratch word it reads.  Outputs and limits otherwise as
- * ssa_build_index. */
+ * writes every scratch word it reads.  The looked-up address is cached per
+ * device for the life of the process: after cudaDeviceReset, or anything else
+ * that destroys and recreates the device's primary context, the cached
+ * address is stale and this entry point must not be called again.  Outputs
+ * and limits otherwise as ssa_build_index. */
 ssa_status ssa_build_index_noalloc(const SsaRouteArgs* args, const int32_t* k_codes,
                                    int32_t* bucket_ptr, int32_t* bucket_keys, void* stream);
 

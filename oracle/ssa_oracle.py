@@ -53,6 +53,9 @@ __all__ = [
     "group_mean_scores",
     "select_topk_index",
     "select_topk_dense",
+    "key_codes_one_head",
+    "query_codes_rows",
+    "route_rows_one_head",
     "route",
     "sparse_attention",
     "sparse_attention_reference_gather",
@@ -318,6 +321,66 @@ def select_topk_dense(q, k, q_codes, k_codes, top_k, causal=True, dtype=np.float
     return out
 
 
+def key_codes_one_head(k_head, w_kr, codebook_head, b, temperature=1.0, block=8192, dtype=np.float64):
+    """Top-``b`` codes ``[n, b]`` of every key of one KV head
+    (``k_head [n, d]``, ``codebook_head [N_c, d_s]``): the key half of
+    ssa/router.py:102-130, in blocks of ``block`` keys so that the
+    ``[block, N_c]`` score matrix is the only large temporary."""
+    kr = np.asarray(k_head, dtype=dtype) @ np.asarray(w_kr, dtype=dtype).T      # [n, d_s]
+    cb = l2_normalize(np.asarray(codebook_head, dtype=dtype))
+    kn = l2_normalize(kr)
+    out = np.empty((kn.shape[0], b), dtype=np.int64)
+    for s in range(0, kn.shape[0], block):
+        out[s:s + block] = stable_topk((kn[s:s + block] @ cb.T) / temperature, b)
+    return out
+
+
+def query_codes_rows(q_rows, w_qr, codebook_head, a, temperature=1.0, dtype=np.float64):
+    """Top-``a`` codes ``[r, a]`` of query rows ``q_rows [r, g, d]`` of one KV
+    group: the group mean of the per-head routes, normalised, scored against
+    the normalised codebook (ssa/router.py:102-141)."""
+    qr = (np.asarray(q_rows, dtype=dtype) @ np.asarray(w_qr, dtype=dtype).T).mean(axis=1)   # [r, d_s]
+    cb = l2_normalize(np.asarray(codebook_head, dtype=dtype))
+    return stable_topk((l2_normalize(qr) @ cb.T) / temperature, a)
+
+
+def route_rows_one_head(q_rows, positions, k_head, w_qr, w_kr, codebook_head, a, b, top_k,
+                        causal=True, temperature=1.0, dtype=np.float64, k_codes=None):
+    """``CodebookRouter.forward`` (ssa/router.py:73-214, with the oracle's
+    corrections) for a SAMPLE of query rows of one KV head, so that full
+    benchmark sizes (n = 32768 .. 131072) can be checked row by row.
+
+    ``q_rows [r, g, d]`` are the group's query heads at sequence positions
+    ``positions [r]``; ``k_head [n, d]`` is every key of the head.  Each row's
+    candidates are the keys ``j <= position`` (when causal) sharing one of its
+    ``a`` codes (the inverted-index form of ssa/router.py:216-259), ranked by
+    ``qbar . k_j`` (the group mean of the logits, ssa/router.py:180-191)
+    with the lower key first among equal scores, completed with the
+    lowest-index non-candidates and zero-padded past ``n`` (:func:`_fill_row`).
+    Returns ``(k_codes [n, b], q_codes [r, a], indices [r, top_k])``;
+    ``k_codes`` may be passed in to skip the key scoring."""
+    k_head = np.asarray(k_head, dtype=dtype)
+    n, d = k_head.shape
+    if k_codes is None:
+        k_codes = key_codes_one_head(k_head, w_kr, codebook_head, b, temperature, dtype=dtype)
+    n_codes = np.asarray(codebook_head).shape[0]
+    q_rows = np.asarray(q_rows, dtype=dtype)
+    q_codes = query_codes_rows(q_rows, w_qr, codebook_head, a, temperature, dtype=dtype)
+    ptr, keys = build_inverted_index(k_codes[:, None, :], n_codes)
+    ptr, keys = ptr[0], keys[0]
+    qbar = q_rows.mean(axis=1)                                    # [r, d]
+    out = np.zeros((len(positions), top_k), dtype=np.int64)
+    for t, pos in enumerate(positions):
+        cand = np.concatenate([keys[ptr[c]:ptr[c + 1]] for c in q_codes[t]])
+        cand = np.unique(cand)
+        if causal:
+            cand = cand[cand <= pos]
+        sc = (k_head[cand] @ qbar[t]) / np.sqrt(d)
+        order = np.lexsort((cand, -sc))
+        out[t] = _fill_row(cand[order], cand, n, top_k)
+    return k_codes, q_codes, out
+
+
 def route(q, k, w_qr, w_kr, codebook, a, b, top_k, causal=True, temperature=1.0,
           dtype=np.float64, dense=False):
     """Full ``CodebookRouter.forward`` (ssa/router.py:73-149): indices ``[n,h_kv,k]`` int64."""
@@ -336,16 +399,21 @@ def _softmax_attend(q_grouped, k_sel, v_sel, valid, scale):
     logits = np.matmul(q_grouped, np.swapaxes(k_sel, -1, -2)) / scale         # [n, h, g, kk]
     logits = np.where(valid[:, :, None, :], logits, -np.inf)
     m = logits.max(axis=-1, keepdims=True)
+    m = np.where(np.isfinite(m), m, 0.0)                   # a row with no valid key
     p = np.exp(logits - m)
-    p /= p.sum(axis=-1, keepdims=True)
+    den = p.sum(axis=-1, keepdims=True)
+    p /= np.where(den > 0, den, 1.0)
     return np.matmul(p, v_sel)
 
 
 def sparse_attention(q, k, v, indices, scale=None, causal=False, dtype=np.float64,
-                     q_offset=0):
+                     q_offset=0, positions=None):
     """Stage 3 with the per-head gather ``k[idx, h]`` (ssa/attention.py:12-115,
     corrected).  ``scale`` divides the logits (default ``sqrt(d)``,
-    ssa/attention.py:37-38,107).  ``causal`` masks keys ``j > i + q_offset``.
+    ssa/attention.py:37-38,107).  ``causal`` masks keys ``j > i + q_offset``,
+    or ``j > positions[i]`` when the rows of ``q`` are a sample at the
+    sequence positions ``positions``.  A row with no valid key is zero (the
+    reference never masks here; the build defines the empty softmax as 0).
     Duplicate indices count once per occurrence, like the reference's gather."""
     q = np.asarray(q, dtype=dtype)
     k = np.asarray(k, dtype=dtype)
@@ -360,7 +428,8 @@ def sparse_attention(q, k, v, indices, scale=None, causal=False, dtype=np.float6
     k_sel = k[idx, hh]                                    # [n, h_kv, kk, d]
     v_sel = v[idx, hh]
     if causal:
-        valid = idx <= (np.arange(n) + q_offset)[:, None, None]
+        pos = np.arange(n) + q_offset if positions is None else np.asarray(positions)
+        valid = idx <= pos[:, None, None]
     else:
         valid = np.ones(idx.shape, dtype=bool)
     out = _softmax_attend(q.reshape(n, h_kv, g, d), k_sel, v_sel, valid, scale)
@@ -433,11 +502,16 @@ def rope_reference(x, freqs):
 
 
 def module_forward(x, weights, h_q, h_kv, d, n_codes, a, b, top_k, freqs=None,
-                   position_ids=None, temperature=1.0):
+                   position_ids=None, temperature=1.0, indices=None, return_attn=False):
     """``SSAAttention.forward`` (ssa/ssa_layer.py:68-138) with the oracle's
     corrections: projections, per-batch RoPE quirk, router, stage 3 with the
     causal mask, ``o_proj``.  ``weights`` maps the reference state_dict keys
-    (``q_proj.weight`` ... ``router.codebook``) to arrays."""
+    (``q_proj.weight`` ... ``router.codebook``) to arrays.
+
+    ``indices [B, n, h_kv, k]``, if given, replace the router's selection (to
+    check stage 3 and ``o_proj`` on another implementation's selection);
+    ``return_attn`` adds the stage-3 output ``[B, n, h_q, d]`` (the input of
+    ``o_proj``) to the result."""
     x = np.asarray(x, dtype=np.float64)
     bsz, n, _ = x.shape
     w = {kk: np.asarray(v, dtype=np.float64) for kk, v in weights.items()}
@@ -450,12 +524,18 @@ def module_forward(x, weights, h_q, h_kv, d, n_codes, a, b, top_k, freqs=None,
         if freqs is not None:
             fb = freqs[position_ids[bi]] if position_ids is not None else freqs[:n]
             qb, kb = rope_reference(qb, fb), rope_reference(kb, fb)
-        idx = route(qb, kb, w["router.W_qr.weight"], w["router.W_kr.weight"],
-                    w["router.codebook"], a, b, top_k, causal=True, temperature=temperature)
+        if indices is None:
+            idx = route(qb, kb, w["router.W_qr.weight"], w["router.W_kr.weight"],
+                        w["router.codebook"], a, b, top_k, causal=True, temperature=temperature)
+        else:
+            idx = np.asarray(indices[bi], dtype=np.int64)
         idxs.append(idx)
         outs.append(sparse_attention(qb, kb, v[bi], idx, causal=True))
-    o = np.stack(outs).reshape(bsz, n, h_q * d)
-    return o @ w["o_proj.weight"].T, np.stack(idxs)
+    attn = np.stack(outs)
+    y = attn.reshape(bsz, n, h_q * d) @ w["o_proj.weight"].T
+    if return_attn:
+        return y, np.stack(idxs), attn
+    return y, np.stack(idxs)
 
 
 # ---------------------------------------------------------------------------

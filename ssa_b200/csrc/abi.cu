@@ -118,6 +118,9 @@ ssa_status check_route(const SsaRouteArgs* a, bool need_q, bool need_stage2) {
   }
   if (static_cast<int64_t>(a->n) * a->b >= (1ll << 31))
     return fail(SSA_ERR_UNSUPPORTED, "n * codes_per_key must be < 2^31");
+  // the re-score numbers its (sequence, KV head, query) units with 32-bit ints
+  if (static_cast<int64_t>(a->batch) * a->h_kv * std::max(a->n_q, a->n) >= (1ll << 31))
+    return fail(SSA_ERR_UNSUPPORTED, "batch * num_kv_heads * seq_len must be < 2^31");
   if (!(a->temperature > 0.f)) return fail(SSA_ERR_INVALID_ARG, "temperature must be > 0");
   if (!valid_dtype(a->dtype) || !valid_dtype(a->w_dtype))
     return fail(SSA_ERR_INVALID_ARG, "bad dtype");
@@ -326,6 +329,8 @@ ssa_status attn_params(const SsaAttnArgs* a, ssa::AttnParams& p) {
   if (a->h_kv < 1 || a->h_q % a->h_kv != 0)
     return fail(SSA_ERR_INVALID_ARG, "num_q_heads (%d) must be a multiple of num_kv_heads (%d)", a->h_q, a->h_kv);
   if (a->h_q / a->h_kv > 16) return fail(SSA_ERR_UNSUPPORTED, "GQA group size %d > 16", a->h_q / a->h_kv);
+  if (static_cast<int64_t>(a->batch) * a->h_kv * a->n_q >= (1ll << 31))
+    return fail(SSA_ERR_UNSUPPORTED, "batch * num_kv_heads * query rows must be < 2^31");
   if (a->d < 8 || a->d > 256 || a->d % 8 != 0)
     return fail(SSA_ERR_UNSUPPORTED, "head_dim %d: need a multiple of 8 in [8, 256]", a->d);
   if (!valid_dtype(a->dtype)) return fail(SSA_ERR_INVALID_ARG, "bad dtype");

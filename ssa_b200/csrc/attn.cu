@@ -139,7 +139,7 @@ __global__ void __launch_bounds__(kAttnWarps * kWarp) sparse_attn_kernel(AttnPar
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
     if (gg < g && has_dims) {
-      const float inv = 1.0f / l;
+      const float inv = l > 0.f ? 1.0f / l : 0.f;   // no valid key: a zero row
 #pragma unroll
       for (int t = 0; t < DPL; ++t)
         if (dim0 + t < d) orow[gg * p.o_sh + dim0 + t] = Elem<T>::from_f(o[gg][t] * inv);

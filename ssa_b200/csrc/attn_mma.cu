@@ -263,7 +263,9 @@ __global__ void __launch_bounds__(kMmaWarps * kWarp) sparse_attn_mma_kernel(Attn
       t += __shfl_xor_sync(0xffffffffu, t, 4);
       t += __shfl_xor_sync(0xffffffffu, t, 8);
       t += __shfl_xor_sync(0xffffffffu, t, 16);
-      inv[e] = 1.0f / t;
+      // a head with no valid key (every index masked) has t = 0 and o = 0:
+      // its output row is written as zeros
+      inv[e] = t > 0.f ? 1.0f / t : 0.f;
     }
     const int head = nt * 8 + gid;
     uint32_t* dst = reinterpret_cast<uint32_t*>(orow + static_cast<int64_t>(head < g ? head : 0) * p.o_sh);

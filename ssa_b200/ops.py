@@ -18,18 +18,14 @@ reference's unbatched ``[n, h, d]`` forms.
 from __future__ import annotations
 
 import ctypes
-import os
 from typing import Optional, Tuple
 
 import torch
 
 from . import _lib as L
+from . import _status as S
 
 _DT = {torch.float32: L.SSA_F32, torch.bfloat16: L.SSA_BF16, torch.float16: L.SSA_F16}
-
-
-def _checked() -> bool:
-    return os.environ.get("SSA_CHECKED", "1") != "0"
 
 
 def _require_cuda(*ts: torch.Tensor) -> torch.device:
@@ -121,15 +117,13 @@ def route(q: torch.Tensor, k: torch.Tensor, w_qr: torch.Tensor, w_kr: torch.Tens
     counts = torch.empty((B, n_q, h_kv), dtype=torch.int32, device=dev)
     args = route_args(q, k, w_qr, w_kr, codebook, a, b, top_k, causal, temperature, q_offset,
                       indices, index_i64, q_codes, k_codes, counts)
-    check = _checked() and not torch.cuda.is_current_stream_capturing()
-    status = torch.zeros(1, dtype=torch.int32, device=dev) if check else None
-    args.status = _ptr(status)
+    slot = S.acquire(dev)
+    args.status = slot.ptr if slot is not None else None
     ws = workspace(args, dev)
     with torch.cuda.device(dev):
         L.check("ssa_route", L.lib().ssa_route(ctypes.byref(args), ws.data_ptr(), ws.numel(),
                                                _stream(dev)))
-    if status is not None and int(status.item()) & L.SSA_DEVICE_TIMEOUT:
-        raise RuntimeError("ssa_route: a device pipeline wait timed out; results are undefined")
+        S.release(slot, "ssa_route", S.route_error)
     return indices, q_codes, k_codes, counts
 
 
@@ -203,15 +197,13 @@ def route_rope(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin: torch.T
     rope.q_out_stride_b, rope.q_out_stride_n, rope.q_out_stride_h = q_rot.stride(0), q_rot.stride(1), q_rot.stride(2)
     rope.k_out = k_rot.data_ptr()
     rope.k_out_stride_b, rope.k_out_stride_n, rope.k_out_stride_h = k_rot.stride(0), k_rot.stride(1), k_rot.stride(2)
-    check = _checked() and not torch.cuda.is_current_stream_capturing()
-    status = torch.zeros(1, dtype=torch.int32, device=dev) if check else None
-    args.status = _ptr(status)
+    slot = S.acquire(dev)
+    args.status = slot.ptr if slot is not None else None
     ws = workspace(args, dev)
     with torch.cuda.device(dev):
         L.check("ssa_route_rope", L.lib().ssa_route_rope(ctypes.byref(args), ctypes.byref(rope), ws.data_ptr(),
                                                          ws.numel(), _stream(dev)))
-    if status is not None and int(status.item()) & L.SSA_DEVICE_TIMEOUT:
-        raise RuntimeError("ssa_route_rope: a device pipeline wait timed out; results are undefined")
+        S.release(slot, "ssa_route_rope", S.route_error)
     return indices, q_codes, k_codes, counts, q_rot, k_rot
 
 
@@ -249,20 +241,14 @@ def route_with_key_codes(q: torch.Tensor, k: torch.Tensor, k_codes: torch.Tensor
                           device=dev)
     args = route_args(q, k, w_qr, w_kr, codebook, a, kc.shape[-1], top_k, causal, temperature,
                       q_offset, indices, index_i64, None, kc, None)
-    check = _checked() and not torch.cuda.is_current_stream_capturing()
-    status = torch.zeros(1, dtype=torch.int32, device=dev) if check else None
-    args.status = _ptr(status)
+    slot = S.acquire(dev)
+    args.status = slot.ptr if slot is not None else None
     ws = workspace(args, dev)
     with torch.cuda.device(dev):
         L.check("ssa_route_with_key_codes",
                 L.lib().ssa_route_with_key_codes(ctypes.byref(args), ws.data_ptr(), ws.numel(),
                                                  _stream(dev)))
-    if status is not None:
-        bits = int(status.item())
-        if bits & L.SSA_DEVICE_BAD_CODE:
-            raise ValueError(f"ssa_route_with_key_codes: a key code is outside [0, {codebook.shape[-2]})")
-        if bits & L.SSA_DEVICE_TIMEOUT:
-            raise RuntimeError("ssa_route_with_key_codes: a device pipeline wait timed out")
+        S.release(slot, "ssa_route_with_key_codes", S.route_error)
     return indices
 
 
@@ -299,22 +285,14 @@ def route_with_index(q: torch.Tensor, k: torch.Tensor, k_codes: torch.Tensor, bu
                           device=dev)
     args = route_args(q, k, w_qr, w_kr, codebook, a, kc.shape[-1], top_k, causal, temperature,
                       q_offset, indices, index_i64, None, kc, None)
-    check = _checked() and not torch.cuda.is_current_stream_capturing()
-    status = torch.zeros(1, dtype=torch.int32, device=dev) if check else None
-    args.status = _ptr(status)
+    slot = S.acquire(dev)
+    args.status = slot.ptr if slot is not None else None
     ws = workspace(args, dev)
     with torch.cuda.device(dev):
         L.check("ssa_route_with_index",
                 L.lib().ssa_route_with_index(ctypes.byref(args), ptr.data_ptr(), keys.data_ptr(), ws.data_ptr(),
                                              ws.numel(), _stream(dev)))
-    if status is not None:
-        bits = int(status.item())
-        if bits & L.SSA_DEVICE_BAD_INDEX:
-            raise ValueError("ssa_route_with_index: the code->key index failed its check")
-        if bits & L.SSA_DEVICE_BAD_CODE:
-            raise ValueError(f"ssa_route_with_index: a code is outside [0, {n_codes})")
-        if bits & L.SSA_DEVICE_TIMEOUT:
-            raise RuntimeError("ssa_route_with_index: a device pipeline wait timed out")
+        S.release(slot, "ssa_route_with_index", S.route_error)
     return indices
 
 
@@ -389,15 +367,11 @@ def sparse_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices: torc
         raise TypeError(f"indices must be int64 or int32, got {indices.dtype}")
     q, k, v, indices = _last_contig(q), _last_contig(k), _last_contig(v), _last_contig(indices)
     out = torch.empty(q.shape, dtype=q.dtype, device=dev)
-    check = _checked() and not torch.cuda.is_current_stream_capturing()
-    status = torch.zeros(1, dtype=torch.int32, device=dev) if check else None
-    args = attn_args(q, k, v, indices, out, scale, causal, q_offset, status)
+    slot = S.acquire(dev)
+    args = attn_args(q, k, v, indices, out, scale, causal, q_offset, slot.ptr if slot is not None else None)
     with torch.cuda.device(dev):
         L.check("ssa_sparse_attn", L.lib().ssa_sparse_attn(ctypes.byref(args), _stream(dev)))
-    if status is not None:
-        bits = int(status.item())
-        if bits & L.SSA_DEVICE_INDEX_OOB:
-            raise IndexError(f"sparse_exact_attention: an index is outside [0, {k.shape[1]})")
+        S.release(slot, "sparse_exact_attention", S.attn_error)
     return out
 
 
@@ -422,15 +396,13 @@ def sparse_attn_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indi
     dq = torch.empty_like(q)
     dk = torch.empty((B, n, h_kv, d), dtype=torch.float32, device=dev)
     dv = torch.empty((B, n, h_kv, d), dtype=torch.float32, device=dev)
-    check = _checked() and not torch.cuda.is_current_stream_capturing()
-    status = torch.zeros(1, dtype=torch.int32, device=dev) if check else None
-    args = attn_args(q, k, v, indices, out, scale, causal, q_offset, status)
+    slot = S.acquire(dev)
+    args = attn_args(q, k, v, indices, out, scale, causal, q_offset, slot.ptr if slot is not None else None)
     with torch.cuda.device(dev):
         L.check("ssa_sparse_attn_backward",
                 L.lib().ssa_sparse_attn_backward(ctypes.byref(args), d_out.data_ptr(), dq.data_ptr(),
                                                  dk.data_ptr(), dv.data_ptr(), _stream(dev)))
-    if status is not None and int(status.item()) & L.SSA_DEVICE_INDEX_OOB:
-        raise IndexError(f"sparse_exact_attention backward: an index is outside [0, {n})")
+        S.release(slot, "sparse_exact_attention backward", S.attn_error)
     return dq, dk.to(k.dtype), dv.to(v.dtype)
 
 
@@ -470,17 +442,29 @@ def select_from_scores(scores: torch.Tensor, kk: int) -> torch.Tensor:
     return out.reshape(*scores.shape[:-1], kk)
 
 
+def index_args(B: int, n: int, h_kv: int, b: int, n_codes: int, placeholder: torch.Tensor) -> L.SsaRouteArgs:
+    """:class:`SsaRouteArgs` for the index-only calls (``ssa_build_index`` and
+    ``ssa_build_index_noalloc``), which read the sizes and nothing else: the
+    pointers the argument check wants set all name ``placeholder`` (any
+    16-byte-aligned device buffer; it is never read) and the strides are 0."""
+    args = L.SsaRouteArgs()
+    args.batch, args.n, args.n_q, args.q_offset = B, n, 0, 0
+    args.h_q, args.h_kv, args.d, args.d_s = h_kv, h_kv, 8, 4
+    args.n_codes, args.a, args.b, args.top_k = n_codes, 1, b, 1
+    args.causal, args.temperature = 0, 1.0
+    args.dtype, args.w_dtype, args.codebook_heads = L.SSA_F32, L.SSA_F32, 1
+    p = placeholder.data_ptr()
+    args.q = args.k = args.w_qr = args.w_kr = args.codebook = p
+    return args
+
+
 def build_index(k_codes: torch.Tensor, n_codes: int, h_q: int = 1):
     """Inverted index of ``k_codes [B, n, h_kv, b]`` -> ``(bucket_ptr, bucket_keys)``."""
     dev = _require_cuda(k_codes)
     kc = k_codes.to(torch.int32).contiguous()
     B, n, h_kv, b = kc.shape
-    dummy_k = torch.empty((B, n, h_kv, 8), dtype=torch.float32, device=dev)
-    w = torch.empty((4, 8), dtype=torch.float32, device=dev)
-    cb = torch.empty((1, n_codes, 4), dtype=torch.float32, device=dev)
-    args = route_args(dummy_k, dummy_k, w, w, cb, 1, b, 1, False, 1.0, 0)
-    args.h_q = h_kv
     ptr = torch.empty((B, h_kv, n_codes + 1), dtype=torch.int32, device=dev)
+    args = index_args(B, n, h_kv, b, n_codes, ptr)
     keys = torch.empty((B, h_kv, n * b), dtype=torch.int32, device=dev)
     ws = workspace(args, dev)
     with torch.cuda.device(dev):

@@ -62,10 +62,22 @@ def is_lower_triangular_mask(mask: torch.Tensor) -> bool:
 
 
 def expand_kv_for_gqa(kv: torch.Tensor, num_q_heads: int, num_kv_heads: int) -> torch.Tensor:
-    """Repeat each KV head ``num_q_heads // num_kv_heads`` times (ssa/utils.py:89-106)."""
+    """``[..., h_kv, d]`` -> ``[..., h_q, d]`` exactly as the reference helper
+    returns it (ssa/utils.py:89-106): the whole run of KV heads is tiled
+    ``num_q_heads // num_kv_heads`` times, so query head ``j`` gets KV head
+    ``j % num_kv_heads``.
+
+    Note that this is not the pairing the attention itself uses: the router,
+    ``sparse_exact_attention`` and ``dense_attention`` (here and in the
+    reference, ssa/router.py:108-112, ssa/attention.py:143-146) give query head
+    ``j`` KV head ``j // (num_q_heads // num_kv_heads)``.  The helper keeps the
+    reference's output because it is part of the public API; nothing on the
+    hot path calls it."""
     if num_q_heads % num_kv_heads:
         raise ValueError("num_q_heads must be divisible by num_kv_heads")
-    return kv.repeat_interleave(num_q_heads // num_kv_heads, dim=-2)
+    g = num_q_heads // num_kv_heads
+    tiled = kv.unsqueeze(-3).expand(*kv.shape[:-2], g, kv.shape[-2], kv.shape[-1])
+    return tiled.reshape(*kv.shape[:-2], num_q_heads, kv.shape[-1])
 
 
 def validate_indices(indices: torch.Tensor, seq_len: int, max_k: int, name: str = "indices") -> None:

@@ -25,6 +25,10 @@ Each fixture stores seeded inputs together with the outputs of the
   RoPE, ``num_kv_heads = 1``; the RoPE'd ``q``/``k`` handed to the router
   (captured at ssa/ssa_layer.py:129) and the rows whose selection is well
   defined.
+* ``gqa_expand.npz`` -- ``expand_kv_for_gqa`` (ssa/utils.py:89-106) on
+  unbatched and batched inputs for several group sizes.
+
+``--only gqa_expand`` writes that one fixture and leaves the others as they are.
 
 The reference directory is read-only, so bytecode writing is disabled.
 """
@@ -48,12 +52,29 @@ def _import_reference():
     return ssa
 
 
+def gqa_expand(ssa):
+    import numpy as np
+    import torch
+
+    torch.manual_seed(31)
+    out = {}
+    for name, shape, h_q in (("u", (5, 2, 3), 6), ("b", (2, 4, 3, 8), 12), ("one", (3, 1, 4), 4)):
+        kv = torch.randn(*shape)
+        out[f"kv_{name}"] = kv.numpy()
+        out[f"out_{name}"] = ssa.expand_kv_for_gqa(kv, h_q, shape[-2]).numpy()
+        out[f"hq_{name}"] = np.array(h_q)
+    np.savez_compressed(os.path.join(HERE, "gqa_expand.npz"), **out)
+
+
 def main():
     import numpy as np
     import torch
 
     ssa = _import_reference()
     torch.set_num_threads(max(1, os.cpu_count() or 1))
+    gqa_expand(ssa)
+    if "--only" in sys.argv:
+        return
 
     # ---------------- stage 1 + 2 ----------------
     torch.manual_seed(1234)

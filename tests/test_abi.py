@@ -111,6 +111,8 @@ def test_workspace_grows_with_the_query_units(lib):
     (dict(k=0x2004), 4),              # misaligned k
     (dict(q_offset=10), 1),           # q_offset + n_q > n
     (dict(top_k=20000, n=20000, n_q=20000), 2),  # min(k, n) above the shared-memory capacity
+    # 2^31 (sequence, KV head, query) units: the re-score numbers units with 32-bit ints
+    (dict(batch=1 << 14, h_kv=8, n=1 << 14, n_q=1 << 14, top_k=16), 2),
 ])
 def test_route_argument_errors(lib, over, code):
     a = _route_args(**over)
@@ -135,6 +137,10 @@ def test_attn_argument_errors(lib):
     a.h_q = 8
     a.d = 12
     assert lib.ssa_sparse_attn(ctypes.byref(a), None) == 2
+    a.d = 64
+    a.batch, a.n_q, a.n = 1 << 14, 1 << 16, 1 << 16          # 2^31 (sequence, head, query) units
+    assert lib.ssa_sparse_attn(ctypes.byref(a), None) == 2
+    assert b"2^31" in lib.ssa_last_error()
     assert lib.ssa_sparse_attn(None, None) == 1
 
 

@@ -98,9 +98,16 @@ def test_dense_attention_torch_path_matches_oracle():
 
 
 def test_expand_kv_and_validate_indices():
+    # the reference's own outputs (tests/golden/make_golden.py): head tiling,
+    # query head j -> KV head j % h_kv
+    z = np.load(os.path.join(os.path.dirname(__file__), "golden", "gqa_expand.npz"))
+    for name in ("u", "b", "one"):
+        kv = torch.from_numpy(z[f"kv_{name}"])
+        e = ssa.expand_kv_for_gqa(kv, int(z[f"hq_{name}"]), kv.shape[-2])
+        assert torch.equal(e, torch.from_numpy(z[f"out_{name}"])), name
     kv = torch.randn(5, 2, 3)
     e = ssa.expand_kv_for_gqa(kv, 6, 2)
-    assert e.shape == (5, 6, 3) and torch.equal(e[:, 2], kv[:, 0]) and torch.equal(e[:, 3], kv[:, 1])
+    assert [torch.equal(e[:, j], kv[:, j % 2]) for j in range(6)] == [True] * 6
     ssa.validate_indices(torch.zeros(4, 1, 3, dtype=torch.long), 4, 3)
     with pytest.raises(ValueError):
         ssa.validate_indices(torch.full((4, 1, 3), 4), 4, 3)

@@ -113,8 +113,69 @@ def test_out_of_range_index_raises():
     k = torch.randn(8, 2, 16, device=DEV)
     idx = torch.zeros(8, 2, 4, dtype=torch.long, device=DEV)
     idx[3, 1, 2] = 8
+    # the device status word is read lazily: the error comes at check_errors()
+    # (or at a later op call), without a host synchronisation after the op
     with pytest.raises(IndexError):
         ssa.sparse_exact_attention(q, k, k, idx)
+        ssa.check_errors()
+    ssa.check_errors()                                    # nothing left pending
+
+
+def test_out_of_range_index_raises_at_the_next_op_call():
+    q = torch.randn(8, 4, 16, device=DEV)
+    k = torch.randn(8, 2, 16, device=DEV)
+    idx = torch.zeros(8, 2, 4, dtype=torch.long, device=DEV)
+    idx[0, 0, 0] = -3
+    ssa.sparse_exact_attention(q, k, k, idx)
+    torch.cuda.synchronize()
+    with pytest.raises(IndexError):
+        ssa.sparse_exact_attention(q, k, k, torch.zeros_like(idx))
+    ssa.check_errors()
+
+
+def test_sync_mode_raises_in_the_failing_call(monkeypatch):
+    monkeypatch.setenv("SSA_CHECKED", "sync")
+    q = torch.randn(8, 4, 16, device=DEV)
+    k = torch.randn(8, 2, 16, device=DEV)
+    idx = torch.zeros(8, 2, 4, dtype=torch.long, device=DEV)
+    idx[5, 0, 1] = 99
+    with pytest.raises(IndexError):
+        ssa.sparse_exact_attention(q, k, k, idx)
+    monkeypatch.setenv("SSA_CHECKED", "0")              # no status word at all
+    ssa.sparse_exact_attention(q, k, k, idx)
+    ssa.check_errors()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_fully_masked_rows_are_zero(dtype):
+    """With is_causal=True a row whose indices all lie after its position has
+    no valid key; its output is a zero row (no NaN), other rows are unchanged,
+    and its gradient is zero."""
+    rng = np.random.default_rng(21)
+    n, h_q, h_kv, d, kk = 64, 8, 2, 128, 16
+    qn, kn, vn, idx, (q, k, v) = _inputs(rng, n, h_q, h_kv, d, kk, dtype)
+    idx[..., 0] = rng.integers(0, np.arange(n) + 1)[None, :, None]
+    dead = [(3, 0), (10, 1), (40, 0)]
+    for i, h in dead:
+        idx[0, i, h] = rng.integers(i + 1, n, size=kk)
+    it = torch.from_numpy(idx[0]).to(DEV)
+    out = ssa.sparse_exact_attention(q[0], k[0], v[0], it, is_causal=True)
+    g = h_q // h_kv
+    for i, h in dead:
+        assert torch.count_nonzero(out[i, h * g:(h + 1) * g]) == 0
+    assert torch.isfinite(out).all()
+    keep = np.ones((n, h_q), dtype=bool)
+    for i, h in dead:
+        keep[i, h * g:(h + 1) * g] = False
+    ref = O.sparse_attention(qn[0], kn[0], vn[0], idx[0], causal=True)
+    _close(out.cpu()[torch.from_numpy(keep)], ref[keep], dtype)
+    # backward: the dead rows get a zero gradient, everything stays finite
+    qg = q[0].clone().requires_grad_()
+    o = ssa.sparse_exact_attention(qg, k[0], v[0], it, is_causal=True)
+    o.float().sum().backward()
+    assert torch.isfinite(qg.grad).all()
+    for i, h in dead:
+        assert torch.count_nonzero(qg.grad[i, h * g:(h + 1) * g]) == 0
 
 
 def test_out_of_range_index_raises_on_the_tensor_core_path():
@@ -125,6 +186,7 @@ def test_out_of_range_index_raises_on_the_tensor_core_path():
         idx[17, 1, 20] = bad
         with pytest.raises(IndexError):
             ssa.sparse_exact_attention(q, k, k, idx)
+            ssa.check_errors()
 
 
 def test_deterministic():

@@ -1,0 +1,210 @@
+"""Parity against the oracle at the benchmark configurations' own sizes.
+
+The oracle's O(n^2)-free, per-head, sampled-row form
+(``O.route_rows_one_head``, itself pinned to the full oracle on CPU) checks
+the CUDA path where the benchmarks run it:
+
+* config 3 at n = 32768 (the headline): 2 KV heads, ~2k query rows spread
+  over every position including the last block;
+* config 4's routing shape (n = 131072, N_c = 8192, k = 512) on one GPU: rows
+  from every zig-zag block of an 8-rank split, where the second and third
+  re-score tiers do most of the work;
+* GQA groups g = 7 (config 5's 28/4 heads, also through the fused-RoPE call)
+  and g = 3, every row;
+* config 1 at its stated shape through ``SSAAttention`` (fp32, RoPE).
+
+Bars (north star): code rows and final candidate sets >= 99.9% equal to the
+oracle's; stage-3 outputs within tests/_tol.py (2e-3 relative for bf16,
+1e-5 for fp32) against the oracle evaluated on the GPU's own selection.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import ssa_b200 as ssa
+from oracle import ssa_oracle as O
+from ssa_b200 import ops
+from ssa_b200 import workloads as W
+from _tol import assert_output_close
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _router(shape, t=None):
+    r = ssa.CodebookRouter(head_dim=shape.d, route_dim=shape.d_s, num_kv_heads=shape.h_kv,
+                           num_codebook=shape.n_codes, codes_per_key=shape.b, codes_per_query=shape.a,
+                           top_k=shape.top_k).to(DEV)
+    if t is not None:
+        with torch.no_grad():
+            r.W_qr.weight.copy_(t["w_qr"])
+            r.W_kr.weight.copy_(t["w_kr"])
+            r.codebook.copy_(t["codebook"])
+    return r
+
+
+def _same_rows(a, b):
+    """Fraction of rows whose code sets are equal."""
+    return float((np.sort(a, -1) == np.sort(b, -1)).all(-1).mean())
+
+
+def _overlap(a, b):
+    """Mean |set(a_row) & set(b_row)| / k over the rows of [..., k] index arrays."""
+    a = np.sort(a.reshape(-1, a.shape[-1]), axis=1)
+    b = np.sort(b.reshape(-1, b.shape[-1]), axis=1)
+    return sum(np.intersect1d(x, y).size for x, y in zip(a, b)) / a.size
+
+
+def _np(x):
+    return x.double().cpu().numpy()
+
+
+def _check_sampled(t, shape, idx, q_codes, k_codes, out, rows, heads):
+    """Oracle comparison of the GPU's codes, indices and output at the given
+    rows of the given KV heads.  Returns a dict of the measured figures."""
+    g = shape.h_q // shape.h_kv
+    w_qr, w_kr = _np(t["w_qr"]), _np(t["w_kr"])
+    rows_t = torch.from_numpy(rows).to(DEV)
+    res = {}
+    for h in heads:
+        k_h = _np(t["k"][0, :, h])
+        q_rows = _np(t["q"][0, rows_t, h * g:(h + 1) * g])
+        kc, qc, ref_idx = O.route_rows_one_head(q_rows, rows, k_h, w_qr, w_kr, _np(t["codebook"][h]),
+                                                shape.a, shape.b, shape.top_k, causal=True)
+        k_same = _same_rows(k_codes[0, :, h].cpu().numpy(), kc)
+        q_same = _same_rows(q_codes[0, rows_t, h].cpu().numpy(), qc)
+        gpu_idx = idx[0, rows_t, h].long().cpu().numpy()
+        ov = _overlap(gpu_idx, ref_idx)
+        assert k_same >= 0.999 and q_same >= 0.999, (h, k_same, q_same)
+        assert ov >= 0.999, (h, ov)
+        # stage 3 on the GPU's own selection, against the oracle on the same one
+        ref_out = O.sparse_attention(q_rows, k_h[:, None], _np(t["v"][0, :, h])[:, None], gpu_idx[:, None],
+                                     causal=True, positions=rows)
+        got = out[0, rows_t, h * g:(h + 1) * g]
+        assert_output_close(got, ref_out, torch.bfloat16)
+        res[h] = dict(k_codes=k_same, q_codes=q_same, overlap=ov)
+    return res
+
+
+def _sample_rows(rng, n, count, tail):
+    rows = np.concatenate([rng.choice(n, size=count, replace=False), np.arange(n - tail, n), np.arange(8)])
+    return np.unique(rows)
+
+
+def test_config3_headline_n32768_sampled_rows():
+    shape = W.CONFIG3                                     # n = 32768, k = 256, bf16
+    t = W.make_inputs(shape, seed=0, dtype=torch.bfloat16)
+    r = _router(shape, t)
+    idx, q_codes, k_codes, counts = r.route(t["q"], t["k"], causal=True, index_dtype=torch.int32)
+    out = ssa.sparse_exact_attention(t["q"], t["k"], t["v"], idx, is_causal=True)
+    ssa.check_errors()
+    rows = _sample_rows(np.random.default_rng(1), shape.n, 1920, 128)
+    _check_sampled(t, shape, idx, q_codes, k_codes, out, rows, heads=(0, 5))
+    # the sample covers the filler regime and the above-k regime
+    c = counts[0, torch.from_numpy(rows).to(DEV)].cpu().numpy()
+    assert (c < shape.top_k).any() and (c > shape.top_k).any()
+
+
+def test_config4_routing_shape_rows_of_every_zigzag_block():
+    shape = W.CONFIG4                                     # n = 131072, N_c = 8192, k = 512
+    t = W.make_inputs(shape, seed=4, dtype=torch.bfloat16, planted=False, generate_on_device=True)
+    r = _router(shape, t)
+    idx, q_codes, k_codes, counts = r.route(t["q"], t["k"], causal=True, index_dtype=torch.int32)
+    out = ssa.sparse_exact_attention(t["q"], t["k"], t["v"], idx, is_causal=True)
+    ssa.check_errors()
+    world = 8
+    blk = shape.n // (2 * world)
+    rng = np.random.default_rng(2)
+    rows = np.unique(np.concatenate([s * blk + rng.choice(blk, size=48, replace=False)
+                                     for s in range(2 * world)] + [np.array([shape.n - 1])]))
+    _check_sampled(t, shape, idx, q_codes, k_codes, out, rows, heads=(3,))
+    # the rows hit the second and third re-score tiers (more than 512 / 1024 candidates)
+    c = counts[0, torch.from_numpy(rows).to(DEV), 3].cpu().numpy()
+    assert (c > 512).any() and (c > 1024).any(), (c.max(), np.percentile(c, 90))
+    # a rank's query-split call (route_with_index at the block's offset) gives the same rows
+    index = r.key_index(k_codes)
+    for s in (0, 2 * world - 1):
+        got = r.route_with_index(t["q"][:, s * blk:(s + 1) * blk], t["k"], k_codes, index, causal=True,
+                                 q_offset=s * blk, index_dtype=torch.int32)
+        assert torch.equal(got, idx[:, s * blk:(s + 1) * blk]), s
+
+
+@pytest.mark.parametrize("h_q,h_kv", [(28, 4), (12, 4)])
+def test_non_power_of_two_groups_match_oracle(h_q, h_kv):
+    """g = 7 (config 5's heads) and g = 3: the K = g*d routing projection, the
+    group-mean query and the re-score's qbar against the oracle, every row."""
+    shape = W.Shape(n=4096, h_q=h_q, h_kv=h_kv, d=128, d_s=32, n_codes=4096, a=16, b=4, top_k=256)
+    t = W.make_inputs(shape, seed=h_q, dtype=torch.bfloat16)
+    r = _router(shape, t)
+    idx, q_codes, k_codes, _ = r.route(t["q"], t["k"], causal=True)
+    qn, kn = _np(t["q"][0]), _np(t["k"][0])
+    oq, ok = O.route_codes(qn, kn, _np(t["w_qr"]), _np(t["w_kr"]), _np(t["codebook"]), shape.a, shape.b)
+    assert _same_rows(q_codes[0].cpu().numpy(), oq) >= 0.999
+    assert _same_rows(k_codes[0].cpu().numpy(), ok) >= 0.999
+    ref = O.select_topk_index(qn, kn, oq, ok, shape.n_codes, shape.top_k, causal=True)
+    assert _overlap(idx[0].cpu().numpy(), ref) >= 0.999
+    out = ssa.sparse_exact_attention(t["q"][0], t["k"][0], t["v"][0], idx[0], is_causal=True)
+    assert_output_close(out, O.sparse_attention(qn, kn, _np(t["v"][0]), idx[0].cpu().numpy(), causal=True),
+                        torch.bfloat16)
+
+
+def test_group_7_fused_rope_routing_matches_oracle():
+    """config 5's attention (28/4 heads, RoPE base 1e6) through the fused
+    RoPE + routing call, against the oracle on the rotated rows."""
+    shape = W.Shape(n=4096, h_q=28, h_kv=4, d=128, d_s=32, n_codes=4096, a=16, b=4, top_k=256)
+    t = W.make_inputs(shape, seed=55, dtype=torch.bfloat16)
+    r = _router(shape, t)
+    inv = 1.0 / (1e6 ** (torch.arange(0, 128, 2, device=DEV, dtype=torch.float32) / 128))
+    ang = torch.arange(shape.n, device=DEV, dtype=torch.float32)[:, None] * inv[None]
+    cos = torch.cat([ang.cos(), ang.cos()], -1).to(torch.bfloat16)
+    sin = torch.cat([ang.sin(), ang.sin()], -1).to(torch.bfloat16)
+    idx, q_codes, k_codes, _, q_rot, k_rot = ops.route_rope(
+        t["q"], t["k"], cos, sin, r.W_qr.weight, r.W_kr.weight, r.codebook, shape.a, shape.b, shape.top_k,
+        True, 1.0, 0, True)
+    qn, kn = _np(q_rot[0]), _np(k_rot[0])
+    oq, ok = O.route_codes(qn, kn, _np(t["w_qr"]), _np(t["w_kr"]), _np(t["codebook"]), shape.a, shape.b)
+    assert _same_rows(q_codes[0].cpu().numpy(), oq) >= 0.999
+    assert _same_rows(k_codes[0].cpu().numpy(), ok) >= 0.999
+    ref = O.select_topk_index(qn, kn, oq, ok, shape.n_codes, shape.top_k, causal=True)
+    assert _overlap(idx[0].cpu().numpy(), ref) >= 0.999
+
+
+def test_config1_stated_shape_through_ssa_attention():
+    """Config 1 as BASELINE states it: SSAAttention, batch 2, n = 1024,
+    d_model 512, 8/2 heads of 64, d_s 32, shared codebook (2048, 32), b 4,
+    a 16, k 256, causal, RoPE base 1e4, fp32, xavier-uniform weights."""
+    torch.manual_seed(101)
+    B, n, dm, hq, hkv, hd = 2, 1024, 512, 8, 2, 64
+    m = ssa.SSAAttention(hidden_size=dm, num_q_heads=hq, num_kv_heads=hkv, head_dim=hd, route_dim=32,
+                         num_codebook=2048, codes_per_key=4, codes_per_query=16, top_k=256)
+    for lin in (m.q_proj, m.k_proj, m.v_proj, m.o_proj, m.router.W_qr, m.router.W_kr):
+        torch.nn.init.xavier_uniform_(lin.weight)
+    m.router.codebook = torch.nn.Parameter(torch.randn(2048, 32) / 32 ** 0.5)
+    m = m.to(DEV)
+    x = torch.randn(B, n, dm, device=DEV)
+    freqs = ssa.precompute_rope_freqs(hd, n, 10000.0, device=DEV)
+    seen = {}
+    orig_route = m.router.route
+
+    def capture(*a, **kw):
+        res = orig_route(*a, **kw)
+        seen["idx"] = res[0]
+        return res
+
+    m.router.route = capture
+    hook = m.o_proj.register_forward_pre_hook(lambda mod, inp: seen.__setitem__("attn", inp[0].detach()))
+    with torch.no_grad():
+        y = m(x, freqs=freqs)
+    hook.remove()
+    w = {kk: v.detach().double().cpu().numpy() for kk, v in m.state_dict().items()}
+    xn = x.double().cpu().numpy()
+    fr = freqs.double().cpu().numpy()
+    # the oracle's own selection: >= 99.9% of the GPU's
+    _, ref_idx = O.module_forward(xn, w, hq, hkv, hd, 2048, 16, 4, 256, freqs=fr)
+    assert _overlap(seen["idx"].long().cpu().numpy(), ref_idx) >= 0.999
+    # stage 3 and o_proj on the GPU's selection: fp32 bound on the attention output
+    y_ref, _, attn_ref = O.module_forward(xn, w, hq, hkv, hd, 2048, 16, 4, 256, freqs=fr,
+                                          indices=seen["idx"].long().cpu().numpy(), return_attn=True)
+    assert_output_close(seen["attn"].reshape(B, n, hq, hd), attn_ref, torch.float32)
+    np.testing.assert_allclose(y.cpu().numpy(), y_ref, rtol=1e-4, atol=2e-5)

@@ -208,6 +208,7 @@ def test_route_with_key_codes_flags_codes_outside_the_codebook():
         c[0, 17, 1, 2] = bad
         with pytest.raises(ValueError, match="outside"):
             r.route_with_key_codes(q, k, c, causal=True)
+            ssa.check_errors()
     # the device word is clear again on valid codes
     r.route_with_key_codes(q, k, codes, causal=True)
     torch.cuda.synchronize()
@@ -256,5 +257,6 @@ def test_route_with_index_refuses_a_corrupt_index():
     for index in [(ptr, bad_key), (bad_order, keys), (bad_end, keys)]:
         with pytest.raises(ValueError, match="index"):
             r.route_with_index(q, k, codes, index, causal=True)
+            ssa.check_errors()
     # a valid index still gives the same result afterwards
     assert torch.equal(r.route_with_index(q, k, codes, (ptr, keys), causal=True), good)

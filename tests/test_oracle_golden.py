@@ -169,3 +169,43 @@ def test_torch_port_matches_oracle_on_tie_free_rows():
         np.testing.assert_array_equal(idx[full], idx_o[full, h])
         out = P.attention(qh, kh, vh, T(idx_o[:, h]), 0, True, block=100).numpy()
         np.testing.assert_allclose(out, out_o[:, h * g:(h + 1) * g], rtol=1e-10, atol=1e-10)
+
+
+def test_sampled_row_router_matches_the_full_oracle():
+    """route_rows_one_head (the per-head, sampled-row form the GPU tests use
+    at full benchmark sizes) equals route_codes + select_topk_index on every
+    row it is given, for causal and non-causal routing, g = 3, k > candidates."""
+    rng = np.random.default_rng(17)
+    n, h_q, h_kv, d, d_s, n_c, a, b, k = 300, 6, 2, 32, 8, 64, 6, 3, 40
+    q = rng.standard_normal((n, h_q, d))
+    kk = rng.standard_normal((n, h_kv, d))
+    w_qr = rng.standard_normal((d_s, d))
+    w_kr = rng.standard_normal((d_s, d))
+    cb = rng.standard_normal((h_kv, n_c, d_s))
+    q_codes, k_codes = O.route_codes(q, kk, w_qr, w_kr, cb, a, b)
+    g = h_q // h_kv
+    rows = np.array([0, 1, 7, 50, 151, 298, 299])
+    for causal in (True, False):
+        full = O.select_topk_index(q, kk, q_codes, k_codes, n_c, k, causal=causal)
+        for h in range(h_kv):
+            kc, qc, idx = O.route_rows_one_head(q[rows, h * g:(h + 1) * g], rows, kk[:, h], w_qr, w_kr, cb[h],
+                                                a, b, k, causal=causal)
+            np.testing.assert_array_equal(kc, k_codes[:, h])
+            np.testing.assert_array_equal(qc, q_codes[rows, h])
+            np.testing.assert_array_equal(idx, full[rows, h])
+
+
+def test_sampled_rows_of_stage3_match_the_full_rows():
+    rng = np.random.default_rng(18)
+    n, h_q, h_kv, d, k = 50, 4, 2, 16, 9
+    q, kk, v = (rng.standard_normal((n, h, d)) for h in (h_q, h_kv, h_kv))
+    idx = rng.integers(0, n, size=(n, h_kv, k))
+    full = O.sparse_attention(q, kk, v, idx, causal=True)
+    rows = np.array([0, 3, 20, 49])
+    part = O.sparse_attention(q[rows], kk, v, idx[rows], causal=True, positions=rows)
+    np.testing.assert_allclose(part, full[rows], rtol=1e-12, atol=1e-12)
+    # row 0 with every index in the future has no valid key: a zero row
+    idx0 = idx.copy()
+    idx0[0] = n - 1
+    z = O.sparse_attention(q, kk, v, idx0, causal=True)
+    assert np.all(z[0] == 0) and np.isfinite(z).all()

@@ -28,12 +28,10 @@ DEV = "cuda"
 
 
 def _args(B, n, h_kv, b, n_codes):
-    dummy_k = torch.empty((B, n, h_kv, 8), dtype=torch.float32, device=DEV)
-    w = torch.empty((4, 8), dtype=torch.float32, device=DEV)
-    cb = torch.empty((1, n_codes, 4), dtype=torch.float32, device=DEV)
-    args = ops.route_args(dummy_k, dummy_k, w, w, cb, 1, b, 1, False, 1.0, 0)
-    args.h_q = h_kv
-    return args, (dummy_k, w, cb)
+    # the index build takes no K: the args carry sizes, and the pointers the
+    # argument check wants set name one small placeholder that is never read
+    placeholder = torch.empty(4, dtype=torch.int32, device=DEV)
+    return ops.index_args(B, n, h_kv, b, n_codes, placeholder), placeholder
 
 
 def _codes(seed, B, n, h_kv, b, n_codes):
