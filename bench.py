@@ -84,7 +84,7 @@ def parse():
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--no-config4", action="store_true",
                    help="skip the config-4 (query-split n=131072) record of the default run")
-    p.add_argument("--workload", default="config3", choices=["config3", "config4", "config5"],
+    p.add_argument("--workload", default="config3", choices=["config3", "config4", "config5", "decode"],
                    help="config3: one sequence per GPU (the headline); config4: one n=131072 "
                         "sequence split by queries over the GPUs (strong scaling); config5: a Qwen-style "
                         "28-layer decoder stack with SSA attention, one batch per GPU")
@@ -826,10 +826,82 @@ def run_config5(args):
     return 0
 
 
+def run_decode(args):
+    """Per-token decode time (``ssa_b200.decode.DecodeCache.step``: the new
+    key's codes, one index append, routing of the query against the cache's
+    index, sparse attention) at cache lengths 4k / 32k / 128k, config-3 heads
+    (32 / 8 of 128, d_s 32, N_c 4096, a 16, b 4, k 256), batch 1, bf16.
+    Beside it, the same step with the index rebuilt from every cached key
+    (``route_with_key_codes``), which is what a decode loop without an
+    incremental index does.  CUDA events around ``--steps`` consecutive steps."""
+    import torch
+
+    import ssa_b200 as ssa
+    from ssa_b200 import workloads as W
+    from ssa_b200.decode import DecodeCache
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    steps = max(args.steps, 10)
+    res = {}
+    for n in (4096, 32768, 131072):
+        shape = W.Shape(**{**W.CONFIG3.asdict(), "n": n + steps})
+        t = W.make_inputs(shape, seed=args.seed, dtype=torch.bfloat16, device=dev, planted=False,
+                          generate_on_device=True)
+        r = ssa.CodebookRouter(head_dim=shape.d, route_dim=shape.d_s, num_kv_heads=shape.h_kv,
+                               num_codebook=shape.n_codes, codes_per_key=shape.b, codes_per_query=shape.a,
+                               top_k=shape.top_k).to(dev)
+        with torch.no_grad():
+            r.W_qr.weight.copy_(t["w_qr"])
+            r.W_kr.weight.copy_(t["w_kr"])
+            r.codebook.copy_(t["codebook"])
+        q, k, v = t["q"], t["k"], t["v"]
+        cache = DecodeCache(r, 1, capacity=n + steps + args.warmup, num_q_heads=shape.h_q, device=dev)
+        cache.append(k[:, :n - args.warmup], v[:, :n - args.warmup])
+        p = n - args.warmup
+        for _ in range(args.warmup):
+            cache.step(q[:, p:p + 1], k[:, p:p + 1], v[:, p:p + 1])
+            p += 1
+        rebuilds0 = cache.rebuilds
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            cache.step(q[:, p:p + 1], k[:, p:p + 1], v[:, p:p + 1])
+            p += 1
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ms_inc = e0.elapsed_time(e1) / steps
+        # the same steps with a full index build per step
+        codes = cache.codes[:, :p]
+        e0.record()
+        for s in range(steps):
+            pos = n + s
+            idx = r.route_with_key_codes(q[:, pos:pos + 1], k[:, :pos + 1], codes[:, :pos + 1], causal=True,
+                                         q_offset=pos, index_dtype=torch.int32)
+            ssa.sparse_exact_attention(q[:, pos:pos + 1], k[:, :pos + 1], v[:, :pos + 1], idx, is_causal=True,
+                                       q_offset=pos)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ssa.check_errors(dev)
+        res[str(n)] = {"ms_per_token": ms_inc, "rebuilds_in_timed_steps": cache.rebuilds - rebuilds0,
+                       "ms_per_token_full_index_build": e0.elapsed_time(e1) / steps}
+        del cache, t, q, k, v
+        torch.cuda.empty_cache()
+    print(json.dumps({"metric": "SSA decode ms per token (batch 1, config-3 heads, bf16)", "unit": "ms",
+                      "higher_is_better": False, "steps": steps, "warmup": args.warmup,
+                      "per_cache_length": res,
+                      "note": "full_index_build: route_with_key_codes (index of all cached keys rebuilt each step), "
+                              "without the key-code assignment of the new key"}), flush=True)
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "decode":
+        return run_decode(args)
     if args.workload == "config4":
         return run_config4(args)
     if args.workload == "config5":

@@ -63,6 +63,9 @@ typedef enum {
 #define SSA_DEVICE_BAD_INDEX 0x4   /* a caller-given code->key index failed its check
                                       (a bucket or a key out of range); the indices
                                       are written as zeros                          */
+#define SSA_DEVICE_INDEX_FULL 0x8  /* decode index: a bucket had no free slot; the
+                                      entry was dropped (rebuild before appending
+                                      more keys than min_free allows)               */
 #define SSA_DEVICE_TIMEOUT 0x100   /* route: a pipeline wait gave up (~1 s); the
                                       affected codes are undefined                  */
 
@@ -178,6 +181,57 @@ typedef struct {
  * SSA_ERR_UNSUPPORTED.  Workspace: ssa_route_workspace_size(args). */
 ssa_status ssa_route_rope(const SsaRouteArgs* args, const SsaRopeArgs* rope, void* workspace,
                           size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Incremental decode: the code->key index of a growing key cache            */
+/* ------------------------------------------------------------------------ */
+/* The reference has no decode path; its design notes keep the code->key
+ * index incrementally so that a decode step need not rescan the cache
+ * (ssa_design.md, incremental decode).  Bucket c of sequence bat, KV head h
+ * (bh = bat * h_kv + h) owns the slots [start[c], start[c+1]) of row bh of
+ * bucket_keys (and of bucket_codes) and holds its keys, ascending, in
+ * [start[c], end[c]).  A build gives every bucket max(slack, its size) free
+ * slots; an append writes a key's b entries at the ends of its b buckets.
+ * *min_free is the fewest free slots of any bucket: the b codes of a key are
+ * distinct, so appending t keys takes at most t slots of any bucket, and the
+ * caller rebuilds before appending more keys than *min_free. */
+typedef struct {
+  int32_t* bucket_start;   /* [B, h_kv, n_codes + 1]                              */
+  int32_t* bucket_end;     /* [B, h_kv, n_codes + 1] (the last column is unused)  */
+  int32_t* bucket_keys;    /* [B, h_kv, entry_capacity]                           */
+  int32_t* bucket_codes;   /* [B, h_kv, entry_capacity, 4], 16-byte aligned: each
+                              entry's key codes (b == 4 only; NULL otherwise)     */
+  int64_t entry_capacity;  /* slots per (sequence, KV head), see below            */
+  int32_t slack;           /* >= 1                                                 */
+  int32_t* min_free;       /* device word                                          */
+  int64_t k_codes_stride_b; /* elements between the sequences of args->k_codes (a
+                              cache of capacity C: C * h_kv * b); 0: n * h_kv * b */
+} SsaDecodeIndex;
+
+/* Slots per (sequence, KV head) that always suffice for up to max_keys keys:
+ * 2 * max_keys * b + n_codes * slack. */
+int64_t ssa_decode_index_capacity(int32_t max_keys, int32_t b, int32_t n_codes, int32_t slack);
+
+/* (Re)builds the index of the args->n cached keys from their codes
+ * args->k_codes [B, n, h_kv, b] and resets *min_free.  Workspace:
+ * ssa_route_workspace_size(args).  Replaces the per-step index build of a
+ * decode loop (the reference rebuilds its candidate mask from all keys,
+ * ssa/router.py:216-259). */
+ssa_status ssa_decode_index_build(const SsaRouteArgs* args, const SsaDecodeIndex* index, void* workspace,
+                                  size_t workspace_bytes, void* stream);
+
+/* Appends keys first .. first + count - 1 of args->k_codes (each after every
+ * key already in the index) to the index: one small launch, independent of
+ * the number of cached keys. */
+ssa_status ssa_decode_index_append(const SsaRouteArgs* args, const SsaDecodeIndex* index, int32_t first,
+                                   int32_t count, void* stream);
+
+/* CodebookRouter.forward (ssa/router.py:73-149) for args->n_q query rows at
+ * positions q_offset .. against the args->n keys of the index: the queries'
+ * codes, then the candidate union, re-score and top-k of ssa_route, with the
+ * index given (args->k_codes are the keys' codes).  Output as ssa_route. */
+ssa_status ssa_decode_route(const SsaRouteArgs* args, const SsaDecodeIndex* index, void* workspace,
+                            size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Sparse exact attention (stage 3)                                          */

@@ -19,6 +19,7 @@ SSA_I32, SSA_I64 = 0, 1
 SSA_DEVICE_INDEX_OOB = 0x1
 SSA_DEVICE_BAD_CODE = 0x2
 SSA_DEVICE_BAD_INDEX = 0x4
+SSA_DEVICE_INDEX_FULL = 0x8
 SSA_DEVICE_TIMEOUT = 0x100
 STATUS_NAMES = {0: "SSA_OK", 1: "SSA_ERR_INVALID_ARG", 2: "SSA_ERR_UNSUPPORTED", 3: "SSA_ERR_WORKSPACE",
                 4: "SSA_ERR_ALIGNMENT", 5: "SSA_ERR_CUDA", 6: "SSA_ERR_DEVICE"}
@@ -66,8 +67,22 @@ class SsaRopeArgs(ctypes.Structure):
     ]
 
 
+class SsaDecodeIndex(ctypes.Structure):
+    _fields_ = [
+        ("bucket_start", _vp), ("bucket_end", _vp), ("bucket_keys", _vp), ("bucket_codes", _vp),
+        ("entry_capacity", _c_i64), ("slack", _c_i32), ("min_free", _vp), ("k_codes_stride_b", _c_i64),
+    ]
+
+
 # exported symbol -> (restype, argtypes)
 SIGNATURES = {
+    "ssa_decode_index_capacity": (_c_i64, [_c_i32, _c_i32, _c_i32, _c_i32]),
+    "ssa_decode_index_build": (ctypes.c_int, [ctypes.POINTER(SsaRouteArgs), ctypes.POINTER(SsaDecodeIndex), _vp,
+                                              ctypes.c_size_t, _vp]),
+    "ssa_decode_index_append": (ctypes.c_int, [ctypes.POINTER(SsaRouteArgs), ctypes.POINTER(SsaDecodeIndex),
+                                               _c_i32, _c_i32, _vp]),
+    "ssa_decode_route": (ctypes.c_int, [ctypes.POINTER(SsaRouteArgs), ctypes.POINTER(SsaDecodeIndex), _vp,
+                                        ctypes.c_size_t, _vp]),
     "ssa_route_workspace_size": (ctypes.c_size_t, [ctypes.POINTER(SsaRouteArgs)]),
     "ssa_route": (ctypes.c_int, [ctypes.POINTER(SsaRouteArgs), _vp, ctypes.c_size_t, _vp]),
     "ssa_code_assign": (ctypes.c_int, [ctypes.POINTER(SsaRouteArgs), _vp, ctypes.c_size_t, _vp]),

@@ -156,6 +156,8 @@ def check_errors(device=None) -> None:
 # decoders: status bits -> the exception each op raises
 # ---------------------------------------------------------------------------
 def route_error(op: str, bits: int) -> Optional[Exception]:
+    if bits & L.SSA_DEVICE_INDEX_FULL:
+        return RuntimeError(f"{op}: a bucket of the decode index had no free slot (rebuild it first)")
     if bits & L.SSA_DEVICE_BAD_INDEX:
         return ValueError(f"{op}: the code->key index failed its check")
     if bits & L.SSA_DEVICE_BAD_CODE:

@@ -226,6 +226,7 @@ ssa::IndexParams index_params(const SsaRouteArgs& a, const RouteLayout& L, void*
   ip.counts = at<uint32_t>(ws, L.counts);
   ip.partials = at<uint32_t>(ws, L.partials);
   ip.status = a.status;
+  ip.k_codes_sb = static_cast<int64_t>(a.n) * a.h_kv * a.b;
   ip.batch = a.batch;
   ip.n = a.n;
   ip.h_kv = a.h_kv;
@@ -238,19 +239,33 @@ ssa::IndexParams index_params(const SsaRouteArgs& a, const RouteLayout& L, void*
 }
 
 // Candidate union, re-score and top-k over a built code->key index.
+// `dix` (decode): the index is the slotted one of ssa_decode_index_build,
+// bucket_ptr / bucket_keys are ignored and its entry codes are read as stored.
 ssa_status run_rescore(const SsaRouteArgs& a, const RouteLayout& L, void* ws, cudaStream_t st,
                        const int32_t* q_codes, const int32_t* k_codes, const int32_t* bucket_ptr,
-                       const int32_t* bucket_keys, const int32_t* index_bad) {
+                       const int32_t* bucket_keys, const int32_t* index_bad,
+                       const SsaDecodeIndex* dix = nullptr) {
   using namespace ssa;
   RescoreParams rp{};
   rp.q = a.q; rp.q_sb = a.q_stride_b; rp.q_sn = a.q_stride_n; rp.q_sh = a.q_stride_h;
   rp.k = a.k; rp.k_sb = a.k_stride_b; rp.k_sn = a.k_stride_n; rp.k_sh = a.k_stride_h;
   rp.q_codes = q_codes;
   rp.k_codes = k_codes;
+  rp.k_codes_sb = static_cast<int64_t>(a.n) * a.h_kv * a.b;
   rp.bucket_ptr = bucket_ptr;
   rp.bucket_keys = bucket_keys;
+  rp.bucket_end = nullptr;                            // packed index
+  rp.ptr_stride = static_cast<int64_t>(a.n_codes) + 1;
+  rp.entry_stride = static_cast<int64_t>(a.n) * a.b;
   rp.index_bad = index_bad;
-  if (a.b == 4) {
+  if (dix) {
+    rp.bucket_ptr = dix->bucket_start;
+    rp.bucket_end = dix->bucket_end;
+    rp.bucket_keys = dix->bucket_keys;
+    rp.entry_stride = dix->entry_capacity;
+    rp.bucket_codes = reinterpret_cast<const int4*>(dix->bucket_codes);
+    if (dix->k_codes_stride_b) rp.k_codes_sb = dix->k_codes_stride_b;
+  } else if (a.b == 4) {
     int4* bc = at<int4>(ws, L.bucket_codes);
     const cudaError_t ec = launch_index_codes(bucket_keys, k_codes, bc, static_cast<int64_t>(a.batch) * a.h_kv, a.n,
                                               a.h_kv, st);
@@ -319,6 +334,39 @@ ssa_status noalloc_scratch(void** out) {
   }
   *out = g_scratch_addr[dev];
   return SSA_OK;
+}
+
+// Validation of a caller's decode index (ssa_decode_*).
+ssa_status check_decode_index(const SsaRouteArgs& a, const SsaDecodeIndex* ix) {
+  if (!ix) return fail(SSA_ERR_INVALID_ARG, "index is NULL");
+  if (!ix->bucket_start || !ix->bucket_end || !ix->bucket_keys || !ix->min_free)
+    return fail(SSA_ERR_INVALID_ARG, "bucket_start / bucket_end / bucket_keys / min_free is NULL");
+  if (ix->slack < 1) return fail(SSA_ERR_INVALID_ARG, "slack %d < 1", ix->slack);
+  if (ix->entry_capacity < 1 || ix->entry_capacity >= (1ll << 31))
+    return fail(SSA_ERR_UNSUPPORTED, "entry_capacity must be in [1, 2^31)");
+  if (a.b == 4 && !ix->bucket_codes)
+    return fail(SSA_ERR_INVALID_ARG, "bucket_codes is required when codes_per_key == 4");
+  if (a.b != 4 && ix->bucket_codes)
+    return fail(SSA_ERR_INVALID_ARG, "bucket_codes is for codes_per_key == 4 only");
+  if (ix->bucket_codes && !aligned16(ix->bucket_codes))
+    return fail(SSA_ERR_ALIGNMENT, "bucket_codes must be 16-byte aligned");
+  if (!a.k_codes || !aligned16(a.k_codes)) return fail(SSA_ERR_ALIGNMENT, "k_codes must be set and 16-byte aligned");
+  return SSA_OK;
+}
+
+ssa::DecodeIndexParams decode_params(const SsaRouteArgs& a, const SsaDecodeIndex* ix) {
+  ssa::DecodeIndexParams p{};
+  p.start = ix->bucket_start;
+  p.end = ix->bucket_end;
+  p.keys = ix->bucket_keys;
+  p.codes = reinterpret_cast<int4*>(ix->bucket_codes);
+  p.min_free = ix->min_free;
+  p.k_codes = a.k_codes;
+  p.k_codes_sb = ix->k_codes_stride_b ? ix->k_codes_stride_b : static_cast<int64_t>(a.n) * a.h_kv * a.b;
+  p.status = a.status;
+  p.entry_capacity = ix->entry_capacity;
+  p.batch = a.batch; p.n = a.n; p.h_kv = a.h_kv; p.b = a.b; p.n_codes = a.n_codes; p.slack = ix->slack;
+  return p;
 }
 
 // Validation shared by the attention entry points; fills the kernel params.
@@ -502,6 +550,73 @@ ssa_status ssa_build_index(const SsaRouteArgs* args, const int32_t* k_codes, int
   if (args->batch == 0) return SSA_OK;
   ssa::IndexParams ip = index_params(*args, L, workspace, k_codes, bucket_ptr, bucket_keys);
   return cuda_status(ssa::launch_build_index(ip, static_cast<cudaStream_t>(stream)), "build_index");
+}
+
+int64_t ssa_decode_index_capacity(int32_t max_keys, int32_t b, int32_t n_codes, int32_t slack) {
+  if (max_keys < 0 || b < 1 || n_codes < 1 || slack < 1) return 0;
+  return 2 * static_cast<int64_t>(max_keys) * b + static_cast<int64_t>(n_codes) * slack;
+}
+
+ssa_status ssa_decode_index_build(const SsaRouteArgs* args, const SsaDecodeIndex* index, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  ssa_status s = check_route(args, false, false);
+  if (s != SSA_OK) return s;
+  s = check_decode_index(*args, index);
+  if (s != SSA_OK) return s;
+  if (!args->k_codes) return fail(SSA_ERR_INVALID_ARG, "k_codes (the cached keys' codes) is NULL");
+  const int64_t need = ssa_decode_index_capacity(args->n, args->b, args->n_codes, index->slack);
+  if (index->entry_capacity < need)
+    return fail(SSA_ERR_WORKSPACE, "decode index holds %lld slots per (sequence, head); %d keys need %lld",
+                static_cast<long long>(index->entry_capacity), args->n, static_cast<long long>(need));
+  const RouteLayout L = route_layout(*args);
+  if (!workspace || workspace_bytes < L.total)
+    return fail(SSA_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", L.total, workspace_bytes);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(index->min_free, 0x7f, sizeof(int32_t), st);
+  if (e != cudaSuccess) return cuda_status(e, "reset min_free");
+  if (args->batch == 0) return SSA_OK;
+  // the packed index in the workspace, then laid out with free slots
+  ssa::IndexParams ip = index_params(*args, L, workspace, args->k_codes, at<int32_t>(workspace, L.bucket_ptr),
+                                     at<int32_t>(workspace, L.bucket_keys));
+  if (index->k_codes_stride_b) ip.k_codes_sb = index->k_codes_stride_b;
+  e = ssa::launch_build_index(ip, st);
+  if (e != cudaSuccess) return cuda_status(e, "build_index");
+  return cuda_status(ssa::launch_decode_index_layout(decode_params(*args, index), ip.bucket_ptr, ip.bucket_keys, st),
+                     "decode_index_layout");
+}
+
+ssa_status ssa_decode_index_append(const SsaRouteArgs* args, const SsaDecodeIndex* index, int32_t first,
+                                   int32_t count, void* stream) {
+  ssa_status s = check_route(args, false, false);
+  if (s != SSA_OK) return s;
+  s = check_decode_index(*args, index);
+  if (s != SSA_OK) return s;
+  if (!args->k_codes) return fail(SSA_ERR_INVALID_ARG, "k_codes (the cached keys' codes) is NULL");
+  if (first < 0 || count < 0 || static_cast<int64_t>(first) + count > args->n)
+    return fail(SSA_ERR_INVALID_ARG, "keys %d .. %d + %d are not all among the %d cached keys", first, first, count,
+                args->n);
+  if (args->batch == 0 || count == 0) return SSA_OK;
+  return cuda_status(ssa::launch_decode_index_append(decode_params(*args, index), first, count,
+                                                     static_cast<cudaStream_t>(stream)),
+                     "decode_index_append");
+}
+
+ssa_status ssa_decode_route(const SsaRouteArgs* args, const SsaDecodeIndex* index, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  ssa_status s = check_route(args, true, true);
+  if (s != SSA_OK) return s;
+  s = check_decode_index(*args, index);
+  if (s != SSA_OK) return s;
+  if (!args->k_codes) return fail(SSA_ERR_INVALID_ARG, "k_codes (the cached keys' codes) is NULL");
+  const RouteLayout L = route_layout(*args);
+  if (!workspace || workspace_bytes < L.total)
+    return fail(SSA_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", L.total, workspace_bytes);
+  if (args->batch == 0 || args->n_q == 0) return SSA_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int32_t* qc = args->q_codes ? args->q_codes : at<int32_t>(workspace, L.q_codes);
+  s = run_stage1(*args, L, workspace, st, false, true, qc, nullptr);
+  if (s != SSA_OK) return s;
+  return run_rescore(*args, L, workspace, st, qc, args->k_codes, nullptr, nullptr, nullptr, index);
 }
 
 ssa_status ssa_build_index_noalloc(const SsaRouteArgs* args, const int32_t* k_codes, int32_t* bucket_ptr,

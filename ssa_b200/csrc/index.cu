@@ -34,7 +34,7 @@ __global__ void __launch_bounds__(kIndexThreads) index_count_kernel(IndexParams 
   const int entries = nk * p.b;
   for (int e = threadIdx.x; e < entries; e += blockDim.x) {
     const int jl = e / p.b, s = e % p.b;
-    const int c = checked_code(p.k_codes[((static_cast<int64_t>(bat) * p.n + j0 + jl) * p.h_kv + h) * p.b + s],
+    const int c = checked_code(p.k_codes[bat * p.k_codes_sb + (static_cast<int64_t>(j0 + jl) * p.h_kv + h) * p.b + s],
                                p.n_codes, p.status);
     // warp-aggregated: one shared atomic per distinct code in the warp
     const unsigned active = __activemask();
@@ -169,7 +169,7 @@ __global__ void __launch_bounds__(kIndexThreads) index_scatter_kernel(IndexParam
     if (e < entries) {
       const int jl = e / p.b, s = e % p.b;
       const uint32_t c = static_cast<uint32_t>(checked_code(
-          p.k_codes[((static_cast<int64_t>(bat) * p.n + j0 + jl) * p.h_kv + h) * p.b + s], p.n_codes, nullptr));
+          p.k_codes[bat * p.k_codes_sb + (static_cast<int64_t>(j0 + jl) * p.h_kv + h) * p.b + s], p.n_codes, nullptr));
       kv = (c << 16) | static_cast<uint32_t>(e);
     }
     keys[e] = kv;

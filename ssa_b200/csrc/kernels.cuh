@@ -57,6 +57,7 @@ struct IndexParams {
   uint32_t* counts;        // [B*h_kv, n_codes, tiles] workspace
   uint32_t* partials;      // [B*h_kv, chunks] workspace
   int32_t* status;         // optional device word (SSA_DEVICE_BAD_CODE)
+  int64_t k_codes_sb;      // elements between sequences of k_codes (n*h_kv*b when contiguous)
   int batch, n, h_kv, b, n_codes, tile_keys, tiles;
   int64_t chunks;          // scan chunks per (bat, h)
 };
@@ -76,12 +77,35 @@ cudaError_t launch_index_codes(const int32_t* bucket_keys, const int32_t* k_code
 cudaError_t launch_validate_index(const int32_t* bucket_ptr, const int32_t* bucket_keys, int64_t batch_heads,
                                   int n_codes, int n, int b, int32_t* bad, int32_t* status, cudaStream_t st);
 
+// The code->key index of a growing key cache (decode_index.cu): bucket c of
+// (bat, h) = bh owns slots [start[c], start[c+1]) and holds its keys,
+// ascending, in [start[c], end[c]) of keys + bh * entry_capacity.
+struct DecodeIndexParams {
+  int32_t* start;              // [B*h_kv, n_codes+1]
+  int32_t* end;                // [B*h_kv, n_codes+1]
+  int32_t* keys;               // [B*h_kv, entry_capacity]
+  int4* codes;                 // optional (b == 4): each entry's key codes, [B*h_kv, entry_capacity]
+  int32_t* min_free;           // optional device word: fewest free slots of any bucket (atomicMin)
+  const int32_t* k_codes;      // [B, n, h_kv, b] codes of the cached keys ...
+  int64_t k_codes_sb;          // ... sequences k_codes_sb elements apart
+  int32_t* status;             // optional device word (SSA_DEVICE_BAD_CODE, SSA_DEVICE_INDEX_FULL)
+  int64_t entry_capacity;
+  int batch, n, h_kv, b, n_codes, slack;
+};
+// Lays the packed index (packed_ptr [B*h_kv, n_codes+1], packed_keys
+// [B*h_kv, n*b]) out with max(slack, size) free slots after every bucket.
+cudaError_t launch_decode_index_layout(const DecodeIndexParams& p, const int32_t* packed_ptr,
+                                       const int32_t* packed_keys, cudaStream_t st);
+// Appends keys first .. first+count-1 (each above every key already indexed).
+cudaError_t launch_decode_index_append(const DecodeIndexParams& p, int first, int count, cudaStream_t st);
+
 // K3: candidate union + causal filter + re-score + top-k + filler.
 struct RescoreParams {
   const void* q; int64_t q_sb, q_sn, q_sh;
   const void* k; int64_t k_sb, k_sn, k_sh;
   const int32_t* q_codes;      // [B, n_q, h_kv, a]
-  const int32_t* k_codes;      // [B, n, h_kv, b]
+  const int32_t* k_codes;      // [B, n, h_kv, b], sequences k_codes_sb elements apart
+  int64_t k_codes_sb;
   const int32_t* bucket_ptr;   // [B*h_kv, n_codes+1]
   const int32_t* bucket_keys;  // [B*h_kv, n*b]
   void* out; int index_i64;    // [B, n_q, h_kv, top_k]
@@ -89,6 +113,14 @@ struct RescoreParams {
   int32_t* status;             // optional device word (SSA_DEVICE_BAD_CODE)
   const int32_t* index_bad;    // optional: non-zero when a caller-given index failed validation
   const int4* bucket_codes;    // optional (b == 4): the codes of each index entry's key, [B*h_kv, n*4]
+  // The index layout.  Packed (bucket_end NULL): bucket c of (bat, h) holds the
+  // entries [ptr[c], ptr[c+1]) of bucket_keys + bh * entry_stride, with
+  // ptr = bucket_ptr + bh * ptr_stride, ptr_stride = n_codes + 1 and
+  // entry_stride = n * b.  With free room after each bucket (the decode index):
+  // bucket c holds [ptr[c], bucket_end[bh * ptr_stride + c]) and entry_stride is
+  // the entry capacity of one (bat, h); bucket_codes uses the same entry offsets.
+  const int32_t* bucket_end;
+  int64_t ptr_stride, entry_stride;
   int batch, n, n_q, q_offset, h_kv, group, d, a, b, n_codes, top_k, causal;
   int cap;                     // shared-memory candidate capacity (power of two)
   int tier1_rows;              // warp path: query rows per (bat, h) the first tier takes (the
@@ -103,6 +135,16 @@ struct RescoreParams {
   int32_t* ovf3_next;          // the claim counter and
   int32_t* ovf3_list;          // their indices [B * n_q * h_kv]
 };
+
+// Entries of (bat, h) = bh in the index, and the range [lo, hi) of bucket c.
+__device__ __forceinline__ const int32_t* bucket_base(const RescoreParams& p, int bh) {
+  return p.bucket_keys + static_cast<int64_t>(bh) * p.entry_stride;
+}
+__device__ __forceinline__ void bucket_range(const RescoreParams& p, int bh, int c, int& lo, int& hi) {
+  const int32_t* ptr = p.bucket_ptr + static_cast<int64_t>(bh) * p.ptr_stride;
+  lo = ptr[c];
+  hi = p.bucket_end ? p.bucket_end[static_cast<int64_t>(bh) * p.ptr_stride + c] : ptr[c + 1];
+}
 
 // A caller-given code->key index that failed validation: the unit's indices
 // are written as zeros (and its candidate count as 0) instead of being

@@ -145,16 +145,15 @@ __device__ void rescore_unit_block(const RescoreParams& p, int64_t unit, RsStati
   const int pos = p.q_offset + i;
   const int a = p.a;
   const int k_eff = min(p.top_k, p.n);
-  const int32_t* bk = p.bucket_keys + static_cast<int64_t>(bh) * p.n * p.b;
+  const int32_t* bk = bucket_base(p, bh);
 
   if (threadIdx.x < kWarp) {
     int len = 0;
     if (threadIdx.x < a) {
       const int c = checked_code(p.q_codes[((static_cast<int64_t>(bat) * p.n_q + i) * p.h_kv + h) * a + threadIdx.x],
                                  p.n_codes, p.status);
-      const int32_t* ptr = p.bucket_ptr + static_cast<int64_t>(bh) * (p.n_codes + 1);
-      const int lo = ptr[c];
-      int hi = ptr[c + 1];
+      int lo, hi;
+      bucket_range(p, bh, c, lo, hi);
       if (p.causal) {  // bucket keys ascend: keep the prefix with j <= pos
         int l = lo, u = hi;
         while (l < u) {
@@ -189,7 +188,7 @@ __device__ void rescore_unit_block(const RescoreParams& p, int64_t unit, RsStati
   __syncthreads();
 
   RsUnit<T> u{p, s, qbar, bk,
-              p.k_codes + static_cast<int64_t>(bat) * p.n * p.h_kv * p.b,
+              p.k_codes + static_cast<int64_t>(bat) * p.k_codes_sb,
               static_cast<const T*>(p.k) + bat * p.k_sb + static_cast<int64_t>(h) * p.k_sh, h, a};
   const uint32_t cap = static_cast<uint32_t>(p.cap);
   u.enumerate([&](uint64_t key) {
@@ -434,15 +433,14 @@ __global__ void __launch_bounds__(kWarpUnits * kWarp) rescore_warp_kernel(Rescor
   const int pos = p.q_offset + i;
   const int a = p.a;
   const int k_eff = min(p.top_k, p.n);
-  const int32_t* bk = p.bucket_keys + static_cast<int64_t>(bh) * p.n * p.b;
+  const int32_t* bk = bucket_base(p, bh);
 
   int len = 0;
   if (lane < a) {
     const int c = checked_code(p.q_codes[((static_cast<int64_t>(bat) * p.n_q + i) * p.h_kv + h) * a + lane],
                                p.n_codes, p.status);
-    const int32_t* ptr = p.bucket_ptr + static_cast<int64_t>(bh) * (p.n_codes + 1);
-    const int lo = ptr[c];
-    int hi = ptr[c + 1];
+    int lo, hi;
+    bucket_range(p, bh, c, lo, hi);
     if (p.causal) {
       int l = lo, u = hi;
       while (l < u) {
@@ -476,7 +474,7 @@ __global__ void __launch_bounds__(kWarpUnits * kWarp) rescore_warp_kernel(Rescor
   }
   __syncwarp();
 
-  const int32_t* kcodes = p.k_codes + static_cast<int64_t>(bat) * p.n * p.h_kv * p.b;
+  const int32_t* kcodes = p.k_codes + static_cast<int64_t>(bat) * p.k_codes_sb;
   const T* kbase = static_cast<const T*>(p.k) + bat * p.k_sb + static_cast<int64_t>(h) * p.k_sh;
   // Two candidates per lane per iteration.  For each, the K row and the key's
   // codes are loaded as soon as the key index is known, so the dedupe test

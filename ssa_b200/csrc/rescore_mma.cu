@@ -179,7 +179,7 @@ __device__ __forceinline__ void rescore_mma_unit(const RescoreParams& p, int64_t
   const int pos = p.q_offset + i;
   const int a = p.a;
   const int k_eff = min(p.top_k, p.n);
-  const int32_t* bk = p.bucket_keys + static_cast<int64_t>(bh) * p.n * p.b;
+  const int32_t* bk = bucket_base(p, bh);
   const int gid = lane >> 2, tig = lane & 3;
   uint32_t* hist = reinterpret_cast<uint32_t*>(s.sel) + (sizeof(s.sel) / 4 - 256);
 
@@ -188,9 +188,8 @@ __device__ __forceinline__ void rescore_mma_unit(const RescoreParams& p, int64_t
   if (lane < a) {
     const int c = checked_code(p.q_codes[((static_cast<int64_t>(bat) * p.n_q + i) * p.h_kv + h) * a + lane],
                                p.n_codes, p.status);
-    const int32_t* ptr = p.bucket_ptr + static_cast<int64_t>(bh) * (p.n_codes + 1);
-    const int lo = ptr[c];
-    int hi = ptr[c + 1];
+    int lo, hi;
+    bucket_range(p, bh, c, lo, hi);
     if (p.causal) hi = first_above(bk, lo, hi, pos);
     s.qc[lane] = c;
     s.lo[lane] = lo;
@@ -260,11 +259,11 @@ __device__ __forceinline__ void rescore_mma_unit(const RescoreParams& p, int64_t
   __syncwarp();
 
   // ---- 1b. walk the buckets: first-match dedupe, compact kept key indices ----
-  const int32_t* kcodes = p.k_codes + static_cast<int64_t>(bat) * p.n * p.h_kv * p.b;
+  const int32_t* kcodes = p.k_codes + static_cast<int64_t>(bat) * p.k_codes_sb;
   int32_t* jlist = reinterpret_cast<int32_t*>(s.sel);
   // with b == 4 the index carries each entry's key codes beside it: key and
   // codes of an entry are loaded in the same round trip
-  const int4* bcodes = p.bucket_codes ? p.bucket_codes + static_cast<int64_t>(bh) * p.n * 4 : nullptr;
+  const int4* bcodes = p.bucket_codes ? p.bucket_codes + static_cast<int64_t>(bh) * p.entry_stride : nullptr;
   int count = 0;
   int t = 0;
   for (int m0 = 0; m0 < total; m0 += kWalk * kWarp) {

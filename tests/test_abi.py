@@ -60,7 +60,8 @@ def _c_layout(struct: str, fields):
 
 
 @pytest.mark.parametrize("cls,name", [(L.SsaRouteArgs, "SsaRouteArgs"), (L.SsaAttnArgs, "SsaAttnArgs"),
-                                      (L.SsaRopeArgs, "SsaRopeArgs")])
+                                      (L.SsaRopeArgs, "SsaRopeArgs"),
+                                      (L.SsaDecodeIndex, "SsaDecodeIndex")])
 def test_ctypes_structs_match_c_layout(cls, name):
     fields = [f for f, _ in cls._fields_]
     size, offsets = _c_layout(name, fields)
