@@ -66,10 +66,11 @@ LAUNCHES_PER_STEP = 17
 # measured by ncu (dram__bytes_read.sum + dram__bytes_write.sum, one pass on this
 # workload; profiles/sparse_attn_mma_config3.txt).  Other n scale by the query rows.
 ATTN_DRAM_BYTES_N32768 = 920.29e6
-# DRAM bytes of stage 2 (ssa_select_candidates: index build, entry codes, re-score
-# tiers) per call at n = 32768, from the ncu DRAM counters of its kernels
-# (profiles/rescore_mma_config3.txt).
-RESCORE_DRAM_BYTES_N32768 = 2 * 289.7e6
+# DRAM bytes of stage 2 (ssa_select_candidates: index count / scatter / entry
+# codes and the re-score tiers) per call at n = 32768: the sum of the ncu
+# dram__bytes_read.sum + dram__bytes_write.sum of its kernels in one step of the
+# bench's own workload (profiles/rescore_mma_config3.txt); tier 1 alone 613.9 MB.
+RESCORE_DRAM_BYTES_N32768 = 745.7e6
 
 
 def parse():
@@ -261,23 +262,29 @@ def run_reference(args):
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
-def measure_l2_read_peak(dev, reps=40):
-    """Read bandwidth of an L2-resident buffer (outside the timed region):
-    ``torch.sum`` over an fp32 tensor of 16 / 32 / 48 MiB that a warm-up pass
-    left in the 126 MB L2, timed with CUDA events; the best of the sizes.
-    The denominator of the ``l2`` fractions below."""
+def measure_l2_read_peak(dev, reps=50):
+    """L2 read bandwidth (outside the timed region): ``ssa_l2_read_probe``
+    (16-byte L2-only loads over the whole GPU) on 16 / 32 / 48 MiB buffers
+    that stay in the 126 MB L2, one launch of ``reps`` passes each, timed with
+    CUDA events; the best of the sizes.  The denominator of the ``l2``
+    fractions below."""
     import torch
+    from ssa_b200 import _lib as L
 
+    lib = L.lib()
+    sink = torch.zeros(1, dtype=torch.int64, device=dev)
+    st = torch.cuda.current_stream(dev)
     best = 0.0
     for mib in (16, 32, 48):
         x = torch.ones(mib * 2 ** 20 // 4, device=dev)
-        for _ in range(5):
-            x.sum()
+        for _ in range(2):
+            L.check("ssa_l2_read_probe", lib.ssa_l2_read_probe(x.data_ptr(), x.numel() * 4, 2, sink.data_ptr(),
+                                                               st.cuda_stream))
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(reps):
-            x.sum()
-        e1.record()
+        e0.record(st)
+        L.check("ssa_l2_read_probe", lib.ssa_l2_read_probe(x.data_ptr(), x.numel() * 4, reps, sink.data_ptr(),
+                                                           st.cuda_stream))
+        e1.record(st)
         torch.cuda.synchronize(dev)
         best = max(best, mib * 2 ** 20 * reps / (e0.elapsed_time(e1) / 1e3) / 1e9)
         del x

@@ -315,6 +315,14 @@ ssa_status ssa_build_index_noalloc(const SsaRouteArgs* args, const int32_t* k_co
 ssa_status ssa_select_candidates(const SsaRouteArgs* args, void* workspace,
                                  size_t workspace_bytes, void* stream);
 
+/* Measurement hook (no reference counterpart): reads `bytes` of the device
+ * buffer `buf` (16-byte aligned) `reps` times with 16-byte L2-only loads
+ * across the whole GPU.  With a buffer that fits in L2, bytes * reps over the
+ * launch's duration is the L2 read bandwidth the benchmark reports the
+ * gather-bound kernels against.  *sink (device) is touched only to keep the
+ * loads alive. */
+ssa_status ssa_l2_read_probe(const void* buf, size_t bytes, int32_t reps, unsigned long long* sink, void* stream);
+
 /* Human-readable text of a status code. */
 const char* ssa_status_str(ssa_status s);
 

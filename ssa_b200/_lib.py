@@ -97,6 +97,7 @@ SIGNATURES = {
     "ssa_route_rope": (ctypes.c_int, [ctypes.POINTER(SsaRouteArgs), ctypes.POINTER(SsaRopeArgs), _vp,
                                       ctypes.c_size_t, _vp]),
     "ssa_sparse_attn_backward": (ctypes.c_int, [ctypes.POINTER(SsaAttnArgs), _vp, _vp, _vp, _vp, _vp]),
+    "ssa_l2_read_probe": (ctypes.c_int, [_vp, ctypes.c_size_t, _c_i32, _vp, _vp]),
     "ssa_status_str": (ctypes.c_char_p, [ctypes.c_int]),
     "ssa_last_error": (ctypes.c_char_p, []),
 }

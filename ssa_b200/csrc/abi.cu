@@ -188,6 +188,7 @@ ssa_status run_stage1(const SsaRouteArgs& a, const RouteLayout& L, void* ws, cud
     RouteProjectParams kp{a.k, a.k_stride_b, a.k_stride_n, a.k_stride_h, a.w_kr,
                           at<float>(ws, L.k_route), static_cast<int64_t>(a.batch) * a.h_kv * a.n, a.n,
                           a.h_kv, 1, a.d, a.d_s};
+    kp.status = a.status;
     if (rope) {
       kp.rope_cos = rope->cos; kp.rope_sin = rope->sin;
       kp.rope_sb = rope->table_stride_b; kp.rope_sn = rope->table_stride_n; kp.pos_offset = 0;
@@ -203,6 +204,7 @@ ssa_status run_stage1(const SsaRouteArgs& a, const RouteLayout& L, void* ws, cud
     RouteProjectParams qp{a.q, a.q_stride_b, a.q_stride_n, a.q_stride_h, a.w_qr,
                           at<float>(ws, L.q_route), static_cast<int64_t>(a.batch) * a.h_kv * a.n_q,
                           a.n_q, a.h_kv, a.h_q / a.h_kv, a.d, a.d_s};
+    qp.status = a.status;
     if (rope) {
       qp.rope_cos = rope->cos; qp.rope_sin = rope->sin;
       qp.rope_sb = rope->table_stride_b; qp.rope_sn = rope->table_stride_n; qp.pos_offset = a.q_offset;
@@ -657,6 +659,13 @@ ssa_status ssa_select_candidates(const SsaRouteArgs* args, void* workspace, size
   if (args->batch == 0 || args->n_q == 0) return SSA_OK;
   return run_stage2(*args, L, workspace, static_cast<cudaStream_t>(stream), args->q_codes,
                     args->k_codes);
+}
+
+ssa_status ssa_l2_read_probe(const void* buf, size_t bytes, int32_t reps, unsigned long long* sink, void* stream) {
+  if (!buf || !sink) return fail(SSA_ERR_INVALID_ARG, "NULL pointer");
+  if (!aligned16(buf) || bytes < 16 || reps < 1) return fail(SSA_ERR_INVALID_ARG, "need a 16-byte aligned buffer and reps >= 1");
+  return cuda_status(ssa::launch_l2_read_probe(buf, bytes, reps, sink, static_cast<cudaStream_t>(stream)),
+                     "l2_read_probe");
 }
 
 ssa_status ssa_sparse_attn(const SsaAttnArgs* a, void* stream) {

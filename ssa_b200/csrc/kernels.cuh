@@ -25,8 +25,13 @@ struct RouteProjectParams {
   int64_t rope_sb = 0, rope_sn = 0, pos_offset = 0;
   void* x_out = nullptr;
   int64_t out_sb = 0, out_sn = 0, out_sh = 0;
+  int32_t* status = nullptr;   // optional device word (SSA_DEVICE_TIMEOUT from the tcgen05 kernel)
 };
 bool route_project_rope_supported(int d, int d_s, ssa_dtype xt);
+// The TMA-fed tcgen05 projection (route_tc.cu): 16-bit x without RoPE, d a
+// multiple of 64, d_s in {16, 32, 64}, the group's heads contiguous in a row.
+bool route_project_tc_supported(const RouteProjectParams& p, ssa_dtype xt, ssa_dtype wt);
+cudaError_t launch_route_project_tc(const RouteProjectParams& p, ssa_dtype xt, ssa_dtype wt, cudaStream_t st);
 
 // K1: codebook scoring + top-kk selection.  Route rows in (bat, h, i) order.
 struct CodeSelectParams {
@@ -98,6 +103,9 @@ cudaError_t launch_decode_index_layout(const DecodeIndexParams& p, const int32_t
                                        const int32_t* packed_keys, cudaStream_t st);
 // Appends keys first .. first+count-1 (each above every key already indexed).
 cudaError_t launch_decode_index_append(const DecodeIndexParams& p, int first, int count, cudaStream_t st);
+
+// Measurement hook (probe.cu): L2-only 16-byte reads of `bytes` of buf, `reps` times.
+cudaError_t launch_l2_read_probe(const void* buf, size_t bytes, int reps, unsigned long long* sink, cudaStream_t st);
 
 // K3: candidate union + causal filter + re-score + top-k + filler.
 struct RescoreParams {

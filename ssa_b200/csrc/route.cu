@@ -557,6 +557,7 @@ cudaError_t launch_route_project(const RouteProjectParams& p, ssa_dtype xt, ssa_
                                  cudaStream_t st) {
   if (p.rows == 0) return cudaSuccess;
   if (p.rope_cos && !route_project_rope_supported(p.d, p.d_s, xt)) return cudaErrorInvalidValue;
+  if (route_project_tc_supported(p, xt, wt)) return launch_route_project_tc(p, xt, wt, st);
   if (route_project_mma_ok(p, xt)) {
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);

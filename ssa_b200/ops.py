@@ -353,7 +353,8 @@ def attn_args(q, k, v, indices, out, scale, causal, q_offset, status=None):
                                                                 indices.stride(2))
     args.out = out.data_ptr()
     args.out_stride_b, args.out_stride_n, args.out_stride_h = out.stride(0), out.stride(1), out.stride(2)
-    args.status = _ptr(status)
+    # the status word: a device address (an int) or a one-element int32 tensor
+    args.status = status if status is None or isinstance(status, int) else status.data_ptr()
     return args
 
 
