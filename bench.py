@@ -483,7 +483,7 @@ def run_ours(args):
             "dram_frac": traffic / attn_s / 1e9 / hbm,
             "l2": {"achieved": attn_logical / attn_s / 1e9, "peak": l2_peak, "unit": "GB/s",
                    "frac": attn_logical / attn_s / 1e9 / l2_peak, "bytes": attn_logical,
-                   "peak_kind": "measured in this run: torch.sum over an L2-resident buffer"},
+                   "peak_kind": "measured in this run: ssa_l2_read_probe (L2-only 16-byte reads of a 16-48 MiB buffer)"},
             "binding": "l2 (k gathered K/V rows per query and head, served from L2)",
             "logical_bytes_per_launch": attn_logical, "launch_ms": attn_ms, "router_ms": route_ms}
     # parity of the timed steps' own outputs, before anything rewrites them

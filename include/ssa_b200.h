@@ -153,6 +153,27 @@ ssa_status ssa_route_with_index(const SsaRouteArgs* args, const int32_t* bucket_
                                 const int32_t* bucket_keys, void* workspace, size_t workspace_bytes,
                                 void* stream);
 
+/* Query rows given as up to SSA_MAX_SEGMENTS runs of consecutive sequence
+ * positions: rows[s] rows starting at position positions[s], in order
+ * (positions ascending, runs not overlapping, sum of rows = n_q).  A GPU
+ * holding several blocks of one long sequence routes and attends all of them
+ * in one call each.  (The reference processes one whole sequence; its
+ * per-query computation, ssa/router.py:151-214 and ssa/attention.py:12-115,
+ * does not depend on which other queries share the call.) */
+#define SSA_MAX_SEGMENTS 8
+typedef struct {
+  int32_t count;
+  int32_t rows[SSA_MAX_SEGMENTS];
+  int32_t positions[SSA_MAX_SEGMENTS];
+} SsaQuerySegments;
+
+/* ssa_route_with_index for query rows in segments (args->q_offset is
+ * ignored): row i of segment s is routed as the query at position
+ * positions[s] + i, exactly as ssa_route would route it. */
+ssa_status ssa_route_with_index_segments(const SsaRouteArgs* args, const SsaQuerySegments* segments,
+                                         const int32_t* bucket_ptr, const int32_t* bucket_keys, void* workspace,
+                                         size_t workspace_bytes, void* stream);
+
 /* Rotary position embedding applied on load by ssa_route_rope: the
  * rotate-half form of the Qwen2 path of the reference
  * (training/train_qwen.py:134-135, transformers' apply_rotary_pos_emb):
@@ -258,6 +279,10 @@ typedef struct {
  * q_offset + i) gets a zero output row; the reference never masks in this
  * stage, and a softmax over no key would be 0/0. */
 ssa_status ssa_sparse_attn(const SsaAttnArgs* args, void* stream);
+
+/* ssa_sparse_attn for query rows in segments (args->q_offset is ignored):
+ * with causal = 1, row i of segment s masks keys above positions[s] + i. */
+ssa_status ssa_sparse_attn_segments(const SsaAttnArgs* args, const SsaQuerySegments* segments, void* stream);
 
 /* Gradients of ssa_sparse_attn (the backward of sparse_exact_attention,
  * ssa/attention.py:12-115, which the reference differentiates with autograd).

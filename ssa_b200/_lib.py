@@ -67,6 +67,13 @@ class SsaRopeArgs(ctypes.Structure):
     ]
 
 
+SSA_MAX_SEGMENTS = 8
+
+
+class SsaQuerySegments(ctypes.Structure):
+    _fields_ = [("count", _c_i32), ("rows", _c_i32 * SSA_MAX_SEGMENTS), ("positions", _c_i32 * SSA_MAX_SEGMENTS)]
+
+
 class SsaDecodeIndex(ctypes.Structure):
     _fields_ = [
         ("bucket_start", _vp), ("bucket_end", _vp), ("bucket_keys", _vp), ("bucket_codes", _vp),
@@ -98,6 +105,9 @@ SIGNATURES = {
                                       ctypes.c_size_t, _vp]),
     "ssa_sparse_attn_backward": (ctypes.c_int, [ctypes.POINTER(SsaAttnArgs), _vp, _vp, _vp, _vp, _vp]),
     "ssa_l2_read_probe": (ctypes.c_int, [_vp, ctypes.c_size_t, _c_i32, _vp, _vp]),
+    "ssa_route_with_index_segments": (ctypes.c_int, [ctypes.POINTER(SsaRouteArgs), ctypes.POINTER(SsaQuerySegments),
+                                                     _vp, _vp, _vp, ctypes.c_size_t, _vp]),
+    "ssa_sparse_attn_segments": (ctypes.c_int, [ctypes.POINTER(SsaAttnArgs), ctypes.POINTER(SsaQuerySegments), _vp]),
     "ssa_status_str": (ctypes.c_char_p, [ctypes.c_int]),
     "ssa_last_error": (ctypes.c_char_p, []),
 }

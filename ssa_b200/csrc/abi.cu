@@ -246,7 +246,7 @@ ssa::IndexParams index_params(const SsaRouteArgs& a, const RouteLayout& L, void*
 ssa_status run_rescore(const SsaRouteArgs& a, const RouteLayout& L, void* ws, cudaStream_t st,
                        const int32_t* q_codes, const int32_t* k_codes, const int32_t* bucket_ptr,
                        const int32_t* bucket_keys, const int32_t* index_bad,
-                       const SsaDecodeIndex* dix = nullptr) {
+                       const SsaDecodeIndex* dix = nullptr, const ssa::QuerySegs* segs = nullptr) {
   using namespace ssa;
   RescoreParams rp{};
   rp.q = a.q; rp.q_sb = a.q_stride_b; rp.q_sn = a.q_stride_n; rp.q_sh = a.q_stride_h;
@@ -279,6 +279,7 @@ ssa_status run_rescore(const SsaRouteArgs& a, const RouteLayout& L, void* ws, cu
   rp.cand_counts = a.cand_counts;
   rp.status = a.status;
   rp.batch = a.batch; rp.n = a.n; rp.n_q = a.n_q; rp.q_offset = a.q_offset;
+  rp.seg = segs ? *segs : ssa::contiguous_segs(a.q_offset, a.n_q);
   rp.h_kv = a.h_kv; rp.group = a.h_q / a.h_kv; rp.d = a.d; rp.a = a.a; rp.b = a.b;
   rp.n_codes = a.n_codes; rp.top_k = a.top_k; rp.causal = a.causal ? 1 : 0;
   rp.cap = rescore_cap(std::min(a.top_k, a.n));
@@ -335,6 +336,31 @@ ssa_status noalloc_scratch(void** out) {
     g_scratch_addr[dev] = ptr;
   }
   *out = g_scratch_addr[dev];
+  return SSA_OK;
+}
+
+// Query segments of a caller (ssa_*_segments): 1..kMaxSeg runs covering the
+// n_q rows in order, positions ascending and inside [0, n).
+ssa_status check_segments(const SsaQuerySegments* s, int n_q, int n, ssa::QuerySegs& out) {
+  if (!s) return fail(SSA_ERR_INVALID_ARG, "segments is NULL");
+  if (s->count < 1 || s->count > SSA_MAX_SEGMENTS)
+    return fail(SSA_ERR_INVALID_ARG, "segment count %d outside 1..%d", s->count, SSA_MAX_SEGMENTS);
+  out = ssa::QuerySegs{};
+  out.count = s->count;
+  int64_t rows = 0, next_pos = 0;
+  for (int i = 0; i < s->count; ++i) {
+    if (s->rows[i] < 0 || s->positions[i] < next_pos)
+      return fail(SSA_ERR_INVALID_ARG, "segment %d: rows %d at position %d (positions must ascend, segments not overlap)",
+                  i, s->rows[i], s->positions[i]);
+    out.row[i] = static_cast<int>(rows);
+    out.pos[i] = s->positions[i];
+    rows += s->rows[i];
+    next_pos = static_cast<int64_t>(s->positions[i]) + s->rows[i];
+    if (next_pos > n) return fail(SSA_ERR_INVALID_ARG, "segment %d ends at position %lld > n = %d", i,
+                                  static_cast<long long>(next_pos), n);
+  }
+  if (rows != n_q) return fail(SSA_ERR_INVALID_ARG, "segments cover %lld rows, n_q = %d", static_cast<long long>(rows), n_q);
+  out.row[s->count] = n_q;
   return SSA_OK;
 }
 
@@ -398,6 +424,7 @@ ssa_status attn_params(const SsaAttnArgs* a, ssa::AttnParams& p) {
   p.out = a->out; p.o_sb = a->out_stride_b; p.o_sn = a->out_stride_n; p.o_sh = a->out_stride_h;
   p.status = a->status;
   p.batch = a->batch; p.n_q = a->n_q; p.n = a->n; p.q_offset = a->q_offset;
+  p.seg = ssa::contiguous_segs(a->q_offset, a->n_q);
   p.h_kv = a->h_kv; p.group = a->h_q / a->h_kv; p.d = a->d; p.top_k = a->top_k;
   p.causal = a->causal ? 1 : 0;
   p.inv_scale = 1.0f / a->scale;
@@ -659,6 +686,40 @@ ssa_status ssa_select_candidates(const SsaRouteArgs* args, void* workspace, size
   if (args->batch == 0 || args->n_q == 0) return SSA_OK;
   return run_stage2(*args, L, workspace, static_cast<cudaStream_t>(stream), args->q_codes,
                     args->k_codes);
+}
+
+ssa_status ssa_route_with_index_segments(const SsaRouteArgs* args, const SsaQuerySegments* segments,
+                                         const int32_t* bucket_ptr, const int32_t* bucket_keys, void* workspace,
+                                         size_t workspace_bytes, void* stream) {
+  ssa_status s = check_route(args, true, true);
+  if (s != SSA_OK) return s;
+  ssa::QuerySegs segs;
+  s = check_segments(segments, args->n_q, args->n, segs);
+  if (s != SSA_OK) return s;
+  if (!args->k_codes || !bucket_ptr || !bucket_keys)
+    return fail(SSA_ERR_INVALID_ARG, "k_codes, bucket_ptr and bucket_keys are inputs here and must be set");
+  const RouteLayout L = route_layout(*args);
+  if (!workspace || workspace_bytes < L.total)
+    return fail(SSA_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", L.total, workspace_bytes);
+  if (args->batch == 0 || args->n_q == 0) return SSA_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int32_t* qc = args->q_codes ? args->q_codes : at<int32_t>(workspace, L.q_codes);
+  int32_t* bad = at<int32_t>(workspace, L.flags);
+  cudaError_t e = ssa::launch_validate_index(bucket_ptr, bucket_keys, static_cast<int64_t>(args->batch) * args->h_kv,
+                                             args->n_codes, args->n, args->b, bad, args->status, st);
+  if (e != cudaSuccess) return cuda_status(e, "validate_index");
+  s = run_stage1(*args, L, workspace, st, false, true, qc, nullptr);
+  if (s != SSA_OK) return s;
+  return run_rescore(*args, L, workspace, st, qc, args->k_codes, bucket_ptr, bucket_keys, bad, nullptr, &segs);
+}
+
+ssa_status ssa_sparse_attn_segments(const SsaAttnArgs* a, const SsaQuerySegments* segments, void* stream) {
+  ssa::AttnParams p{};
+  ssa_status s = attn_params(a, p);
+  if (s != SSA_OK) return s;
+  s = check_segments(segments, a->n_q, a->n, p.seg);
+  if (s != SSA_OK || a->batch == 0 || a->n_q == 0) return s;
+  return cuda_status(ssa::launch_sparse_attn(p, a->dtype, static_cast<cudaStream_t>(stream)), "sparse_attn");
 }
 
 ssa_status ssa_l2_read_probe(const void* buf, size_t bytes, int32_t reps, unsigned long long* sink, void* stream) {

@@ -46,7 +46,7 @@ __global__ void __launch_bounds__(kAttnWarps * kWarp) sparse_attn_kernel(AttnPar
   const char* ib = static_cast<const char*>(p.idx) +
                    (bat * p.i_sb + static_cast<int64_t>(i) * p.i_sn + static_cast<int64_t>(h) * p.i_sh) *
                        (p.index_i64 ? 8 : 4);
-  const int64_t limit = static_cast<int64_t>(p.q_offset) + i;
+  const int64_t limit = seg_pos(p.seg, i);
   constexpr float kLog2e = 1.4426950408889634f;
 
   float m_run[GMAX], l_lane[GMAX], o[GMAX][DPL];

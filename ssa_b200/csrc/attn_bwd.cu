@@ -70,7 +70,7 @@ __global__ void __launch_bounds__(kWarp) sparse_attn_bwd_kernel(AttnBwdParams p)
   const char* ib = static_cast<const char*>(a.idx) +
                    (bat * a.i_sb + static_cast<int64_t>(i) * a.i_sn + static_cast<int64_t>(h) * a.i_sh) *
                        (a.index_i64 ? 8 : 4);
-  const int64_t limit = static_cast<int64_t>(a.q_offset) + i;
+  const int64_t limit = seg_pos(a.seg, i);
   auto slot_key = [&](int t, bool& valid) -> int64_t {
     const int64_t j = a.index_i64 ? reinterpret_cast<const int64_t*>(ib)[t]
                                   : static_cast<int64_t>(reinterpret_cast<const int32_t*>(ib)[t]);

@@ -72,7 +72,7 @@ __global__ void __launch_bounds__(kMmaWarps * kWarp) sparse_attn_mma_kernel(Attn
   const char* ib = static_cast<const char*>(p.idx) +
                    (bat * p.i_sb + static_cast<int64_t>(i) * p.i_sn + static_cast<int64_t>(h) * p.i_sh) *
                        (p.index_i64 ? 8 : 4);
-  const int64_t limit = static_cast<int64_t>(p.q_offset) + i;
+  const int64_t limit = seg_pos(p.seg, i);
 
   // ---- Q^T as the B operand: column n = head 8 nt + gid, k = head dims ----
   uint32_t qb[NT][KSTEPS][2];

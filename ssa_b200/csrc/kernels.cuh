@@ -9,6 +9,31 @@
 
 namespace ssa {
 
+// Query rows as up to kMaxSeg runs of consecutive sequence positions: row i
+// of segment s (rows row[s] .. row[s+1]-1) sits at position pos[s] + i - row[s].
+// Positions ascend with the row index.  One segment at q_offset is the plain
+// contiguous block.
+constexpr int kMaxSeg = 8;
+struct QuerySegs {
+  int count;
+  int row[kMaxSeg + 1];
+  int pos[kMaxSeg];
+};
+__device__ __forceinline__ int seg_pos(const QuerySegs& s, int i) {
+  int k = 0;
+#pragma unroll
+  for (int t = 1; t < kMaxSeg; ++t) k += (t < s.count && i >= s.row[t]) ? 1 : 0;
+  return s.pos[k] + (i - s.row[k]);
+}
+inline QuerySegs contiguous_segs(int q_offset, int n_q) {
+  QuerySegs s{};
+  s.count = 1;
+  s.row[0] = 0;
+  s.row[1] = n_q;
+  s.pos[0] = q_offset;
+  return s;
+}
+
 // K0: routing projection.  rows = batch*h_kv*n_rows, row order (bat, h, i).
 struct RouteProjectParams {
   const void* x;           // q [B,n_rows,h_q,d] (group>1) or k [B,n_rows,h_kv,d]
@@ -130,6 +155,7 @@ struct RescoreParams {
   const int32_t* bucket_end;
   int64_t ptr_stride, entry_stride;
   int batch, n, n_q, q_offset, h_kv, group, d, a, b, n_codes, top_k, causal;
+  QuerySegs seg;               // positions of the query rows (ascending)
   int cap;                     // shared-memory candidate capacity (power of two)
   int tier1_rows;              // warp path: query rows per (bat, h) the first tier takes (the
                                // lowest positions; 0 means all n_q)
@@ -179,6 +205,7 @@ struct AttnParams {
   void* out; int64_t o_sb, o_sn, o_sh;
   int32_t* status;
   int batch, n_q, n, q_offset, h_kv, group, d, top_k, causal;
+  QuerySegs seg;               // positions of the query rows
   float inv_scale;
 };
 

@@ -142,7 +142,7 @@ __device__ void rescore_unit_block(const RescoreParams& p, int64_t unit, RsStati
   unit_coords(p, unit, bh, i);
   const int bat = bh / p.h_kv, h = bh % p.h_kv;
   if (rescore_skip_bad_index(p, bat, i, h, threadIdx.x, blockDim.x)) return;
-  const int pos = p.q_offset + i;
+  const int pos = seg_pos(p.seg, i);
   const int a = p.a;
   const int k_eff = min(p.top_k, p.n);
   const int32_t* bk = bucket_base(p, bh);
@@ -430,7 +430,7 @@ __global__ void __launch_bounds__(kWarpUnits * kWarp) rescore_warp_kernel(Rescor
   unit_coords(p, unit, bh, i);
   const int bat = bh / p.h_kv, h = bh % p.h_kv;
   if (rescore_skip_bad_index(p, bat, i, h, lane, kWarp)) return;
-  const int pos = p.q_offset + i;
+  const int pos = seg_pos(p.seg, i);
   const int a = p.a;
   const int k_eff = min(p.top_k, p.n);
   const int32_t* bk = bucket_base(p, bh);

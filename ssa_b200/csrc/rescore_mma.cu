@@ -176,7 +176,7 @@ __device__ __forceinline__ void rescore_mma_unit(const RescoreParams& p, int64_t
   const int i = p.n_q - 1 - static_cast<int>(unit % p.n_q);
   const int bat = bh / p.h_kv, h = bh % p.h_kv;
   if (rescore_skip_bad_index(p, bat, i, h, lane, kWarp)) return;
-  const int pos = p.q_offset + i;
+  const int pos = seg_pos(p.seg, i);
   const int a = p.a;
   const int k_eff = min(p.top_k, p.n);
   const int32_t* bk = bucket_base(p, bh);
@@ -533,8 +533,14 @@ static int tier1_rows(const RescoreParams& p, int cap1) {
   const double limit = 1.25 * cap1;
   if (!p.causal) return per_key * p.n > limit ? 0 : p.n_q;
   const double first_pos = std::ceil(limit / per_key);      // expected count above limit from here on
-  const double rows = first_pos - p.q_offset;
-  return rows <= 0 ? 0 : (rows >= p.n_q ? p.n_q : static_cast<int>(rows));
+  // rows whose position lies below first_pos (positions ascend with the row)
+  int rows = 0;
+  for (int s = 0; s < p.seg.count; ++s) {
+    const double below = first_pos - p.seg.pos[s];
+    const int len = p.seg.row[s + 1] - p.seg.row[s];
+    rows += below <= 0 ? 0 : (below >= len ? len : static_cast<int>(below));
+  }
+  return rows;
 }
 
 // A persistent launch of a list tier: as many CTAs per SM as fit.

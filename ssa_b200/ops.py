@@ -304,6 +304,64 @@ def _route_with_index_fake(q, k, k_codes, bucket_ptr, bucket_keys, w_qr, w_kr, c
 
 
 # ---------------------------------------------------------------------------
+# query rows in segments (several blocks of one sequence in one call)
+# ---------------------------------------------------------------------------
+def segments_struct(blocks) -> L.SsaQuerySegments:
+    """``blocks``: ``[(position, rows), ...]`` in ascending positions."""
+    if not 1 <= len(blocks) <= L.SSA_MAX_SEGMENTS:
+        raise ValueError(f"{len(blocks)} query segments: 1..{L.SSA_MAX_SEGMENTS} supported")
+    s = L.SsaQuerySegments()
+    s.count = len(blocks)
+    for i, (pos, rows) in enumerate(blocks):
+        s.positions[i], s.rows[i] = int(pos), int(rows)
+    return s
+
+
+def route_with_index_segments(q, k, k_codes, bucket_ptr, bucket_keys, w_qr, w_kr, codebook, a, top_k, causal,
+                              temperature, blocks, index_i64=False):
+    """:func:`route_with_index` for query rows ``q [B, n_q, h_q, d]`` that are
+    several runs of positions ``blocks = [(position, rows), ...]`` (ascending),
+    in one call: the GPU of a sequence shard routes all its blocks at once."""
+    dev = _require_cuda(q, k, k_codes, bucket_ptr, bucket_keys, w_qr, w_kr, codebook)
+    q, k = _last_contig(q), _last_contig(k)
+    kc = k_codes.to(torch.int32).contiguous()
+    ptr = bucket_ptr.to(torch.int32).contiguous()
+    keys = bucket_keys.to(torch.int32).contiguous()
+    w_qr, w_kr, codebook = _prep_weights(w_qr, w_kr, codebook, k.dtype)
+    B, n_q, _, _ = q.shape
+    _, n, h_kv, _ = k.shape
+    indices = torch.empty((B, n_q, h_kv, top_k), dtype=torch.int64 if index_i64 else torch.int32, device=dev)
+    args = route_args(q, k, w_qr, w_kr, codebook, a, kc.shape[-1], top_k, causal, temperature, 0, indices,
+                      index_i64, None, kc, None)
+    segs = segments_struct(blocks)
+    slot = S.acquire(dev)
+    args.status = slot.ptr if slot is not None else None
+    ws = workspace(args, dev)
+    with torch.cuda.device(dev):
+        L.check("ssa_route_with_index_segments",
+                L.lib().ssa_route_with_index_segments(ctypes.byref(args), ctypes.byref(segs), ptr.data_ptr(),
+                                                      keys.data_ptr(), ws.data_ptr(), ws.numel(), _stream(dev)))
+        S.release(slot, "ssa_route_with_index_segments", S.route_error)
+    return indices
+
+
+def sparse_attn_segments(q, k, v, indices, scale, causal, blocks):
+    """:func:`sparse_attn` for query rows in runs of positions ``blocks =
+    [(position, rows), ...]`` (ascending), in one launch."""
+    dev = _require_cuda(q, k, v, indices)
+    q, k, v, indices = _last_contig(q), _last_contig(k), _last_contig(v), _last_contig(indices)
+    out = torch.empty(q.shape, dtype=q.dtype, device=dev)
+    segs = segments_struct(blocks)
+    slot = S.acquire(dev)
+    args = attn_args(q, k, v, indices, out, scale, causal, 0, slot.ptr if slot is not None else None)
+    with torch.cuda.device(dev):
+        L.check("ssa_sparse_attn_segments",
+                L.lib().ssa_sparse_attn_segments(ctypes.byref(args), ctypes.byref(segs), _stream(dev)))
+        S.release(slot, "sparse_exact_attention", S.attn_error)
+    return out
+
+
+# ---------------------------------------------------------------------------
 # code_assign
 # ---------------------------------------------------------------------------
 @torch.library.custom_op("ssa_b200::code_assign", mutates_args=())

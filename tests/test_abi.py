@@ -61,7 +61,8 @@ def _c_layout(struct: str, fields):
 
 @pytest.mark.parametrize("cls,name", [(L.SsaRouteArgs, "SsaRouteArgs"), (L.SsaAttnArgs, "SsaAttnArgs"),
                                       (L.SsaRopeArgs, "SsaRopeArgs"),
-                                      (L.SsaDecodeIndex, "SsaDecodeIndex")])
+                                      (L.SsaDecodeIndex, "SsaDecodeIndex"),
+                                      (L.SsaQuerySegments, "SsaQuerySegments")])
 def test_ctypes_structs_match_c_layout(cls, name):
     fields = [f for f, _ in cls._fields_]
     size, offsets = _c_layout(name, fields)
@@ -184,3 +185,36 @@ def test_route_rope_argument_errors(lib, route_over, rope_over, code):
 def test_route_rope_null_rope_is_an_argument_error(lib):
     a = _route_args()
     assert lib.ssa_route_rope(ctypes.byref(a), None, None, 0, None) == 1
+
+
+def _segments(rows, positions):
+    s = L.SsaQuerySegments()
+    s.count = len(rows)
+    for i, (r, p) in enumerate(zip(rows, positions)):
+        s.rows[i], s.positions[i] = r, p
+    return s
+
+
+@pytest.mark.parametrize("rows,positions,ok", [
+    ([32, 32], [0, 32], True),
+    ([16, 48], [0, 16], True),
+    ([32, 32], [32, 0], False),          # positions must ascend
+    ([32, 32], [0, 16], False),          # runs overlap
+    ([32, 31], [0, 32], False),          # rows do not add up to n_q
+    ([32, 32], [0, 40], False),          # the last run ends past n
+    ([8] * 9, list(range(0, 72, 8)), False),   # more than SSA_MAX_SEGMENTS
+])
+def test_segment_argument_checks(lib, rows, positions, ok):
+    """Segment checks run before any launch; valid segments then fail only on
+    the (deliberately missing) workspace, never as argument errors."""
+    a = _route_args(k_codes=0x7000)
+    s = _segments(rows[:8], positions[:8])
+    if len(rows) > 8:
+        s.count = len(rows)
+    rc = lib.ssa_route_with_index_segments(ctypes.byref(a), ctypes.byref(s), 0x8000, 0x9000, None, 0, None)
+    assert rc == (3 if ok else 1), lib.ssa_last_error()
+    at = L.SsaAttnArgs()
+    at.batch, at.n_q, at.n, at.h_q, at.h_kv, at.d, at.top_k, at.scale, at.dtype = 1, 64, 64, 8, 2, 64, 4, 8.0, 1
+    at.q = at.k = at.v = at.indices = at.out = 0x1000
+    if not ok:
+        assert lib.ssa_sparse_attn_segments(ctypes.byref(at), ctypes.byref(s), None) == 1

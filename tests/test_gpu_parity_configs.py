@@ -160,7 +160,7 @@ def test_group_7_fused_rope_routing_matches_oracle():
     cos = torch.cat([ang.cos(), ang.cos()], -1).to(torch.bfloat16)
     sin = torch.cat([ang.sin(), ang.sin()], -1).to(torch.bfloat16)
     idx, q_codes, k_codes, _, q_rot, k_rot = ops.route_rope(
-        t["q"], t["k"], cos, sin, r.W_qr.weight, r.W_kr.weight, r.codebook, shape.a, shape.b, shape.top_k,
+        t["q"], t["k"], cos, sin, r.W_qr.weight.detach(), r.W_kr.weight.detach(), r.codebook.detach(), shape.a, shape.b, shape.top_k,
         True, 1.0, 0, True)
     qn, kn = _np(q_rot[0]), _np(k_rot[0])
     oq, ok = O.route_codes(qn, kn, _np(t["w_qr"]), _np(t["w_kr"]), _np(t["codebook"]), shape.a, shape.b)

@@ -260,3 +260,30 @@ def test_route_with_index_refuses_a_corrupt_index():
             ssa.check_errors()
     # a valid index still gives the same result afterwards
     assert torch.equal(r.route_with_index(q, k, codes, (ptr, keys), causal=True), good)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_segment_calls_match_the_full_route_and_attention(dtype):
+    """A rank's zig-zag blocks routed and attended in one call each (query
+    segments) give exactly the full sequence's rows."""
+    from ssa_b200 import ops, shard
+
+    r = _random_router()
+    g = torch.Generator(device="cpu").manual_seed(9)
+    n = 3072
+    q = torch.randn((2, n, 8, 128), generator=g).to(DEV, dtype)
+    k = torch.randn((2, n, 2, 128), generator=g).to(DEV, dtype)
+    v = torch.randn((2, n, 2, 128), generator=g).to(DEV, dtype)
+    full, _, codes, _ = r.route(q, k, causal=True, index_dtype=torch.int32)
+    out_full = ops.sparse_attn(q, k, v, full, 128 ** 0.5, True, 0)
+    index = r.key_index(codes)
+    for world, folds, rank in [(2, 1, 0), (3, 2, 2), (4, 1, 3)]:
+        blocks = shard.zigzag_blocks(n, world, rank, folds)
+        ql = shard.local_rows(q, world, rank, folds=folds)
+        idx = ops.route_with_index_segments(ql, k, codes, index[0], index[1], r.W_qr.weight.detach(),
+                                            r.W_kr.weight.detach(), r.codebook.detach(), r.codes_per_query,
+                                            r.top_k, True, 1.0, blocks)
+        assert torch.equal(idx, shard.local_rows(full, world, rank, folds=folds)), (world, folds, rank)
+        out = ops.sparse_attn_segments(ql, k, v, idx, 128 ** 0.5, True, blocks)
+        assert torch.equal(out, shard.local_rows(out_full, world, rank, folds=folds)), (world, folds, rank)
+    ssa.check_errors()

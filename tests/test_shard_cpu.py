@@ -55,40 +55,44 @@ def _oracle_fns(p):
         _, k_route = O.route_vectors(np.zeros((kl.shape[0], HQ, D)), kl, w_qr, w_kr)
         return torch.from_numpy(O.stable_topk(O.code_scores(k_route, cb), B).astype(np.int32))[None]
 
-    def route_fn(qb, k, codes, index, q_offset):
-        qn = qb[0].numpy()
-        q_route, _ = O.route_vectors(qn, k[0].numpy()[:qn.shape[0]], w_qr, w_kr)
-        qc = O.stable_topk(O.code_scores(q_route, cb), A)
-        idx = O.select_topk_dense(qn, k[0].numpy(), qc, codes[0].numpy(), TOPK, causal=True,
-                                  q_start=q_offset)
-        return torch.from_numpy(idx)[None]
+    def route_fn(ql, k, codes, index, blocks):
+        outs, r0 = [], 0
+        for q_offset, ln in blocks:                           # the rank's blocks, in position order
+            qn = ql[0, r0:r0 + ln].numpy()
+            q_route, _ = O.route_vectors(qn, k[0].numpy()[:qn.shape[0]], w_qr, w_kr)
+            qc = O.stable_topk(O.code_scores(q_route, cb), A)
+            outs.append(O.select_topk_dense(qn, k[0].numpy(), qc, codes[0].numpy(), TOPK, causal=True,
+                                            q_start=q_offset))
+            r0 += ln
+        return torch.from_numpy(np.concatenate(outs))[None]
 
-    def attn_fn(qb, k, v, idx, q_offset):
-        out = O.sparse_attention(qb[0].numpy(), k[0].numpy(), v[0].numpy(), idx[0].numpy(),
-                                 causal=True, q_offset=q_offset)
+    def attn_fn(ql, k, v, idx, blocks):
+        pos = np.concatenate([np.arange(s, s + ln) for s, ln in blocks])
+        out = O.sparse_attention(ql[0].numpy(), k[0].numpy(), v[0].numpy(), idx[0].numpy(),
+                                 causal=True, positions=pos)
         return torch.from_numpy(out)[None]
 
     return code_fn, route_fn, attn_fn
 
 
-def _worker(rank, world, port, task, result_dir):
+def _worker(rank, world, port, task, result_dir, folds=1):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         if task == "gather":
             full = torch.arange(2 * N * HKV * 3, dtype=torch.int32).reshape(2, N, HKV, 3)
-            local = shard.local_rows(full, world, rank)
-            got = shard.gather_sequence(local, world)
+            local = shard.local_rows(full, world, rank, folds=folds)
+            got = shard.gather_sequence(local, world, folds=folds)
             ok = torch.equal(got, full)
         else:
             p = _problem()
             q, k, v = (torch.from_numpy(x)[None] for x in p[:3])
-            ql, kl, vl = (shard.local_rows(x, world, rank) for x in (q, k, v))
+            ql, kl, vl = (shard.local_rows(x, world, rank, folds=folds) for x in (q, k, v))
             code_fn, route_fn, attn_fn = _oracle_fns(p)
-            out = shard.sharded_forward(None, ql, kl, vl, code_fn=code_fn, index_fn=lambda c: None,
+            out = shard.sharded_forward(None, ql, kl, vl, folds=folds, code_fn=code_fn, index_fn=lambda c: None,
                                         route_fn=route_fn, attn_fn=attn_fn)
-            want = shard.local_rows(torch.from_numpy(_oracle_full(p))[None], world, rank)
+            want = shard.local_rows(torch.from_numpy(_oracle_full(p))[None], world, rank, folds=folds)
             ok = out.shape == want.shape and torch.allclose(out, want, rtol=0, atol=1e-12)
         with open(os.path.join(result_dir, f"rank{rank}"), "w") as f:
             f.write("ok" if ok else "mismatch")
@@ -96,8 +100,8 @@ def _worker(rank, world, port, task, result_dir):
         dist.destroy_process_group()
 
 
-def _run(world, task, tmp_path):
-    mp.spawn(_worker, args=(world, _free_port(), task, str(tmp_path)), nprocs=world, join=True)
+def _run(world, task, tmp_path, folds=1):
+    mp.spawn(_worker, args=(world, _free_port(), task, str(tmp_path), folds), nprocs=world, join=True)
     for r in range(world):
         assert (tmp_path / f"rank{r}").read_text() == "ok", f"rank {r} of {world}"
 
@@ -121,11 +125,24 @@ def test_zigzag_blocks_cover_the_sequence_and_balance_causal_work():
         shard.zigzag_blocks(100, 3, 0)
 
 
-@pytest.mark.parametrize("world", [2, 3])
-def test_gather_sequence_round_trip(world, tmp_path):
-    _run(world, "gather", tmp_path)
+def test_folded_zigzag_blocks_ascend_and_cover_the_sequence():
+    n = 96
+    for world, folds in ((1, 2), (2, 2), (3, 2), (2, 3)):
+        seen = np.zeros(n, dtype=int)
+        for r in range(world):
+            blocks = shard.zigzag_blocks(n, world, r, folds)
+            assert len(blocks) == 2 * folds
+            assert [s for s, _ in blocks] == sorted(s for s, _ in blocks)
+            for s, ln in blocks:
+                seen[s:s + ln] += 1
+        assert (seen == 1).all()
 
 
-@pytest.mark.parametrize("world", [2, 3])
-def test_sharded_forward_matches_single_process(world, tmp_path):
-    _run(world, "forward", tmp_path)
+@pytest.mark.parametrize("world,folds", [(2, 1), (3, 1), (2, 2)])
+def test_gather_sequence_round_trip(world, folds, tmp_path):
+    _run(world, "gather", tmp_path, folds)
+
+
+@pytest.mark.parametrize("world,folds", [(2, 1), (3, 1), (2, 2)])
+def test_sharded_forward_matches_single_process(world, folds, tmp_path):
+    _run(world, "forward", tmp_path, folds)
