@@ -844,6 +844,7 @@ def run_decode(args):
     import torch
 
     import ssa_b200 as ssa
+    from ssa_b200 import _lib as L
     from ssa_b200 import workloads as W
     from ssa_b200.decode import DecodeCache
 
@@ -879,11 +880,27 @@ def run_decode(args):
         e1.record()
         torch.cuda.synchronize(dev)
         ms_inc = e0.elapsed_time(e1) / steps
-        # the same steps with a full index build per step
+        rebuilds = cache.rebuilds - rebuilds0
+        # the index upkeep alone: one append launch (device time) ...
+        first = cache.n - 1
+        args1 = cache._args(cache.n)
+        st = torch.cuda.current_stream(dev).cuda_stream
+        lib = L.lib()
+        # re-appending the last key: the bucket ends are put back after each
+        # timed call so the live index is not changed
+        saved_end = cache.ix_end.clone()
+        ms_append = _device_ms(lambda: L.check("append", lib.ssa_decode_index_append(
+            ctypes.byref(args1), ctypes.byref(cache.index), first, 1, st)), dev, reps=1,
+            after=lambda: cache.ix_end.copy_(saved_end))
+        # ... against the full index build over every cached key
+        codes_now = cache.codes[:, :cache.n].contiguous()
+        ms_build = _device_ms(lambda: r.key_index(codes_now), dev)
+        # the same decode steps with the index rebuilt from every cached key
         codes = cache.codes[:, :p]
         e0.record()
         for s in range(steps):
             pos = n + s
+            r.key_codes(k[:, pos:pos + 1])                 # the new key's codes, as the incremental step does
             idx = r.route_with_key_codes(q[:, pos:pos + 1], k[:, :pos + 1], codes[:, :pos + 1], causal=True,
                                          q_offset=pos, index_dtype=torch.int32)
             ssa.sparse_exact_attention(q[:, pos:pos + 1], k[:, :pos + 1], v[:, :pos + 1], idx, is_causal=True,
@@ -891,16 +908,38 @@ def run_decode(args):
         e1.record()
         torch.cuda.synchronize(dev)
         ssa.check_errors(dev)
-        res[str(n)] = {"ms_per_token": ms_inc, "rebuilds_in_timed_steps": cache.rebuilds - rebuilds0,
-                       "ms_per_token_full_index_build": e0.elapsed_time(e1) / steps}
+        res[str(n)] = {"ms_per_token": ms_inc, "rebuilds_in_timed_steps": rebuilds,
+                       "index_append_ms": ms_append, "full_index_build_ms": ms_build,
+                       "ms_per_token_rebuilding_the_index": e0.elapsed_time(e1) / steps}
         del cache, t, q, k, v
         torch.cuda.empty_cache()
     print(json.dumps({"metric": "SSA decode ms per token (batch 1, config-3 heads, bf16)", "unit": "ms",
                       "higher_is_better": False, "steps": steps, "warmup": args.warmup,
                       "per_cache_length": res,
-                      "note": "full_index_build: route_with_key_codes (index of all cached keys rebuilt each step), "
-                              "without the key-code assignment of the new key"}), flush=True)
+                      "note": "ms_per_token: DecodeCache.step (key codes, index append, routing, attention); "
+                              "index_append_ms / full_index_build_ms: device time of the index upkeep per token "
+                              "against a build over every cached key; ms_per_token_rebuilding_the_index: the same "
+                              "steps through route_with_key_codes, which builds the index of all cached keys"}),
+          flush=True)
     return 0
+
+
+def _device_ms(fn, dev, reps=10, after=None):
+    """Mean device time of ``fn`` (CUDA events around each call; ``after``
+    runs between calls, outside the events)."""
+    import torch
+
+    tot = 0.0
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        tot += e0.elapsed_time(e1)
+        if after is not None:
+            after()
+    return tot / reps
 
 
 def main():

@@ -110,10 +110,17 @@ class DecodeCache:
 
     # -- the index -------------------------------------------------------
     def _refresh_bound(self) -> None:
-        if self._mf_read is not None and self._mf_read[0].query():
-            _, n_at = self._mf_read
-            self._free_lb = int(self._mf_host[0]) - (self.n - n_at)
-            self._mf_read = None
+        """The fewest free slots, from the last read-back: ``n_at`` keys were
+        indexed when it was queued, ``self.n`` are now, so at most
+        ``self.n - n_at`` slots of any bucket were taken since.  When the host
+        runs ahead of the GPU the read-back may still be in flight; waiting
+        for it (a few steps of GPU work) is cheaper than an O(n) rebuild."""
+        if self._mf_read is None:
+            return
+        ev, n_at = self._mf_read
+        ev.synchronize()
+        self._free_lb = int(self._mf_host[0]) - (self.n - n_at)
+        self._mf_read = None
 
     def _index(self, first: int, t: int) -> None:
         lib, st = L.lib(), torch.cuda.current_stream(self.device).cuda_stream
