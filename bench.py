@@ -91,6 +91,8 @@ def parse():
                         "28-layer decoder stack with SSA attention, one batch per GPU")
     p.add_argument("--layers", type=int, default=28, help="config5: decoder layers")
     p.add_argument("--batch", type=int, default=4, help="config5: sequences per GPU")
+    p.add_argument("--folds", type=int, default=4,
+                   help="config4: zig-zag passes; each rank holds 2 * folds blocks of the sequence")
     return p.parse_args()
 
 
@@ -641,14 +643,15 @@ def config4_timing(args, dev, world, rank, steps, warmup):
         router.W_qr.weight.copy_(t["w_qr"])
         router.W_kr.weight.copy_(t["w_kr"])
         router.codebook.copy_(t["codebook"])
-    ql, kl, vl = (shard.local_rows(t[x], world, rank) for x in ("q", "k", "v"))
+    folds = args.folds
+    ql, kl, vl = (shard.local_rows(t[x], world, rank, folds=folds) for x in ("q", "k", "v"))
     del t
     torch.cuda.empty_cache()
     stream = torch.cuda.current_stream(dev)
 
     def step():
         with torch.no_grad():
-            return shard.sharded_forward(router, ql, kl, vl, causal=True)
+            return shard.sharded_forward(router, ql, kl, vl, causal=True, folds=folds)
 
     for _ in range(warmup):
         step()
@@ -678,7 +681,8 @@ def config4_timing(args, dev, world, rank, steps, warmup):
             "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong", "dtype": "bf16",
             "data": "synthetic (seeded on device: Q/K/V ~ N(0,1))",
             "config": {"workload": "config4 (long single sequence, query-split)", **shape.asdict(),
-                       "parallelism": f"query-split x{world} (zig-zag blocks, NCCL all-gather of K, V, codes)",
+                       "parallelism": f"query-split x{world} ({2 * folds} zig-zag blocks per rank routed and "
+                                      "attended in one call each, NCCL all-gather of K, V, codes)",
                        "l2": "inputs 1.6 GB > 126 MB L2, no flush"},
             "clocks": clk}
 
