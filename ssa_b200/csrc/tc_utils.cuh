@@ -49,7 +49,7 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
-// 1-D bulk copy global -> shared, completion counted on `bar` (no multicast).
+// 1-D bulk copy global -> this CTA's shared memory, completion counted on `bar`.
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
@@ -57,7 +57,7 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
       : "memory");
 }
 // 3-D tiled tensor copy global -> shared (TMA), completion counted on `bar`;
-// `map` is the address of a __grid_constant__ CUtensorMap.  No multicast.
+// `map` is the address of a __grid_constant__ CUtensorMap; this CTA only.
 // The innermost coordinate times the element size must be a multiple of 16 bytes.
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* map, int x, int y, int z, uint32_t bar) {
   asm volatile(
