@@ -12,8 +12,9 @@
 //   2. scan (reduce / partials / apply) -- exclusive prefix over (c, t) per
 //      (bat, h): counts become write offsets, bucket_ptr[c] = offset[c][0].
 //   3. index_scatter_kernel -- each tile sorts its (code, entry) pairs in
-//      shared memory (bitonic; pairs are unique, so the order is fixed),
-//      then writes key j at offset[c][t] + rank within its code run.
+//      shared memory (two stable radix passes of 8 bits on the code; pairs
+//      are unique, so the order is fixed), then writes key j at
+//      offset[c][t] + rank within its code run.
 //      Keys are therefore ascending within every bucket.
 #include "common.cuh"
 #include "kernels.cuh"
@@ -153,42 +154,108 @@ __global__ void __launch_bounds__(kScanThreads) scan_apply_kernel(IndexParams p)
 }
 
 // --- stable scatter -------------------------------------------------------
+// Each tile sorts its composite keys (code << 16 | entry) in shared memory by
+// a two-pass LSD radix sort on the code (8 bits a pass).  A pass is stable:
+// warp w ranks its 256 consecutive keys step by step (__match_any_sync on the
+// digit, per-warp digit counters), a block scan over (digit, warp) turns the
+// counters into offsets, and every key moves to offset + rank.  Entries enter
+// in entry order, so after both passes the keys of a code ascend.  Padding
+// keys (0xffffffff) sort last.
+constexpr int kRadixBins = 256;
+constexpr int kScatterWarps = kIndexThreads / kWarp;                  // 16
+constexpr int kPerThread = kIndexSortEntries / kIndexThreads;        // 8 keys a thread
+static_assert(kPerThread * kIndexThreads == kIndexSortEntries, "tile = threads x keys a thread");
+
+struct ScatterSmem {
+  uint32_t keys[2][kIndexSortEntries];
+  uint32_t cnt[kRadixBins * kScatterWarps];   // [digit][warp]
+  uint32_t part[kIndexThreads];
+};
+
+__device__ __forceinline__ void radix_pass(ScatterSmem& s, const uint32_t* src, uint32_t* dst, int shift) {
+  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+  for (int i = threadIdx.x; i < kRadixBins * kScatterWarps; i += blockDim.x) s.cnt[i] = 0;
+  __syncthreads();
+  // warp w owns keys [w * 256, w * 256 + 256): 8 steps of 32, in order
+  uint32_t key[kPerThread], rank[kPerThread];
+#pragma unroll
+  for (int st = 0; st < kPerThread; ++st) {
+    const int e = warp * (kWarp * kPerThread) + st * kWarp + lane;
+    key[st] = src[e];
+    const uint32_t d = (key[st] >> shift) & (kRadixBins - 1);
+    const unsigned peers = __match_any_sync(0xffffffffu, d);
+    uint32_t* c = &s.cnt[d * kScatterWarps + warp];
+    const uint32_t base = *c;
+    rank[st] = base + __popc(peers & ((1u << lane) - 1u));
+    __syncwarp();
+    if (lane == __ffs(peers) - 1) *c = base + __popc(peers);
+    __syncwarp();
+  }
+  __syncthreads();
+  // exclusive scan of cnt in (digit, warp) order: each thread 8 consecutive counters
+  uint32_t local[kPerThread], sum = 0;
+#pragma unroll
+  for (int t = 0; t < kPerThread; ++t) {
+    local[t] = s.cnt[threadIdx.x * kPerThread + t];
+    sum += local[t];
+  }
+  uint32_t incl = sum;
+#pragma unroll
+  for (int o = 1; o < kWarp; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == kWarp - 1) s.part[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t v = lane < kScatterWarps ? s.part[lane] : 0u, w = v;
+#pragma unroll
+    for (int o = 1; o < kWarp; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < kScatterWarps) s.part[lane] = w - v;                  // exclusive over warps
+  }
+  __syncthreads();
+  uint32_t run = s.part[warp] + incl - sum;
+#pragma unroll
+  for (int t = 0; t < kPerThread; ++t) {
+    s.cnt[threadIdx.x * kPerThread + t] = run;
+    run += local[t];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int st = 0; st < kPerThread; ++st) {
+    const uint32_t d = (key[st] >> shift) & (kRadixBins - 1);
+    dst[s.cnt[d * kScatterWarps + warp] + rank[st]] = key[st];
+  }
+  __syncthreads();
+}
+
 __global__ void __launch_bounds__(kIndexThreads) index_scatter_kernel(IndexParams p) {
-  __shared__ uint32_t keys[kIndexSortEntries];
+  extern __shared__ __align__(16) unsigned char scatter_smem[];
+  ScatterSmem& s = *reinterpret_cast<ScatterSmem*>(scatter_smem);
   const int t = blockIdx.x;
   const int bh = blockIdx.y;
   const int h = bh % p.h_kv, bat = bh / p.h_kv;
   const int j0 = t * p.tile_keys;
   const int nk = min(p.tile_keys, p.n - j0);
   const int entries = nk * p.b;
-  int size = 1;
-  while (size < entries) size <<= 1;
-  // composite key (code << 16 | entry): unique within the tile
-  for (int e = threadIdx.x; e < size; e += blockDim.x) {
+  // composite key (code << 16 | entry): unique within the tile; padding last
+  for (int e = threadIdx.x; e < kIndexSortEntries; e += blockDim.x) {
     uint32_t kv = 0xffffffffu;
     if (e < entries) {
-      const int jl = e / p.b, s = e % p.b;
+      const int jl = e / p.b, sl = e % p.b;
       const uint32_t c = static_cast<uint32_t>(checked_code(
-          p.k_codes[bat * p.k_codes_sb + (static_cast<int64_t>(j0 + jl) * p.h_kv + h) * p.b + s], p.n_codes, nullptr));
+          p.k_codes[bat * p.k_codes_sb + (static_cast<int64_t>(j0 + jl) * p.h_kv + h) * p.b + sl], p.n_codes, nullptr));
       kv = (c << 16) | static_cast<uint32_t>(e);
     }
-    keys[e] = kv;
+    s.keys[0][e] = kv;
   }
   __syncthreads();
-  // ascending bitonic sort
-  for (int k2 = 2; k2 <= size; k2 <<= 1) {
-    for (int j = k2 >> 1; j > 0; j >>= 1) {
-      for (int e = threadIdx.x; e < size; e += blockDim.x) {
-        const int ixj = e ^ j;
-        if (ixj > e) {
-          const uint32_t x = keys[e], y = keys[ixj];
-          const bool up = (e & k2) == 0;
-          if ((x > y) == up) { keys[e] = y; keys[ixj] = x; }
-        }
-      }
-      __syncthreads();
-    }
-  }
+  radix_pass(s, s.keys[0], s.keys[1], 16);      // low 8 bits of the code
+  radix_pass(s, s.keys[1], s.keys[0], 24);      // high 8 bits
+  const uint32_t* keys = s.keys[0];
   const uint32_t* off = p.counts + static_cast<int64_t>(bh) * p.n_codes * p.tiles;
   int32_t* dst = p.bucket_keys + static_cast<int64_t>(bh) * p.n * p.b;
   for (int e = threadIdx.x; e < entries; e += blockDim.x) {
@@ -270,7 +337,9 @@ cudaError_t launch_build_index(const IndexParams& p, cudaStream_t st) {
   scan_reduce_kernel<<<g2, kScanThreads, 0, st>>>(p);
   scan_partials_kernel<<<bhs, kScanThreads, 0, st>>>(p);
   scan_apply_kernel<<<g2, kScanThreads, 0, st>>>(p);
-  index_scatter_kernel<<<g1, kIndexThreads, 0, st>>>(p);
+  cudaFuncSetAttribute(index_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       static_cast<int>(sizeof(ScatterSmem)));
+  index_scatter_kernel<<<g1, kIndexThreads, sizeof(ScatterSmem), st>>>(p);
   return cudaGetLastError();
 }
 
