@@ -174,6 +174,27 @@ ssa_status ssa_route_with_index_segments(const SsaRouteArgs* args, const SsaQuer
                                          const int32_t* bucket_ptr, const int32_t* bucket_keys, void* workspace,
                                          size_t workspace_bytes, void* stream);
 
+/* ssa_route_with_index_segments in two calls, so that a GPU of a
+ * query-sharded sequence computes its query codes while the keys, their
+ * codes and the index are still on their way.
+ *
+ * ssa_query_codes: the query half of stage 1 (ssa/router.py:102-112 and the
+ * query top-a of :130): the a codes of every query group into args->q_codes
+ * (required).  Reads q, w_qr and codebook.  The key fields (k, w_kr, n, b)
+ * are checked as for ssa_route but not read: a caller without its keys yet
+ * may describe its own query rows there (n = n_q).
+ *
+ * ssa_select_candidates_segments: stage 2 for query rows in segments over
+ * given codes and a given index -- reads q, k, args->q_codes (a code outside
+ * [0, n_codes) sets SSA_DEVICE_BAD_CODE), args->k_codes and the index
+ * (checked on the device as in ssa_route_with_index); w_qr / w_kr / codebook
+ * are checked but not read.  The two calls together give exactly the indices
+ * of ssa_route_with_index_segments. */
+ssa_status ssa_query_codes(const SsaRouteArgs* args, void* workspace, size_t workspace_bytes, void* stream);
+ssa_status ssa_select_candidates_segments(const SsaRouteArgs* args, const SsaQuerySegments* segments,
+                                          const int32_t* bucket_ptr, const int32_t* bucket_keys,
+                                          void* workspace, size_t workspace_bytes, void* stream);
+
 /* Rotary position embedding applied on load by ssa_route_rope: the
  * rotate-half form of the Qwen2 path of the reference
  * (training/train_qwen.py:134-135, transformers' apply_rotary_pos_emb):

@@ -108,6 +108,10 @@ SIGNATURES = {
     "ssa_route_with_index_segments": (ctypes.c_int, [ctypes.POINTER(SsaRouteArgs), ctypes.POINTER(SsaQuerySegments),
                                                      _vp, _vp, _vp, ctypes.c_size_t, _vp]),
     "ssa_sparse_attn_segments": (ctypes.c_int, [ctypes.POINTER(SsaAttnArgs), ctypes.POINTER(SsaQuerySegments), _vp]),
+    "ssa_query_codes": (ctypes.c_int, [ctypes.POINTER(SsaRouteArgs), _vp, ctypes.c_size_t, _vp]),
+    "ssa_select_candidates_segments": (ctypes.c_int, [ctypes.POINTER(SsaRouteArgs),
+                                                      ctypes.POINTER(SsaQuerySegments), _vp, _vp, _vp,
+                                                      ctypes.c_size_t, _vp]),
     "ssa_status_str": (ctypes.c_char_p, [ctypes.c_int]),
     "ssa_last_error": (ctypes.c_char_p, []),
 }

@@ -713,6 +713,40 @@ ssa_status ssa_route_with_index_segments(const SsaRouteArgs* args, const SsaQuer
   return run_rescore(*args, L, workspace, st, qc, args->k_codes, bucket_ptr, bucket_keys, bad, nullptr, &segs);
 }
 
+ssa_status ssa_query_codes(const SsaRouteArgs* args, void* workspace, size_t workspace_bytes, void* stream) {
+  ssa_status s = check_route(args, true, false);
+  if (s != SSA_OK) return s;
+  if (!args->q_codes) return fail(SSA_ERR_INVALID_ARG, "q_codes is NULL (it is the output here)");
+  const RouteLayout L = route_layout(*args);
+  if (!workspace || workspace_bytes < L.total)
+    return fail(SSA_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", L.total, workspace_bytes);
+  if (args->batch == 0 || args->n_q == 0) return SSA_OK;
+  return run_stage1(*args, L, workspace, static_cast<cudaStream_t>(stream), false, true, args->q_codes, nullptr);
+}
+
+ssa_status ssa_select_candidates_segments(const SsaRouteArgs* args, const SsaQuerySegments* segments,
+                                          const int32_t* bucket_ptr, const int32_t* bucket_keys,
+                                          void* workspace, size_t workspace_bytes, void* stream) {
+  ssa_status s = check_route(args, true, true);
+  if (s != SSA_OK) return s;
+  ssa::QuerySegs segs;
+  s = check_segments(segments, args->n_q, args->n, segs);
+  if (s != SSA_OK) return s;
+  if (!args->q_codes || !args->k_codes || !bucket_ptr || !bucket_keys)
+    return fail(SSA_ERR_INVALID_ARG, "q_codes, k_codes, bucket_ptr and bucket_keys are inputs here and must be set");
+  const RouteLayout L = route_layout(*args);
+  if (!workspace || workspace_bytes < L.total)
+    return fail(SSA_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", L.total, workspace_bytes);
+  if (args->batch == 0 || args->n_q == 0) return SSA_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int32_t* bad = at<int32_t>(workspace, L.flags);
+  cudaError_t e = ssa::launch_validate_index(bucket_ptr, bucket_keys, static_cast<int64_t>(args->batch) * args->h_kv,
+                                             args->n_codes, args->n, args->b, bad, args->status, st);
+  if (e != cudaSuccess) return cuda_status(e, "validate_index");
+  return run_rescore(*args, L, workspace, st, args->q_codes, args->k_codes, bucket_ptr, bucket_keys, bad, nullptr,
+                     &segs);
+}
+
 ssa_status ssa_sparse_attn_segments(const SsaAttnArgs* a, const SsaQuerySegments* segments, void* stream) {
   ssa::AttnParams p{};
   ssa_status s = attn_params(a, p);

@@ -345,6 +345,64 @@ def route_with_index_segments(q, k, k_codes, bucket_ptr, bucket_keys, w_qr, w_kr
     return indices
 
 
+def query_codes(q, w_qr, codebook, a, h_kv, temperature=1.0):
+    """The query half of stage 1: ``q [B, n_q, h_q, d]`` -> the ``a`` codes
+    ``[B, n_q, h_kv, a]`` int32 of every query group (``ssa_query_codes``).
+    Needs no keys: the first half of :func:`route_with_index_segments` for a
+    GPU whose keys are still being gathered."""
+    dev = _require_cuda(q, w_qr, codebook)
+    q = _last_contig(q)
+    w_qr, _, codebook = _prep_weights(w_qr, w_qr, codebook, q.dtype)
+    B, n_q, h_q, _ = q.shape
+    if h_q % h_kv:
+        raise ValueError(f"num_q_heads ({h_q}) must be a multiple of num_kv_heads ({h_kv})")
+    q_codes = torch.empty((B, n_q, h_kv, a), dtype=torch.int32, device=dev)
+    if B == 0 or n_q == 0:
+        return q_codes
+    # the key fields describe the query rows themselves (checked, not read)
+    args = route_args(q, q[:, :, :h_kv], w_qr, w_qr, codebook, a, 1, 1, False, temperature, 0,
+                      q_codes=q_codes)
+    slot = S.acquire(dev)
+    args.status = slot.ptr if slot is not None else None
+    ws = workspace(args, dev)
+    with torch.cuda.device(dev):
+        L.check("ssa_query_codes", L.lib().ssa_query_codes(ctypes.byref(args), ws.data_ptr(), ws.numel(),
+                                                           _stream(dev)))
+        S.release(slot, "ssa_query_codes", S.route_error)
+    return q_codes
+
+
+def select_candidates_segments(q, k, q_codes, k_codes, bucket_ptr, bucket_keys, top_k, causal, blocks,
+                               index_i64=False):
+    """The second half of :func:`route_with_index_segments`: stage 2 for the
+    query rows ``q`` in runs of positions ``blocks`` from their codes
+    ``q_codes`` (:func:`query_codes`), the keys' codes and their index."""
+    dev = _require_cuda(q, k, q_codes, k_codes, bucket_ptr, bucket_keys)
+    q, k = _last_contig(q), _last_contig(k)
+    qc = q_codes.to(torch.int32).contiguous()
+    kc = k_codes.to(torch.int32).contiguous()
+    ptr = bucket_ptr.to(torch.int32).contiguous()
+    keys = bucket_keys.to(torch.int32).contiguous()
+    B, n_q, _, d = q.shape
+    # routing weights are not read by stage 2; these placeholders carry N_c
+    w = torch.empty((4, d), dtype=k.dtype, device=dev)
+    cb = torch.empty((1, ptr.shape[-1] - 1, 4), dtype=k.dtype, device=dev)
+    indices = torch.empty((B, n_q, k.shape[2], top_k), dtype=torch.int64 if index_i64 else torch.int32,
+                          device=dev)
+    args = route_args(q, k, w, w, cb, qc.shape[-1], kc.shape[-1], top_k, causal, 1.0, 0, indices, index_i64,
+                      qc, kc, None)
+    segs = segments_struct(blocks)
+    slot = S.acquire(dev)
+    args.status = slot.ptr if slot is not None else None
+    ws = workspace(args, dev)
+    with torch.cuda.device(dev):
+        L.check("ssa_select_candidates_segments",
+                L.lib().ssa_select_candidates_segments(ctypes.byref(args), ctypes.byref(segs), ptr.data_ptr(),
+                                                       keys.data_ptr(), ws.data_ptr(), ws.numel(), _stream(dev)))
+        S.release(slot, "ssa_select_candidates_segments", S.route_error)
+    return indices
+
+
 def sparse_attn_segments(q, k, v, indices, scale, causal, blocks):
     """:func:`sparse_attn` for query rows in runs of positions ``blocks =
     [(position, rows), ...]`` (ascending), in one launch."""

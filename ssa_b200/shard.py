@@ -17,12 +17,17 @@ Per forward (:func:`sharded_forward`):
 2. the one exchange step: all-gather of the key codes, K and V into
    full-sequence buffers, in that order (collectives run in issue order, so
    the small code gather is issued first);
-3. the code->key index of all ``n`` keys, built once as soon as the codes
-   have arrived -- K and V are still moving meanwhile;
-4. one routing call for all of the rank's query blocks against all ``n``
-   keys with the gathered codes and the index (query segments: each block at
-   its own sequence position) -- V is still arriving meanwhile -- then one
-   sparse-attention call over the selected keys.
+3. the query codes of the rank's own query rows, which need nothing from
+   the other ranks (``ssa/router.py:102-112,130``), while the gathers move;
+4. the code->key index of all ``n`` keys, built once as soon as the codes
+   have arrived;
+5. one candidate-selection call for all of the rank's query blocks against
+   all ``n`` keys (query segments: each block at its own sequence position)
+   -- V is still arriving meanwhile -- then one sparse-attention call over
+   the selected keys.
+
+On GPUs the gathered rows are put back in sequence order on a side stream,
+so that the copies overlap the routing kernels.
 
 The reference has no distributed code; this follows the per-query
 independence of ``CodebookRouter.forward`` (``ssa/router.py:73-149``) and
@@ -74,12 +79,25 @@ def _block_order(world: int, folds: int = 1) -> torch.Tensor:
     return order
 
 
+_orders = {}
+
+
+def _device_block_order(world: int, folds: int, device: torch.device) -> torch.Tensor:
+    """:func:`_block_order` kept on the device, so that a forward issues no
+    host-to-device copy."""
+    key = (world, folds, str(device))
+    if key not in _orders:
+        _orders[key] = _block_order(world, folds).to(device)
+    return _orders[key]
+
+
 def gather_sequence(local: torch.Tensor, world: int, group=None, async_op: bool = False, folds: int = 1):
     """All-gather the zig-zag shards ``local [B, 2*folds*blk, ...]`` of every
     rank into the full sequence ``[B, 2*folds*W*blk, ...]`` (sequence on dim 1).
 
     With ``async_op`` returns ``(work, finish)``: wait on ``work``, then call
-    ``finish()`` for the full tensor."""
+    ``finish()`` for the full tensor (on any stream: the gathered buffer is
+    marked as used by the stream ``finish`` runs on)."""
     B, rows = local.shape[0], local.shape[1]
     per = 2 * folds
     if rows % per:
@@ -92,7 +110,11 @@ def gather_sequence(local: torch.Tensor, world: int, group=None, async_op: bool 
     work = dist.all_gather_into_tensor(buf, mine, group=group, async_op=async_op)
 
     def finish() -> torch.Tensor:
-        order = _block_order(world, folds).to(local.device)
+        if buf.is_cuda:
+            buf.record_stream(torch.cuda.current_stream(buf.device))
+            order = _device_block_order(world, folds, buf.device)
+        else:
+            order = _block_order(world, folds)
         full = buf.index_select(0, order)                                 # [per*W, B, blk, ...]
         return full.transpose(0, 1).reshape((B, per * world * blk) + tail)
 
@@ -101,10 +123,38 @@ def gather_sequence(local: torch.Tensor, world: int, group=None, async_op: bool 
     return finish()
 
 
+_side_streams = {}
+
+
+def _arrive(work, finish, side):
+    """Wait for one all-gather and put its rows in sequence order.  On a GPU
+    both happen on the side stream ``side`` and the caller's stream waits for
+    them only where it uses the result (:func:`_use`); on CPU ranks, here."""
+    if side is None:
+        work.wait()
+        return finish(), None
+    main = torch.cuda.current_stream(side.device)
+    with torch.cuda.stream(side):
+        work.wait()
+        full = finish()
+        ready = torch.cuda.Event()
+        ready.record(side)
+    full.record_stream(main)
+    return full, ready
+
+
+def _use(x, ready):
+    """``x`` from :func:`_arrive`, once the current stream may read it."""
+    if ready is not None:
+        torch.cuda.current_stream(x.device).wait_event(ready)
+    return x
+
+
 def sharded_forward(router, q_local: torch.Tensor, k_local: torch.Tensor, v_local: torch.Tensor,
                     group=None, causal: bool = True, scale: Optional[float] = None, folds: int = 1,
-                    code_fn: Optional[Callable] = None, index_fn: Optional[Callable] = None,
-                    route_fn: Optional[Callable] = None, attn_fn: Optional[Callable] = None) -> torch.Tensor:
+                    code_fn: Optional[Callable] = None, query_code_fn: Optional[Callable] = None,
+                    index_fn: Optional[Callable] = None, route_fn: Optional[Callable] = None,
+                    attn_fn: Optional[Callable] = None) -> torch.Tensor:
     """SSA forward of this rank's query rows of one sequence.
 
     ``q_local [B, rows, h_q, d]``, ``k_local``/``v_local [B, rows, h_kv, d]``
@@ -112,14 +162,15 @@ def sharded_forward(router, q_local: torch.Tensor, k_local: torch.Tensor, v_loca
     (:func:`local_rows`); returns the attention output for those rows,
     ``[B, rows, h_q, d]``.
 
-    ``code_fn(k) -> codes``, ``index_fn(codes) -> index``,
-    ``route_fn(q_local, k, codes, index, blocks) -> indices`` and
+    ``code_fn(k) -> key codes``, ``query_code_fn(q_local) -> query codes``,
+    ``index_fn(codes) -> index``,
+    ``route_fn(q_local, k, q_codes, codes, index, blocks) -> indices`` and
     ``attn_fn(q_local, k, v, indices, blocks) -> out`` (``blocks`` =
     ``[(start, length), ...]`` of the local rows, ascending) default to the
-    sm_100a kernels (:meth:`CodebookRouter.key_codes`,
-    :meth:`CodebookRouter.key_index`, routing and sparse attention over query
-    segments); they are parameters so that the exchange logic can be checked
-    on CPU ranks."""
+    sm_100a kernels (:meth:`CodebookRouter.key_codes`, ``ssa_query_codes``,
+    :meth:`CodebookRouter.key_index`, candidate selection and sparse attention
+    over query segments); they are parameters so that the exchange logic can
+    be checked on CPU ranks."""
     from . import ops
 
     world = dist.get_world_size(group)
@@ -131,30 +182,36 @@ def sharded_forward(router, q_local: torch.Tensor, k_local: torch.Tensor, v_loca
         scale = math.sqrt(q_local.shape[-1])
     if code_fn is None:
         code_fn = router.key_codes
+    if query_code_fn is None:
+        def query_code_fn(ql):
+            return ops.query_codes(ql, router.W_qr.weight, router.codebook, router.codes_per_query,
+                                   router.num_kv_heads, float(router.temperature))
     if index_fn is None:
         index_fn = router.key_index
     if route_fn is None:
-        def route_fn(ql, k, codes, index, blks):
-            return ops.route_with_index_segments(ql, k, codes, index[0], index[1], router.W_qr.weight,
-                                                 router.W_kr.weight, router.codebook, router.codes_per_query,
-                                                 router.top_k, bool(causal), float(router.temperature), blks)
+        def route_fn(ql, k, qc, codes, index, blks):
+            return ops.select_candidates_segments(ql, k, qc, codes, index[0], index[1], router.top_k,
+                                                  bool(causal), blks)
     if attn_fn is None:
         def attn_fn(ql, k, v, idx, blks):
             return ops.sparse_attn_segments(ql, k, v, idx, float(scale), bool(causal), blks)
 
+    side = None
+    if q_local.is_cuda:
+        dev = q_local.device
+        if dev not in _side_streams:
+            _side_streams[dev] = torch.cuda.Stream(dev, priority=-1)
+        side = _side_streams[dev]
+        side.wait_stream(torch.cuda.current_stream(dev))
+
     # the exchange.  The codes go first: the index built from them needs
-    # neither K nor V, so it is built while K and V are still moving (a code
-    # gather issued after them would wait for both).
+    # neither K nor V.  The query codes need nothing from the other ranks and
+    # are computed while all three gathers are in flight; the reordering of
+    # the gathered rows runs on a side stream, overlapped with routing.
     codes_local = code_fn(k_local)
-    c_work, c_finish = gather_sequence(codes_local, world, group, async_op=True, folds=folds)
-    k_work, k_finish = gather_sequence(k_local, world, group, async_op=True, folds=folds)
-    v_work, v_finish = gather_sequence(v_local, world, group, async_op=True, folds=folds)
-    c_work.wait()
-    codes = c_finish()
-    index = index_fn(codes)
-    k_work.wait()
-    k_full = k_finish()
-    idx = route_fn(q_local, k_full, codes, index, blocks)
-    v_work.wait()
-    v_full = v_finish()
-    return attn_fn(q_local, k_full, v_full, idx, blocks)
+    gathers = [gather_sequence(x, world, group, async_op=True, folds=folds) for x in (codes_local, k_local, v_local)]
+    q_codes = query_code_fn(q_local)
+    (codes, c_ready), (k_full, k_ready), (v_full, v_ready) = (_arrive(w, f, side) for w, f in gathers)
+    index = index_fn(_use(codes, c_ready))
+    idx = route_fn(q_local, _use(k_full, k_ready), q_codes, codes, index, blocks)
+    return attn_fn(q_local, k_full, _use(v_full, v_ready), idx, blocks)

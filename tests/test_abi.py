@@ -213,6 +213,9 @@ def test_segment_argument_checks(lib, rows, positions, ok):
         s.count = len(rows)
     rc = lib.ssa_route_with_index_segments(ctypes.byref(a), ctypes.byref(s), 0x8000, 0x9000, None, 0, None)
     assert rc == (3 if ok else 1), lib.ssa_last_error()
+    a.q_codes = 0xa000
+    rc = lib.ssa_select_candidates_segments(ctypes.byref(a), ctypes.byref(s), 0x8000, 0x9000, None, 0, None)
+    assert rc == (3 if ok else 1), lib.ssa_last_error()
     at = L.SsaAttnArgs()
     at.batch, at.n_q, at.n, at.h_q, at.h_kv, at.d, at.top_k, at.scale, at.dtype = 1, 64, 64, 8, 2, 64, 4, 8.0, 1
     at.q = at.k = at.v = at.indices = at.out = 0x1000

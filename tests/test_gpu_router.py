@@ -284,6 +284,10 @@ def test_segment_calls_match_the_full_route_and_attention(dtype):
                                             r.W_kr.weight.detach(), r.codebook.detach(), r.codes_per_query,
                                             r.top_k, True, 1.0, blocks)
         assert torch.equal(idx, shard.local_rows(full, world, rank, folds=folds)), (world, folds, rank)
+        # the same call split in two: query codes first (no keys), then stage 2
+        qc = ops.query_codes(ql, r.W_qr.weight.detach(), r.codebook.detach(), r.codes_per_query, 2)
+        idx2 = ops.select_candidates_segments(ql, k, qc, codes, index[0], index[1], r.top_k, True, blocks)
+        assert torch.equal(idx2, idx), (world, folds, rank)
         out = ops.sparse_attn_segments(ql, k, v, idx, 128 ** 0.5, True, blocks)
         assert torch.equal(out, shard.local_rows(out_full, world, rank, folds=folds)), (world, folds, rank)
     ssa.check_errors()

@@ -47,10 +47,13 @@ def _worker(rank, world, port, result_dir):
         # single-GPU result of the whole sequence, on this rank's GPU
         idx, _, _, _ = router.route(q, k, causal=True, index_dtype=torch.int32)
         full = ops.sparse_attn(q, k, v, idx, 128 ** 0.5, True, 0)
-        ql, kl, vl = (shard.local_rows(x, world, rank) for x in (q, k, v))
-        out = shard.sharded_forward(router, ql, kl, vl, causal=True)
-        torch.cuda.synchronize(dev)
-        ok = torch.equal(out, shard.local_rows(full, world, rank))
+        ok = True
+        for folds in (1, 2, 2):            # the repeat reuses the side stream and the cached block order
+            ql, kl, vl = (shard.local_rows(x, world, rank, folds=folds) for x in (q, k, v))
+            out = shard.sharded_forward(router, ql, kl, vl, causal=True, folds=folds)
+            torch.cuda.synchronize(dev)
+            ok = ok and torch.equal(out, shard.local_rows(full, world, rank, folds=folds))
+        ssa.check_errors(dev)
         with open(os.path.join(result_dir, f"rank{rank}"), "w") as f:
             f.write("ok" if ok else "mismatch")
     finally:

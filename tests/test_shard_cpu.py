@@ -55,14 +55,17 @@ def _oracle_fns(p):
         _, k_route = O.route_vectors(np.zeros((kl.shape[0], HQ, D)), kl, w_qr, w_kr)
         return torch.from_numpy(O.stable_topk(O.code_scores(k_route, cb), B).astype(np.int32))[None]
 
-    def route_fn(ql, k, codes, index, blocks):
+    def query_code_fn(ql):                                 # [1, rows, h_q, d] -> [1, rows, h_kv, a]
+        qn = ql[0].numpy()
+        q_route, _ = O.route_vectors(qn, np.zeros((qn.shape[0], HKV, D)), w_qr, w_kr)
+        return torch.from_numpy(O.stable_topk(O.code_scores(q_route, cb), A).astype(np.int32))[None]
+
+    def route_fn(ql, k, qc, codes, index, blocks):
         outs, r0 = [], 0
         for q_offset, ln in blocks:                           # the rank's blocks, in position order
             qn = ql[0, r0:r0 + ln].numpy()
-            q_route, _ = O.route_vectors(qn, k[0].numpy()[:qn.shape[0]], w_qr, w_kr)
-            qc = O.stable_topk(O.code_scores(q_route, cb), A)
-            outs.append(O.select_topk_dense(qn, k[0].numpy(), qc, codes[0].numpy(), TOPK, causal=True,
-                                            q_start=q_offset))
+            outs.append(O.select_topk_dense(qn, k[0].numpy(), qc[0, r0:r0 + ln].numpy(), codes[0].numpy(),
+                                            TOPK, causal=True, q_start=q_offset))
             r0 += ln
         return torch.from_numpy(np.concatenate(outs))[None]
 
@@ -72,7 +75,7 @@ def _oracle_fns(p):
                                  causal=True, positions=pos)
         return torch.from_numpy(out)[None]
 
-    return code_fn, route_fn, attn_fn
+    return code_fn, query_code_fn, route_fn, attn_fn
 
 
 def _worker(rank, world, port, task, result_dir, folds=1):
@@ -89,8 +92,9 @@ def _worker(rank, world, port, task, result_dir, folds=1):
             p = _problem()
             q, k, v = (torch.from_numpy(x)[None] for x in p[:3])
             ql, kl, vl = (shard.local_rows(x, world, rank, folds=folds) for x in (q, k, v))
-            code_fn, route_fn, attn_fn = _oracle_fns(p)
-            out = shard.sharded_forward(None, ql, kl, vl, folds=folds, code_fn=code_fn, index_fn=lambda c: None,
+            code_fn, query_code_fn, route_fn, attn_fn = _oracle_fns(p)
+            out = shard.sharded_forward(None, ql, kl, vl, folds=folds, code_fn=code_fn,
+                                        query_code_fn=query_code_fn, index_fn=lambda c: None,
                                         route_fn=route_fn, attn_fn=attn_fn)
             want = shard.local_rows(torch.from_numpy(_oracle_full(p))[None], world, rank, folds=folds)
             ok = out.shape == want.shape and torch.allclose(out, want, rtol=0, atol=1e-12)
