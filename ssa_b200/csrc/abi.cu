@@ -3,8 +3,10 @@
 // This layer validates arguments, lays out the caller's workspace and
 // launches the stage kernels on the caller's stream.  It never allocates.
 #include <algorithm>
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -52,10 +54,41 @@ int rescore_cap(int k_eff) {
 struct RouteLayout {
   size_t q_route, k_route, cb_norm, cb_image, q_codes, k_codes, counts, partials, bucket_ptr,
       bucket_keys, bucket_codes, ovf, ovf2, ovf3, flags;
+  // bucket-major re-score (rescore_bucket.cu), when `bucket`
+  bool bucket;
+  size_t qbar, q_ptr, q_rows, q_counts, q_partials, part, seg_off, cursor, cand;
+  int64_t cand_capacity;
   size_t total;
   int tiles;
   int64_t chunks;
 };
+
+// The bucket-major re-score runs where it applies (16-bit q/k, d 64 or 128,
+// b = 4, a <= 32, min(top_k, n) <= 512) unless SSA_RESCORE=walk selects the
+// walking kernel for every unit (both give the same indices).
+bool bucket_rescore(const SsaRouteArgs& a) {
+  const char* env = std::getenv("SSA_RESCORE");
+  if (env && std::strcmp(env, "walk") == 0) return false;
+  return ssa::rescore_bucket_supported(a.d, a.a, a.b, std::min(a.top_k, a.n), true, static_cast<ssa_dtype>(a.dtype));
+}
+
+// Candidate-buffer entries a unit is given: twice the larger of k and the
+// candidates expected with uniformly used codes (a * b / n_codes of the keys
+// a query sees; under the causal mask a query sees its prefix, taken at the
+// middle of the call's rows or of the sequence, whichever is later).  A unit
+// that finds the buffer full is re-scored by the walking kernel instead.
+// SSA_RESCORE_UNIT_ROOM=<entries> overrides the figure (tests use a small
+// value to send units down the walking kernel).
+int64_t cand_per_unit(const SsaRouteArgs& a) {
+  if (const char* env = std::getenv("SSA_RESCORE_UNIT_ROOM")) {
+    const long long v = std::atoll(env);
+    if (v >= 0) return v;
+  }
+  const double visible = a.causal ? std::min<double>(a.n, std::max(a.q_offset + a.n_q / 2.0, a.n / 2.0)) : a.n;
+  const double expect = static_cast<double>(a.a) * a.b * visible / a.n_codes;
+  const double per = 2.0 * std::max<double>(std::min(a.top_k, a.n), expect);
+  return std::min<int64_t>(static_cast<int64_t>(std::ceil(per)), static_cast<int64_t>(a.n) * a.b);
+}
 
 RouteLayout route_layout(const SsaRouteArgs& a) {
   RouteLayout L{};
@@ -82,6 +115,22 @@ RouteLayout route_layout(const SsaRouteArgs& a) {
   L.ovf2 = take((2 + static_cast<size_t>(B * hk) * a.n_q) * 4);  // second-tier count, claim counter, list
   L.ovf3 = take((2 + static_cast<size_t>(B * hk) * a.n_q) * 4);  // third tier, the same
   L.flags = take(4);                                               // index-validation flag
+  L.bucket = a.a >= 1 && bucket_rescore(a);
+  if (L.bucket) {
+    const int64_t units = B * hk * a.n_q;
+    const int qtiles = static_cast<int>(ssa::cdiv(a.n_q, ssa::index_tile_keys(a.a)));
+    const int64_t qchunks = ssa::cdiv(static_cast<int64_t>(a.n_codes) * qtiles, ssa::kScanChunk);
+    L.qbar = take(static_cast<size_t>(units) * 2 * a.d * 2);
+    L.q_ptr = take(static_cast<size_t>(B * hk) * (a.n_codes + 1) * 4);
+    L.q_rows = take(static_cast<size_t>(B * hk) * a.n_q * a.a * 4);
+    L.q_counts = take(static_cast<size_t>(B * hk) * a.n_codes * qtiles * 4);
+    L.q_partials = take(static_cast<size_t>(B * hk * qchunks) * 4);
+    L.part = take(static_cast<size_t>(units) * (a.a + 1) * 4);
+    L.seg_off = take(static_cast<size_t>(units) * 8);
+    L.cursor = take(8);
+    L.cand_capacity = units * cand_per_unit(a);
+    L.cand = take(static_cast<size_t>(L.cand_capacity) * 8);
+  }
   L.total = off;
   return L;
 }
@@ -292,6 +341,18 @@ ssa_status run_rescore(const SsaRouteArgs& a, const RouteLayout& L, void* ws, cu
   rp.ovf3_count = at<int32_t>(ws, L.ovf3);
   rp.ovf3_next = at<int32_t>(ws, L.ovf3) + 1;
   rp.ovf3_list = at<int32_t>(ws, L.ovf3) + 2;
+  if (L.bucket && !dix) {
+    rp.qbar = at<void>(ws, L.qbar);
+    rp.q_ptr = at<int32_t>(ws, L.q_ptr);
+    rp.q_rows = at<int32_t>(ws, L.q_rows);
+    rp.q_counts = at<uint32_t>(ws, L.q_counts);
+    rp.q_partials = at<uint32_t>(ws, L.q_partials);
+    rp.part = at<int32_t>(ws, L.part);
+    rp.seg_off = at<int64_t>(ws, L.seg_off);
+    rp.cursor = at<unsigned long long>(ws, L.cursor);
+    rp.cand = at<uint64_t>(ws, L.cand);
+    rp.cand_capacity = L.cand_capacity;
+  }
   return cuda_status(launch_rescore(rp, a.dtype, st), "rescore_topk");
 }
 

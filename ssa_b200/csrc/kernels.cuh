@@ -168,6 +168,19 @@ struct RescoreParams {
   int32_t* ovf3_count;         // workspace: units passed from the second warp tier to the third,
   int32_t* ovf3_next;          // the claim counter and
   int32_t* ovf3_list;          // their indices [B * n_q * h_kv]
+  // Bucket-major path (rescore_bucket.cu), used when qbar is set.  Unit
+  // u = (bat * h_kv + h) * n_q + i (row order) indexes the per-unit arrays.
+  void* qbar;                  // [units, 2, d] group-mean query, 16-bit hi row then lo row
+  int32_t* q_ptr;              // [B*h_kv, n_codes+1] code->query-row index of q_codes ...
+  int32_t* q_rows;             // [B*h_kv, n_q*a]     ... (rows ascending within a code)
+  uint32_t* q_counts;          // index-build scratch for that index
+  uint32_t* q_partials;
+  int32_t* part;               // [units, a+1]: offset of each of the unit's buckets in its
+                               // segment; part[a] = the segment's length
+  int64_t* seg_off;            // [units] start of the unit's segment in cand, -1 if none
+  uint64_t* cand;              // candidate ranking keys of all segments (0 = dropped entry)
+  int64_t cand_capacity;       // entries of cand
+  unsigned long long* cursor;  // segment claim counter (zeroed by the launcher)
 };
 
 // Entries of (bat, h) = bh in the index, and the range [lo, hi) of bucket c.
@@ -238,6 +251,13 @@ cudaError_t launch_build_index(const IndexParams& p, cudaStream_t st);
 cudaError_t launch_rescore(const RescoreParams& p, ssa_dtype dt, cudaStream_t st);
 bool rescore_mma_supported(const RescoreParams& p, ssa_dtype dt);
 cudaError_t launch_rescore_mma(const RescoreParams& p, ssa_dtype dt, cudaStream_t st);
+// The bucket-major path: shapes it takes (16-bit, d 64 or 128, b 4, a <= 32,
+// min(top_k, n) <= 512, packed index), and its stages up to the point where
+// the units it could not hold are on the second walking tier's list
+// (ovf2_list / ovf2_count, zeroed by the caller).
+bool rescore_bucket_supported(int d, int a, int b, int k_eff, bool packed_index, ssa_dtype dt);
+template <typename T, int D>
+cudaError_t launch_rescore_bucket(const RescoreParams& p, cudaStream_t st);
 size_t rescore_smem_bytes(int cap, int top_k);
 cudaError_t launch_sparse_attn(const AttnParams& p, ssa_dtype dt, cudaStream_t st);
 bool sparse_attn_mma_supported(const AttnParams& p, ssa_dtype dt);

@@ -28,144 +28,21 @@
 // unit of the list), and its overflow to a third with room for 2048 (2 warps
 // per CTA).  Units beyond that, or with k > 512, go to the CTA-wide path.
 // Queries expected to hold far more candidates than the first tier's room
-// (long sequences only) start in the second tier.
+// (long sequences only) start in the second tier.  Where the bucket-major path
+// (rescore_bucket.cu) applies it replaces the first tier: the units it has no
+// buffer room for start in the second.  The per-unit pieces both paths share
+// are in rescore_unit.cuh.
 #include <cmath>
 
-#include "common.cuh"
-#include "kernels.cuh"
-#include "mma_utils.cuh"
+#include "rescore_unit.cuh"
 
 namespace ssa {
 
 #ifndef SSA_RS_UNITS
 #define SSA_RS_UNITS 4
 #endif
-constexpr int kMaxSel = 512;        // k handled on this path
 constexpr int kBatch = 32;          // candidates per MMA batch (4 n-tiles)
 constexpr int kWalk = 4;            // bucket-walk iterations whose loads are issued together
-
-template <int CAP>
-struct __align__(128) RsMmaSmem {
-  uint64_t keys[CAP];                          // ranking keys of all candidates
-  // kept key indices (CAP int32), then the selected keys (k <= kMaxSel)
-  // (its last 1 KB doubles as the radix-select histogram, and before the walk
-  // as the group-mean query: neither overlaps a live use of sel)
-  uint64_t sel[CAP / 2 > kMaxSel ? CAP / 2 : kMaxSel];
-  int32_t qc[32];
-  int32_t lo[32];
-  int32_t pre[33];
-  uint32_t bitmap[kMaxSel / 32];
-};
-
-// Descending bitonic sort of 32*E keys, blocked layout: key[e] of lane l is
-// at position l*E + e, so the stages with partner distance < E compare within
-// a lane and only log2(32) of every log2(32*E) stages shuffle.  The merge
-// direction of a stage, (position & k2) == 0, depends only on e while
-// k2 < E and only on the lane from k2 = E on, so it is computed once per
-// stage (not per element) and every compare-exchange is one 64-bit compare
-// and two 64-bit selects.  The stage loops from k2 = 2E on stay rolled
-// (run-time distances): the whole network is a few hundred instructions of
-// code, so the warps of a CTA do not evict one another's instructions.
-template <int E>
-__device__ __forceinline__ void cx_desc(uint64_t (&key)[E], int e, int f, bool desc) {
-  const uint64_t x = key[e], y = key[f];
-  const bool sw = (x > y) != desc;           // equal keys: either order
-  key[e] = sw ? y : x;
-  key[f] = sw ? x : y;
-}
-
-template <int E>
-__device__ __forceinline__ void sort_desc_blocked(uint64_t (&key)[E], int lane) {
-  constexpr int N = 32 * E;
-  // k2 < E: within each lane, direction fixed by e
-#pragma unroll
-  for (int k2 = 2; k2 < E; k2 <<= 1)
-#pragma unroll
-    for (int jj = k2 >> 1; jj > 0; jj >>= 1)
-#pragma unroll
-      for (int e = 0; e < E; ++e)
-        if ((e ^ jj) > e) cx_desc<E>(key, e, e ^ jj, (e & k2) == 0);
-  // k2 = E: each lane's E keys in the direction of the lane's parity
-  {
-    const bool desc = (lane & 1) == 0;
-#pragma unroll
-    for (int jj = E >> 1; jj > 0; jj >>= 1)
-#pragma unroll
-      for (int e = 0; e < E; ++e)
-        if ((e ^ jj) > e) cx_desc<E>(key, e, e ^ jj, desc);
-  }
-  const int lk = lane * E;
-#pragma unroll 1
-  for (int k2 = 2 * E; k2 <= N; k2 <<= 1) {
-    const bool desc = (lk & k2) == 0;
-#pragma unroll 1
-    for (int j = k2 >> 1; j >= E; j >>= 1) {       // partner in lane ^ (j / E)
-      const bool keep_max = desc == ((lk & j) == 0);
-#pragma unroll
-      for (int e = 0; e < E; ++e) {
-        const uint64_t other = __shfl_xor_sync(0xffffffffu, key[e], j / E);
-        key[e] = ((key[e] > other) == keep_max) ? key[e] : other;
-      }
-    }
-#pragma unroll
-    for (int jj = E >> 1; jj > 0; jj >>= 1)        // partner in the same lane
-#pragma unroll
-      for (int e = 0; e < E; ++e)
-        if ((e ^ jj) > e) cx_desc<E>(key, e, e ^ jj, desc);
-  }
-}
-
-template <int E>
-__device__ __forceinline__ void sort_and_write(const uint64_t* src, int nsel, int lane, const RescoreParams& p,
-                                               int64_t obase) {
-  uint64_t key[E];
-#pragma unroll
-  for (int e = 0; e < E; ++e) {              // any input order: read conflict-free
-    const int idx = e * 32 + lane;
-    key[e] = idx < nsel ? src[idx] : 0ull;
-  }
-  sort_desc_blocked<E>(key, lane);
-#pragma unroll
-  for (int e = 0; e < E; ++e) {
-    const int idx = lane * E + e;
-    if (idx < nsel) {
-      const int32_t j = static_cast<int32_t>(rank_key_index(key[e]));
-      if (p.index_i64) static_cast<int64_t*>(p.out)[obase + idx] = j;
-      else static_cast<int32_t*>(p.out)[obase + idx] = j;
-    }
-  }
-}
-
-// First index in [l, u) whose key exceeds pos (u if none); keys ascend.  Each
-// round trip to memory loads eight probes that cut the range into nine parts,
-// so a bucket of a few hundred keys takes two or three round trips instead of
-// the eight of a binary search.
-__device__ __forceinline__ int first_above(const int32_t* bk, int l, int u, int pos) {
-  while (u - l > 8) {
-    const int len = u - l;
-    int pr[8], v[8];
-#pragma unroll
-    for (int t = 0; t < 8; ++t) pr[t] = l + ((t + 1) * len) / 9;   // strictly increasing in (l, u)
-#pragma unroll
-    for (int t = 0; t < 8; ++t) v[t] = bk[pr[t]];
-    // the probes <= pos form a prefix: the answer lies after the last of them
-    // and at or before the first probe above pos
-    int nl = l, nu = u;
-#pragma unroll
-    for (int t = 0; t < 8; ++t) nl = v[t] <= pos ? pr[t] + 1 : nl;
-#pragma unroll
-    for (int t = 7; t >= 0; --t) nu = v[t] > pos ? pr[t] : nu;
-    l = nl;
-    u = nu;
-  }
-  int v[8];
-#pragma unroll
-  for (int t = 0; t < 8; ++t) v[t] = l + t < u ? bk[l + t] : INT_MAX;
-  int c = 0;
-#pragma unroll
-  for (int t = 0; t < 8; ++t) c += v[t] <= pos ? 1 : 0;
-  return l + c;
-}
 
 template <typename T, int D, int CAP>
 __device__ __forceinline__ void rescore_mma_unit(const RescoreParams& p, int64_t unit, RsMmaSmem<CAP>& s,
@@ -213,36 +90,8 @@ __device__ __forceinline__ void rescore_mma_unit(const RescoreParams& p, int64_t
   // + 32 / CH, ...); the chunk sums meet in shared memory.
   uint32_t qa[KSTEPS][4];
   {
-    constexpr int CH = D / 8;                     // 8-dim chunks per row
-    constexpr int HP = kWarp / CH;                // heads per pass
-    constexpr int MAXP = 16 / HP;                 // passes for a group of up to 16 heads
-    const T* qrow = static_cast<const T*>(p.q) + bat * p.q_sb + static_cast<int64_t>(i) * p.q_sn +
-                    static_cast<int64_t>(h) * p.group * p.q_sh;
-    const int ch = lane % CH, h0 = lane / CH;
-    float x[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) x[u] = 0.f;
-#pragma unroll
-    for (int ps = 0; ps < MAXP; ++ps) {
-      const int gg = h0 + ps * HP;
-      if (gg < p.group) {
-        float f[8];
-        load8<T>(qrow + static_cast<int64_t>(gg) * p.q_sh + ch * 8, f);
-#pragma unroll
-        for (int u = 0; u < 8; ++u) x[u] += f[u];
-      }
-    }
-#pragma unroll
-    for (int o = CH; o < kWarp; o <<= 1)
-#pragma unroll
-      for (int u = 0; u < 8; ++u) x[u] += __shfl_xor_sync(0xffffffffu, x[u], o);
     float* qs = reinterpret_cast<float*>(hist);      // D floats; sel is free until the walk
-    if (lane < CH) {
-      const float inv_g = 1.0f / static_cast<float>(p.group);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) qs[ch * 8 + u] = p.group != 1 ? x[u] * inv_g : x[u];
-    }
-    __syncwarp();
+    group_mean_smem<T, D>(p, bat, i, h, lane, qs);
 #pragma unroll
     for (int kp = 0; kp < KSTEPS / 2; ++kp) {
       qa[2 * kp][0] = qa[2 * kp][1] = qa[2 * kp][2] = qa[2 * kp][3] = 0u;
@@ -362,112 +211,8 @@ __device__ __forceinline__ void rescore_mma_unit(const RescoreParams& p, int64_t
   }
   __syncwarp();
 
-  // ---- 3. keep the top k: radix select over the 64-bit keys ----
-  const int64_t obase = ((static_cast<int64_t>(bat) * p.n_q + i) * p.h_kv + h) * p.top_k;
-  const uint64_t* src = s.keys;
-  int nsel = count;
-  if (count > k_eff) {
-    uint64_t prefix = 0ull, mask = 0ull;
-    int need = k_eff;
-    for (int shift = 56; shift >= 0; shift -= 8) {
-      for (int b = lane; b < 256; b += kWarp) hist[b] = 0u;
-      __syncwarp();
-      for (int idx = lane; idx < count; idx += kWarp) {
-        const uint64_t kv = s.keys[idx];
-        if ((kv & mask) == prefix) atomicAdd(&hist[(kv >> shift) & 255u], 1u);
-      }
-      __syncwarp();
-      // lane l owns digits 255-8l .. 248-8l (descending)
-      uint32_t cnt[8];
-      uint32_t local = 0;
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        cnt[q] = hist[255 - 8 * lane - q];
-        local += cnt[q];
-      }
-      uint32_t inc = local;
-#pragma unroll
-      for (int o = 1; o < kWarp; o <<= 1) {
-        const uint32_t y = __shfl_up_sync(0xffffffffu, inc, o);
-        if (lane >= o) inc += y;
-      }
-      const uint32_t exc = inc - local;
-      const bool mine = exc < static_cast<uint32_t>(need) && static_cast<uint32_t>(need) <= inc;
-      int dsel = 0;
-      uint32_t above = 0, dcount = 0;
-      if (mine) {
-        uint32_t acc = exc;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          if (dcount == 0 && acc + cnt[q] >= static_cast<uint32_t>(need)) {
-            dsel = 255 - 8 * lane - q;
-            above = acc;
-            dcount = cnt[q];
-          }
-          acc += cnt[q];
-        }
-      }
-      const int src_lane = __ffs(__ballot_sync(0xffffffffu, mine)) - 1;
-      dsel = __shfl_sync(0xffffffffu, dsel, src_lane);
-      above = __shfl_sync(0xffffffffu, above, src_lane);
-      dcount = __shfl_sync(0xffffffffu, dcount, src_lane);
-      prefix |= static_cast<uint64_t>(dsel) << shift;
-      mask |= 0xffull << shift;
-      need -= static_cast<int>(above);
-      if (dcount == static_cast<uint32_t>(need)) break;
-      __syncwarp();
-    }
-    // compact the keys >= prefix (exactly k_eff of them) into sel[]
-    int base = 0;
-    for (int idx0 = 0; idx0 < count; idx0 += kWarp) {
-      const int idx = idx0 + lane;
-      const uint64_t kv = idx < count ? s.keys[idx] : 0ull;
-      const bool take = idx < count && kv >= prefix;
-      const unsigned bal = __ballot_sync(0xffffffffu, take);
-      if (take) s.sel[base + __popc(bal & ((1u << lane) - 1u))] = kv;
-      base += __popc(bal);
-    }
-    __syncwarp();
-    src = s.sel;
-    nsel = k_eff;
-  }
-
-  // ---- 4. sort the selected keys, write them; filler; padding ----
-  // the network for the smallest power of two >= nsel (4 keys a lane for the
-  // early queries of a causal head, which have few candidates)
-  if (nsel <= 32 * 4) sort_and_write<4>(src, nsel, lane, p, obase);
-  else if (nsel <= 32 * 8) sort_and_write<8>(src, nsel, lane, p, obase);
-  else sort_and_write<16>(src, nsel, lane, p, obase);
-  auto put = [&](int slot, int32_t jj) {
-    if (p.index_i64) static_cast<int64_t*>(p.out)[obase + slot] = jj;
-    else static_cast<int32_t*>(p.out)[obase + slot] = jj;
-  };
-  if (count < k_eff) {
-    const int need = k_eff - count;
-    const int words = (k_eff + 31) / 32;
-    if (lane < words) s.bitmap[lane] = 0u;
-    __syncwarp();
-    for (int e = lane; e < count; e += kWarp) {
-      const uint32_t jj = rank_key_index(s.keys[e]);
-      if (jj < static_cast<uint32_t>(k_eff)) atomicOr(&s.bitmap[jj >> 5], 1u << (jj & 31));
-    }
-    __syncwarp();
-    // the lowest `need` free indices, in order: 32 indices per step, ranked
-    // by a ballot (coalesced stores; the loop ends once `need` are placed)
-    int base = 0;
-#pragma unroll 1
-    for (int w0 = 0; w0 < k_eff && base < need; w0 += kWarp) {
-      const int jj = w0 + lane;
-      const bool fr = jj < k_eff && !((s.bitmap[jj >> 5] >> (jj & 31)) & 1u);
-      const unsigned bal = __ballot_sync(0xffffffffu, fr);
-      const int rank = base + __popc(bal & ((1u << lane) - 1u));
-      if (fr && rank < need) put(count + rank, jj);
-      base += __popc(bal);
-    }
-  }
-  for (int e = k_eff + lane; e < p.top_k; e += kWarp) put(e, 0);
-  if (p.cand_counts && lane == 0)
-    p.cand_counts[(static_cast<int64_t>(bat) * p.n_q + i) * p.h_kv + h] = count;
+  select_sort_write<CAP>(p, s, s.keys, count, count, k_eff, lane,
+                         (static_cast<int64_t>(bat) * p.n_q + i) * p.h_kv + h);
 }
 
 // All units (LIST false) or the units of a list (count read on the device;
@@ -560,19 +305,16 @@ static cudaError_t launch_list_tier(Kern kern, int warps, size_t smem, const Res
   return cudaGetLastError();
 }
 
+// Tier 1 of the walking kernel: room for 512 candidates, all units but those
+// expected to need more (which go to tier 2's list first); overflow -> tier
+// 2's list.
 template <typename T, int D>
-static cudaError_t launch_mma_t(const RescoreParams& p, cudaStream_t st) {
-  for (int32_t* z : {p.ovf2_count, p.ovf2_next, p.ovf3_count, p.ovf3_next}) {
-    const cudaError_t e = cudaMemsetAsync(z, 0, sizeof(int32_t), st);
-    if (e != cudaSuccess) return e;
-  }
-  // tier 1: room for 512 candidates, all units but those expected to need
-  // more (which go to tier 2's list first); overflow -> tier 2's list
+static cudaError_t launch_tier1(const RescoreParams& p, cudaStream_t st) {
+  cudaError_t e = cudaSuccess;
   constexpr int U1 = SSA_RS_UNITS, C1 = 512;
   RescoreParams p1 = p;
   p1.tier1_rows = tier1_rows(p, C1);
   const int64_t heads = static_cast<int64_t>(p.batch) * p.h_kv;
-  cudaError_t e = cudaSuccess;
   if (p1.tier1_rows < p.n_q) {
     const int64_t pre = heads * (p.n_q - p1.tier1_rows);
     rescore_prefill_kernel<<<static_cast<unsigned>(cdiv(pre, 256)), 256, 0, st>>>(p.ovf2_list, p.ovf2_count, heads,
@@ -589,6 +331,25 @@ static cudaError_t launch_mma_t(const RescoreParams& p, cudaStream_t st) {
     k1<<<static_cast<unsigned>(cdiv(units1, U1)), U1 * kWarp, smem1, st>>>(p1, nullptr, nullptr, nullptr,
                                                                           p.ovf2_list, p.ovf2_count);
     e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+template <typename T, int D>
+static cudaError_t launch_mma_t(const RescoreParams& p, cudaStream_t st) {
+  for (int32_t* z : {p.ovf2_count, p.ovf2_next, p.ovf3_count, p.ovf3_next}) {
+    const cudaError_t e = cudaMemsetAsync(z, 0, sizeof(int32_t), st);
+    if (e != cudaSuccess) return e;
+  }
+  cudaError_t e = cudaSuccess;
+  if (p.qbar) {
+    // the bucket-major path takes every unit it has room for; the rest go
+    // to tier 2's list
+    e = launch_rescore_bucket<T, D>(p, st);
+    if (e != cudaSuccess) return e;
+  } else {
+    e = launch_tier1<T, D>(p, st);
     if (e != cudaSuccess) return e;
   }
   // tier 2: room for 1024 (4 warps per CTA, warps claiming units from the
