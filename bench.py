@@ -57,11 +57,13 @@ sys.path.insert(0, ROOT)
 METRIC = "SSA fwd tokens/s per GPU (n=32k, k=256, bf16) and % of HBM/tensor roofline"
 UNIT = "tokens/s"
 # kernels of libssa_sm100a.so launched per step (config 3, bf16): route = codebook normalise,
-# codebook tensor-core image, 2x projection, 2x tcgen05 code scoring, index (count, 3x scan,
-# scatter, entry codes), re-score tiers 1, 2 and 3, general overflow pass; attention = 1.
-# (The 4-byte cudaMemsetAsync calls that clear the overflow counters are not kernels and
-# are not counted.)
-LAUNCHES_PER_STEP = 17
+# codebook tensor-core image, 2x projection, 2x tcgen05 code scoring, key index (count, 3x
+# scan, scatter, entry codes), bucket-major re-score (group-mean rows, query index: count,
+# 3x scan, scatter; bucket lengths, bucket tiles, per-query selection), the walking
+# re-score's second and third tiers and the general overflow pass (for the units the
+# bucket path had no room for); attention = 1.  (The cudaMemsetAsync calls that clear the
+# counters are not kernels and are not counted.)
+LAUNCHES_PER_STEP = 25
 # DRAM bytes (read + write) of one sparse-attention launch at config 3, n = 32768,
 # measured by ncu (dram__bytes_read.sum + dram__bytes_write.sum, one pass on this
 # workload; profiles/sparse_attn_mma_config3.txt).  Other n scale by the query rows.

@@ -69,7 +69,8 @@ struct RouteLayout {
 bool bucket_rescore(const SsaRouteArgs& a) {
   const char* env = std::getenv("SSA_RESCORE");
   if (env && std::strcmp(env, "walk") == 0) return false;
-  return ssa::rescore_bucket_supported(a.d, a.a, a.b, std::min(a.top_k, a.n), true, static_cast<ssa_dtype>(a.dtype));
+  return static_cast<int64_t>(a.n_q) * a.a < (1ll << 31) &&
+         ssa::rescore_bucket_supported(a.d, a.a, a.b, std::min(a.top_k, a.n), true, static_cast<ssa_dtype>(a.dtype));
 }
 
 // Candidate-buffer entries a unit is given: twice the larger of k and the

@@ -269,7 +269,8 @@ __global__ void __launch_bounds__(kIndexThreads) index_scatter_kernel(IndexParam
       if (keys[mid] < target) lo = mid + 1; else hi = mid;
     }
     const uint32_t pos = off[static_cast<int64_t>(c) * p.tiles + t] + static_cast<uint32_t>(e - lo);
-    dst[pos] = j0 + static_cast<int32_t>((kv & 0xffffu) / p.b);
+    const int32_t e_tile = static_cast<int32_t>(kv & 0xffffu);
+    dst[pos] = p.store_entry ? j0 * p.b + e_tile : j0 + e_tile / p.b;
   }
 }
 

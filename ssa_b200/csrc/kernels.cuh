@@ -90,6 +90,7 @@ struct IndexParams {
   int64_t k_codes_sb;      // elements between sequences of k_codes (n*h_kv*b when contiguous)
   int batch, n, h_kv, b, n_codes, tile_keys, tiles;
   int64_t chunks;          // scan chunks per (bat, h)
+  int store_entry;         // 0: bucket_keys holds key rows j; 1: entry numbers j * b + slot
 };
 
 constexpr int kIndexSortEntries = 4096;  // entries sorted per tile
@@ -171,8 +172,8 @@ struct RescoreParams {
   // Bucket-major path (rescore_bucket.cu), used when qbar is set.  Unit
   // u = (bat * h_kv + h) * n_q + i (row order) indexes the per-unit arrays.
   void* qbar;                  // [units, 2, d] group-mean query, 16-bit hi row then lo row
-  int32_t* q_ptr;              // [B*h_kv, n_codes+1] code->query-row index of q_codes ...
-  int32_t* q_rows;             // [B*h_kv, n_q*a]     ... (rows ascending within a code)
+  int32_t* q_ptr;              // [B*h_kv, n_codes+1] code->query index of q_codes: entry
+  int32_t* q_rows;             // [B*h_kv, n_q*a] numbers row * a + slot, ascending within a code
   uint32_t* q_counts;          // index-build scratch for that index
   uint32_t* q_partials;
   int32_t* part;               // [units, a+1]: offset of each of the unit's buckets in its

@@ -167,7 +167,7 @@ __global__ void __launch_bounds__(kScoreWarps * kWarp) bucket_score_kernel(Resco
   const int qlo = qptr[c], nq = qptr[c + 1] - qlo;
   const int nk = khi - klo;
   if (nq <= 0 || nk <= 0) return;
-  const int32_t* qrows = p.q_rows + static_cast<int64_t>(bh) * p.n_q * a + qlo;
+  const int32_t* qents = p.q_rows + static_cast<int64_t>(bh) * p.n_q * a + qlo;
   const int32_t* bkeys = bucket_base(p, bh) + klo;
   const int4* bcodes = p.bucket_codes + static_cast<int64_t>(bh) * p.entry_stride + klo;
   const T* kbase = static_cast<const T*>(p.k) + bat * p.k_sb + static_cast<int64_t>(h) * p.k_sh;
@@ -188,62 +188,62 @@ __global__ void __launch_bounds__(kScoreWarps * kWarp) bucket_score_kernel(Resco
     }
     __syncthreads();
 
+    // the query index holds entry numbers e = row * a + t: query row e / a
+    // has code c in its slot t = e % a.  A warp takes 8 entries (rows) at a
+    // time, lane (gid, tig) working on entry gid; the next group's entry
+    // numbers are loaded while the current group is scored.
+    int next_e = warp * 8 + gid < nq ? qents[warp * 8 + gid] : -1;
     for (int g0 = warp * 8; g0 < nq; g0 += kScoreWarps * 8) {
-      // the group's 8 query rows: their codes, the rank t of c among them,
-      // the causal length m of this bucket for them and their segment part
-      const int nrows = min(8, nq - g0);
-      int my_t = -1, my_m = 0;
-      int64_t my_dst = -1;
-      int64_t my_u = -1;
-      for (int r = 0; r < nrows; ++r) {
-        const int qi = qrows[g0 + r];
-        const int64_t u = unit_of(p, bh, qi);
-        const int raw = lane < a ? p.q_codes[((static_cast<int64_t>(bat) * p.n_q + qi) * p.h_kv + h) * a + lane] : -1;
-        s.qc[warp][r][lane] = raw;
-        const unsigned hit = __ballot_sync(0xffffffffu, lane < a && raw == c);
-        if (lane == r) {
-          my_u = u;
-          my_t = hit ? __ffs(hit) - 1 : -1;
+      const int e = next_e;
+      next_e = g0 + kScoreWarps * 8 + gid < nq ? qents[g0 + kScoreWarps * 8 + gid] : -1;
+      const bool in_group = e >= 0;
+      const int qi = in_group ? e / a : 0, row_t = in_group ? e % a : 0;
+      const int64_t row_u = unit_of(p, bh, qi);
+      // the row's codes before slot t (first-match rule), its A fragments,
+      // its segment and the part of it that belongs to this bucket
+      const int32_t* qcodes = p.q_codes + ((static_cast<int64_t>(bat) * p.n_q + qi) * p.h_kv + h) * a;
+#pragma unroll
+      for (int m = 0; m < 8; ++m) {
+        const int t = tig + 4 * m;
+        if (in_group && t < row_t) s.qc[warp][gid][t] = qcodes[t];
+      }
+      uint4 hi4[KP], lo4[KP];
+      {
+        const T* qr = qbar + row_u * 2 * D + 8 * tig;
+#pragma unroll
+        for (int kp = 0; kp < KP; ++kp) {
+          hi4[kp] = in_group ? __ldg(reinterpret_cast<const uint4*>(qr + kp * 32)) : make_uint4(0, 0, 0, 0);
+          lo4[kp] = in_group ? __ldg(reinterpret_cast<const uint4*>(qr + D + kp * 32)) : make_uint4(0, 0, 0, 0);
         }
       }
-      if (lane < nrows && my_t >= 0) {
-        const int64_t off = p.seg_off[my_u];
+      int row_m = 0;
+      int64_t row_dst = 0;
+      if (in_group) {
+        const int64_t off = p.seg_off[row_u];
+        const int32_t* part = p.part + row_u * (a + 1);
+        const int ps = part[row_t];
+        const int pe = part[row_t + 1];
         if (off >= 0) {
-          const int32_t* part = p.part + my_u * (a + 1);
-          const int ps = part[my_t];
-          my_m = part[my_t + 1] - ps;
-          my_dst = off + ps;
+          row_m = pe - ps;
+          row_dst = off + ps;
         }
       }
-      __syncwarp();
-      int mmax = my_m;
+      __syncwarp();                                         // s.qc rows are complete
+      int mmax = row_m;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) mmax = max(mmax, __shfl_xor_sync(0xffffffffu, mmax, o));
       if (mmax <= k0) continue;                             // every row's keys end before this chunk
-      // lane (gid, tig) works on row gid
-      const int row_t = __shfl_sync(0xffffffffu, my_t, gid);
-      const int row_m = __shfl_sync(0xffffffffu, my_m, gid);
-      const int64_t row_dst = __shfl_sync(0xffffffffu, my_dst, gid);
-      const int64_t row_u = __shfl_sync(0xffffffffu, my_u, gid);
-      const bool live = gid < nrows && row_m > k0;
+      const bool live = row_m > k0;
       uint32_t qa[2 * KP][4];
-      {
-        uint4 hi4[KP], lo4[KP];
-        const T* qr = qbar + (live ? row_u : 0) * 2 * D + 8 * tig;
 #pragma unroll
-        for (int kp = 0; kp < KP; ++kp) {
-          hi4[kp] = live ? __ldg(reinterpret_cast<const uint4*>(qr + kp * 32)) : make_uint4(0, 0, 0, 0);
-          lo4[kp] = live ? __ldg(reinterpret_cast<const uint4*>(qr + D + kp * 32)) : make_uint4(0, 0, 0, 0);
-        }
-#pragma unroll
-        for (int kp = 0; kp < KP; ++kp) {
-          qa[2 * kp][0] = hi4[kp].x; qa[2 * kp][1] = lo4[kp].x; qa[2 * kp][2] = hi4[kp].y; qa[2 * kp][3] = lo4[kp].y;
-          qa[2 * kp + 1][0] = hi4[kp].z; qa[2 * kp + 1][1] = lo4[kp].z;
-          qa[2 * kp + 1][2] = hi4[kp].w; qa[2 * kp + 1][3] = lo4[kp].w;
-        }
+      for (int kp = 0; kp < KP; ++kp) {
+        if (!live) hi4[kp] = lo4[kp] = make_uint4(0, 0, 0, 0);
+        qa[2 * kp][0] = hi4[kp].x; qa[2 * kp][1] = lo4[kp].x; qa[2 * kp][2] = hi4[kp].y; qa[2 * kp][3] = lo4[kp].y;
+        qa[2 * kp + 1][0] = hi4[kp].z; qa[2 * kp + 1][1] = lo4[kp].z;
+        qa[2 * kp + 1][2] = hi4[kp].w; qa[2 * kp + 1][3] = lo4[kp].w;
       }
       const int kend = min(kn, mmax - k0);                  // keys of this chunk some row needs
-      uint64_t* dst = p.cand + (live ? row_dst : 0);
+      uint64_t* dst = p.cand + row_dst;
       const int32_t* qcr = s.qc[warp][gid];
       for (int nt = 0; nt * 8 < kend; ++nt) {
         const int kr = nt * 8 + gid;                        // B: key row kr of the chunk
@@ -368,6 +368,7 @@ cudaError_t launch_rescore_bucket(const RescoreParams& p, cudaStream_t st) {
   ip.tile_keys = index_tile_keys(p.a);
   ip.tiles = static_cast<int>(cdiv(p.n_q, ip.tile_keys));
   ip.chunks = cdiv(static_cast<int64_t>(p.n_codes) * ip.tiles, kScanChunk);
+  ip.store_entry = 1;
   e = launch_build_index(ip, st);
   if (e != cudaSuccess) return e;
   constexpr int per_cta = kLocateWarps * kLocateUnits;
