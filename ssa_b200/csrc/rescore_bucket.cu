@@ -145,9 +145,16 @@ template <int D>
 struct BucketSmem {
   uint4 krow[kKeysPerChunk * D / 8];             // key rows, 16-byte chunks XOR-swizzled by row
   int4 kcode[kKeysPerChunk];                     // the b = 4 codes of each key
+  uint64_t ksig[kKeysPerChunk];                  // code_bits of each key's other codes
   int32_t kidx[kKeysPerChunk];                   // key positions
-  int32_t qc[kScoreWarps][8][32];                // codes of each warp's 8 queries
+  int32_t qc[kScoreWarps][8][33];                // codes of each warp's 8 queries (padded rows)
 };
+
+// One bit per code (code mod 64): if the bits of a key's codes other than the
+// bucket's and the bits of a query's codes before slot t have nothing in
+// common, the two share no code before t and the first-match rule keeps the
+// key; otherwise the codes are compared exactly.
+__device__ __forceinline__ uint64_t code_bit(int c) { return 1ull << (static_cast<unsigned>(c) & 63u); }
 
 template <typename T, int D>
 __global__ void __launch_bounds__(kScoreWarps * kWarp) bucket_score_kernel(RescoreParams p) {
@@ -178,7 +185,10 @@ __global__ void __launch_bounds__(kScoreWarps * kWarp) bucket_score_kernel(Resco
     __syncthreads();                                        // the previous chunk is no longer read
     for (int r = threadIdx.x; r < kn; r += blockDim.x) {
       s.kidx[r] = bkeys[k0 + r];
-      s.kcode[r] = bcodes[k0 + r];
+      const int4 c4 = bcodes[k0 + r];
+      s.kcode[r] = c4;
+      s.ksig[r] = (c4.x != c ? code_bit(c4.x) : 0ull) | (c4.y != c ? code_bit(c4.y) : 0ull) |
+                  (c4.z != c ? code_bit(c4.z) : 0ull) | (c4.w != c ? code_bit(c4.w) : 0ull);
     }
     __syncthreads();
     for (int idx = threadIdx.x; idx < kn * CH; idx += blockDim.x) {
@@ -202,11 +212,18 @@ __global__ void __launch_bounds__(kScoreWarps * kWarp) bucket_score_kernel(Resco
       // the row's codes before slot t (first-match rule), its A fragments,
       // its segment and the part of it that belongs to this bucket
       const int32_t* qcodes = p.q_codes + ((static_cast<int64_t>(bat) * p.n_q + qi) * p.h_kv + h) * a;
+      uint64_t row_sig = 0ull;
 #pragma unroll
       for (int m = 0; m < 8; ++m) {
         const int t = tig + 4 * m;
-        if (in_group && t < row_t) s.qc[warp][gid][t] = qcodes[t];
+        if (in_group && t < row_t) {
+          const int raw = qcodes[t];
+          s.qc[warp][gid][t] = raw;
+          row_sig |= code_bit(raw);
+        }
       }
+      row_sig |= __shfl_xor_sync(0xffffffffu, row_sig, 1);
+      row_sig |= __shfl_xor_sync(0xffffffffu, row_sig, 2);
       uint4 hi4[KP], lo4[KP];
       {
         const T* qr = qbar + row_u * 2 * D + 8 * tig;
@@ -261,7 +278,7 @@ __global__ void __launch_bounds__(kScoreWarps * kWarp) bucket_score_kernel(Resco
             const int colg = k0 + col;
             if (col < kn && colg < row_m) {
               bool keep = true;
-              if (row_t > 0) {
+              if (s.ksig[col] & row_sig) {
                 const int4 c4 = s.kcode[col];
                 for (int uu = 0; uu < row_t; ++uu) {
                   const int32_t q = qcr[uu];
@@ -279,11 +296,14 @@ __global__ void __launch_bounds__(kScoreWarps * kWarp) bucket_score_kernel(Resco
 }
 
 // --- 5. per-unit selection -------------------------------------------------------
-template <int CAP>
+// CAP keys of a unit are compacted into shared memory; SEL >= k is the room
+// for the selected ones.
+template <int CAP, int SEL>
 __global__ void __launch_bounds__(kSelectWarps * kWarp) select_kernel(RescoreParams p, int64_t units) {
+  using Smem = RsMmaSmem<CAP, SEL>;
   extern __shared__ __align__(128) unsigned char dyn[];
   const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
-  RsMmaSmem<CAP>& s = reinterpret_cast<RsMmaSmem<CAP>*>(dyn)[warp];
+  Smem& s = reinterpret_cast<Smem*>(dyn)[warp];
   // warps take the units head by head, largest positions (most candidates)
   // first, so that the launch does not end on a tail of heavy units
   const int64_t w = static_cast<int64_t>(blockIdx.x) * kSelectWarps + warp;
@@ -303,33 +323,47 @@ __global__ void __launch_bounds__(kSelectWarps * kWarp) select_kernel(RescorePar
   const uint64_t* seg = p.cand + off;
   const int k_eff = min(p.top_k, p.n);
   const int64_t row = (static_cast<int64_t>(bat) * p.n_q + i) * p.h_kv + h;
+  constexpr int kAhead = 4;                                  // segment loads in flight per lane
   int count = 0;
   if (total > CAP) {
-    for (int idx0 = 0; idx0 < total; idx0 += kWarp) {
-      const int idx = idx0 + lane;
-      count += __popc(__ballot_sync(0xffffffffu, idx < total && seg[idx] != 0ull));
+    for (int idx0 = 0; idx0 < total; idx0 += kAhead * kWarp) {
+      uint64_t kv[kAhead];
+#pragma unroll
+      for (int r = 0; r < kAhead; ++r) {
+        const int idx = idx0 + r * kWarp + lane;
+        kv[r] = idx < total ? seg[idx] : 0ull;
+      }
+#pragma unroll
+      for (int r = 0; r < kAhead; ++r) count += __popc(__ballot_sync(0xffffffffu, kv[r] != 0ull));
     }
     if (count > CAP) {                                       // select straight from the segment
-      select_sort_write<CAP>(p, s, seg, total, count, k_eff, lane, row);
+      select_sort_write(p, s, seg, total, count, k_eff, lane, row);
       return;
     }
     count = 0;
   }
-  for (int idx0 = 0; idx0 < total; idx0 += kWarp) {
-    const int idx = idx0 + lane;
-    const uint64_t kv = idx < total ? seg[idx] : 0ull;
-    const unsigned bal = __ballot_sync(0xffffffffu, kv != 0ull);
-    if (kv != 0ull) s.keys[count + __popc(bal & ((1u << lane) - 1u))] = kv;
-    count += __popc(bal);
+  for (int idx0 = 0; idx0 < total; idx0 += kAhead * kWarp) {
+    uint64_t kv[kAhead];
+#pragma unroll
+    for (int r = 0; r < kAhead; ++r) {
+      const int idx = idx0 + r * kWarp + lane;
+      kv[r] = idx < total ? seg[idx] : 0ull;
+    }
+#pragma unroll
+    for (int r = 0; r < kAhead; ++r) {
+      const unsigned bal = __ballot_sync(0xffffffffu, kv[r] != 0ull);
+      if (kv[r] != 0ull) s.keys[count + __popc(bal & ((1u << lane) - 1u))] = kv[r];
+      count += __popc(bal);
+    }
   }
   __syncwarp();
-  select_sort_write<CAP>(p, s, s.keys, count, count, k_eff, lane, row);
+  select_sort_write(p, s, s.keys, count, count, k_eff, lane, row);
 }
 
-template <int CAP>
+template <int CAP, int SEL>
 cudaError_t launch_select(const RescoreParams& p, int64_t units, cudaStream_t st) {
-  const size_t smem = sizeof(RsMmaSmem<CAP>) * kSelectWarps;
-  auto kern = select_kernel<CAP>;
+  const size_t smem = sizeof(RsMmaSmem<CAP, SEL>) * kSelectWarps;
+  auto kern = select_kernel<CAP, SEL>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   kern<<<static_cast<unsigned>(cdiv(units, kSelectWarps)), kSelectWarps * kWarp, smem, st>>>(p, units);
@@ -383,7 +417,10 @@ cudaError_t launch_rescore_bucket(const RescoreParams& p, cudaStream_t st) {
   bucket_score_kernel<T, D><<<static_cast<unsigned>(buckets), kScoreWarps * kWarp, smem, st>>>(p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  return std::min(p.top_k, p.n) > 256 ? launch_select<1024>(p, units, st) : launch_select<512>(p, units, st);
+  const int k_eff = std::min(p.top_k, p.n);
+  if (k_eff > 256) return launch_select<1024, kMaxSel>(p, units, st);
+  if (k_eff > 128) return launch_select<512, 256>(p, units, st);
+  return launch_select<512, 128>(p, units, st);
 }
 
 template cudaError_t launch_rescore_bucket<__nv_bfloat16, 64>(const RescoreParams&, cudaStream_t);

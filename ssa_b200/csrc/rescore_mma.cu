@@ -211,7 +211,7 @@ __device__ __forceinline__ void rescore_mma_unit(const RescoreParams& p, int64_t
   }
   __syncwarp();
 
-  select_sort_write<CAP>(p, s, s.keys, count, count, k_eff, lane,
+  select_sort_write(p, s, s.keys, count, count, k_eff, lane,
                          (static_cast<int64_t>(bat) * p.n_q + i) * p.h_kv + h);
 }
 

@@ -16,13 +16,17 @@ namespace ssa {
 
 constexpr int kMaxSel = 512;        // k handled on this path
 
-template <int CAP>
+// SEL: room for the selected keys -- k at most; at least CAP/2 where the
+// walking kernel keeps its CAP kept key indices there, at least 128 for the
+// histogram.
+template <int CAP, int SEL = (CAP / 2 > kMaxSel ? CAP / 2 : kMaxSel)>
 struct __align__(128) RsMmaSmem {
+  static_assert(SEL >= 128, "the radix histogram takes the last 1 KB of sel");
   uint64_t keys[CAP];                          // ranking keys of all candidates
-  // kept key indices (CAP int32), then the selected keys (k <= kMaxSel)
+  // kept key indices (CAP int32), then the selected keys (k <= SEL)
   // (its last 1 KB doubles as the radix-select histogram, and before the walk
   // as the group-mean query: neither overlaps a live use of sel)
-  uint64_t sel[CAP / 2 > kMaxSel ? CAP / 2 : kMaxSel];
+  uint64_t sel[SEL];
   int32_t qc[32];
   int32_t lo[32];
   int32_t pre[33];
@@ -186,8 +190,8 @@ __device__ __forceinline__ void group_mean_smem(const RescoreParams& p, int bat,
 // entries may also hold zeros (empty slots, below every real key) -- the
 // global form is used only when count > k, so a zero is never selected and no
 // filler is needed.  The result does not depend on the order of the keys.
-template <int CAP>
-__device__ __forceinline__ void select_sort_write(const RescoreParams& p, RsMmaSmem<CAP>& s, const uint64_t* keys,
+template <int CAP, int SEL>
+__device__ __forceinline__ void select_sort_write(const RescoreParams& p, RsMmaSmem<CAP, SEL>& s, const uint64_t* keys,
                                                   int entries, int count, int k_eff, int lane, int64_t row) {
   uint32_t* hist = reinterpret_cast<uint32_t*>(s.sel) + (sizeof(s.sel) / 4 - 256);
   const int64_t obase = row * p.top_k;
