@@ -68,11 +68,13 @@ LAUNCHES_PER_STEP = 25
 # measured by ncu (dram__bytes_read.sum + dram__bytes_write.sum, one pass on this
 # workload; profiles/sparse_attn_mma_config3.txt).  Other n scale by the query rows.
 ATTN_DRAM_BYTES_N32768 = 920.29e6
-# DRAM bytes of stage 2 (ssa_select_candidates: index count / scatter / entry
-# codes and the re-score tiers) per call at n = 32768: the sum of the ncu
-# dram__bytes_read.sum + dram__bytes_write.sum of its kernels in one step of the
-# bench's own workload (profiles/rescore_mma_config3.txt); tier 1 alone 613.9 MB.
-RESCORE_DRAM_BYTES_N32768 = 745.7e6
+# DRAM bytes of stage 2 (ssa_select_candidates: the code->key index with its
+# entry codes, then the bucket-major re-score: group-mean rows, code->query
+# index, bucket lengths, bucket tiles, selection) per call at n = 32768: the sum
+# of the ncu dram__bytes_read.sum + dram__bytes_write.sum of its kernels in one
+# route call of the bench's workload (profiles/rescore_bucket_config3.txt); the
+# candidate segments (written by the tiles, read by the selection) are 1.1 GB of it.
+RESCORE_DRAM_BYTES_N32768 = 2233e6
 
 
 def parse():
@@ -336,16 +338,21 @@ def stage_rooflines(lib, rargs, q_codes, k_codes, cand, shape, ws, sptr, stream,
     one call, so they cannot be bracketed inside ssa_route):
       stage 1 (keys): ssa_code_assign -- codebook scoring of the n*h_kv keys on
         tensor cores, 2*n*h_kv*N_c*d_s useful flops (plus the projection);
-      stage 2: ssa_select_candidates -- inverted index, candidate union, re-score
-        and top-k; algorithmic bytes per unit C*(4 + 16 + 2*d) + g*d*2 + k*4 with
-        C the unique candidates of the unit (from the route's cand_counts)."""
+      stage 2: ssa_select_candidates -- code->key index, then the bucket-major
+        re-score: group-mean rows, code->query index, bucket tiles writing each
+        query's candidate segment, per-query top-k.  Algorithmic bytes: the q
+        rows once (g*d*2 a unit), the group-mean hi/lo rows written once and read
+        once per code (2*d*2*(1 + a)), every key row staged once per code it holds
+        (b*d*2 a key), 8 bytes a candidate written and read back (16*C, C the
+        unique candidates of the unit from the route's cand_counts), k*4 out."""
     import torch
     from ssa_b200 import _lib as L
 
     n, hkv, g, d = shape.n, shape.h_kv, shape.h_q // shape.h_kv, shape.d
     c_sum = int(cand.sum().item())
     units = n * hkv
-    s2_bytes = c_sum * (4 + 16 + 2 * d) + units * (g * d * 2 + shape.top_k * 4)
+    s2_bytes = (16 * c_sum + units * (g * d * 2 + 2 * d * 2 * (1 + shape.a) + shape.top_k * 4)
+                + n * hkv * shape.b * d * 2)
     s1_flops = 2.0 * n * hkv * shape.n_codes * shape.d_s
 
     def timed(fn):
@@ -375,9 +382,10 @@ def stage_rooflines(lib, rargs, q_codes, k_codes, cand, shape, ws, sptr, stream,
         "stage1_keys": {"call": "ssa_code_assign", "bound": "tensor", "achieved": f1, "peak": tflops,
                         "unit": "TFLOP/s", "frac": f1 / tflops, "peak_kind": peak_kind,
                         "algorithmic_flops": s1_flops, "ms": t1},
-        # stage 2's gathers (key rows of the candidates) are served from L2 like
-        # the attention's: fractions of the DRAM copy peak (ncu DRAM bytes of the
-        # stage's kernels) and of the measured L2 read peak (logical bytes)
+        # stage 2 against the DRAM copy peak (ncu DRAM bytes of the stage's
+        # kernels) and the measured L2 read peak (algorithmic bytes); both
+        # fractions are low: its kernels are bound by dependent loads and
+        # instruction issue (selection sort, radix select), not by bandwidth
         "stage2": {"call": "ssa_select_candidates", "bound": "hbm", "unit": "GB/s", "ms": t2,
                    "achieved": dram2 / (t2 / 1e3) / 1e9, "peak": hbm, "peak_kind": peak_kind,
                    "frac": dram2 / (t2 / 1e3) / 1e9 / hbm, "traffic": dram2,
