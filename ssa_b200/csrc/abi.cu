@@ -91,7 +91,10 @@ int64_t cand_per_unit(const SsaRouteArgs& a) {
   return std::min<int64_t>(static_cast<int64_t>(std::ceil(per)), static_cast<int64_t>(a.n) * a.b);
 }
 
-RouteLayout route_layout(const SsaRouteArgs& a) {
+// `bucket_ok`: false for the decode entry points, which always take the
+// walking re-score (their index has free room after each bucket), so their
+// workspace never holds the bucket path's regions.
+RouteLayout route_layout(const SsaRouteArgs& a, bool bucket_ok = true) {
   RouteLayout L{};
   const int64_t B = a.batch, hk = a.h_kv;
   size_t off = 0;
@@ -116,7 +119,7 @@ RouteLayout route_layout(const SsaRouteArgs& a) {
   L.ovf2 = take((2 + static_cast<size_t>(B * hk) * a.n_q) * 4);  // second-tier count, claim counter, list
   L.ovf3 = take((2 + static_cast<size_t>(B * hk) * a.n_q) * 4);  // third tier, the same
   L.flags = take(4);                                               // index-validation flag
-  L.bucket = a.a >= 1 && bucket_rescore(a);
+  L.bucket = bucket_ok && a.a >= 1 && bucket_rescore(a);
   if (L.bucket) {
     const int64_t units = B * hk * a.n_q;
     const int qtiles = static_cast<int>(ssa::cdiv(a.n_q, ssa::index_tile_keys(a.a)));
@@ -659,7 +662,7 @@ ssa_status ssa_decode_index_build(const SsaRouteArgs* args, const SsaDecodeIndex
   if (index->entry_capacity < need)
     return fail(SSA_ERR_WORKSPACE, "decode index holds %lld slots per (sequence, head); %d keys need %lld",
                 static_cast<long long>(index->entry_capacity), args->n, static_cast<long long>(need));
-  const RouteLayout L = route_layout(*args);
+  const RouteLayout L = route_layout(*args, false);
   if (!workspace || workspace_bytes < L.total)
     return fail(SSA_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", L.total, workspace_bytes);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -699,7 +702,7 @@ ssa_status ssa_decode_route(const SsaRouteArgs* args, const SsaDecodeIndex* inde
   s = check_decode_index(*args, index);
   if (s != SSA_OK) return s;
   if (!args->k_codes) return fail(SSA_ERR_INVALID_ARG, "k_codes (the cached keys' codes) is NULL");
-  const RouteLayout L = route_layout(*args);
+  const RouteLayout L = route_layout(*args, false);
   if (!workspace || workspace_bytes < L.total)
     return fail(SSA_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", L.total, workspace_bytes);
   if (args->batch == 0 || args->n_q == 0) return SSA_OK;
