@@ -34,7 +34,7 @@ namespace ssa {
 
 namespace {
 
-constexpr int kKeysPerChunk = 128;   // key rows staged per bucket pass
+constexpr int kKeysPerChunk = 64;    // key rows staged per bucket pass
 constexpr int kScoreWarps = 4;       // warps of a bucket CTA (8 queries each at a time)
 constexpr int kLocateWarps = 8;      // warps of a locate CTA ...
 constexpr int kLocateUnits = 4;      // ... and the units each handles: one claim per 32 units
@@ -141,25 +141,33 @@ __global__ void __launch_bounds__(kLocateWarps * kWarp) locate_kernel(RescorePar
 }
 
 // --- 4. bucket tiles ----------------------------------------------------------
+// The first-match rule drops a key reached through code c at slot t of a query
+// when one of the query's codes before slot t is also a code of the key.  Per
+// chunk of staged keys, an open-addressed table maps every code the keys hold
+// besides c to the bit set of the keys holding it; a query row ORs the sets of
+// its codes before t and drops exactly the keys in the union.
+constexpr int kTableSlots = 512;                     // >= 2.6x the 3 * 64 codes a chunk inserts
+static_assert(kTableSlots >= 2 * 3 * kKeysPerChunk, "code table load factor");
+
 template <int D>
 struct BucketSmem {
   uint4 krow[kKeysPerChunk * D / 8];             // key rows, 16-byte chunks XOR-swizzled by row
-  int4 kcode[kKeysPerChunk];                     // the b = 4 codes of each key
-  uint64_t ksig[kKeysPerChunk];                  // code_bits of each key's other codes
   int32_t kidx[kKeysPerChunk];                   // key positions
-  int32_t qc[kScoreWarps][8][33];                // codes of each warp's 8 queries (padded rows)
+  int32_t tcode[kTableSlots];                    // code table: code (-1 = empty) ...
+  uint32_t tkeys[kTableSlots][kKeysPerChunk / 32];  // ... and the chunk's keys that hold it
 };
 
-// One bit per code (code mod 64): if the bits of a key's codes other than the
-// bucket's and the bits of a query's codes before slot t have nothing in
-// common, the two share no code before t and the first-match rule keeps the
-// key; otherwise the codes are compared exactly.
-__device__ __forceinline__ uint64_t code_bit(int c) { return 1ull << (static_cast<unsigned>(c) & 63u); }
+__device__ __forceinline__ unsigned code_slot(int code) {
+  return (static_cast<unsigned>(code) * 0x9E3779B1u) >> (32 - 9);
+}
 
 template <typename T, int D>
 __global__ void __launch_bounds__(kScoreWarps * kWarp) bucket_score_kernel(RescoreParams p) {
   constexpr int CH = D / 8;            // 16-byte chunks per row
   constexpr int KP = D / 32;           // pairs of k-steps
+  constexpr int KW = kKeysPerChunk / 32;
+  static_assert(kTableSlots == 512, "code_slot takes 9 bits");
+  static_assert(KW == 2, "the drop set is two words");
   extern __shared__ __align__(128) unsigned char dyn[];
   BucketSmem<D>& s = *reinterpret_cast<BucketSmem<D>*>(dyn);
   if (p.index_bad && *p.index_bad != 0) return;
@@ -183,14 +191,31 @@ __global__ void __launch_bounds__(kScoreWarps * kWarp) bucket_score_kernel(Resco
   for (int k0 = 0; k0 < nk; k0 += kKeysPerChunk) {
     const int kn = min(kKeysPerChunk, nk - k0);
     __syncthreads();                                        // the previous chunk is no longer read
-    for (int r = threadIdx.x; r < kn; r += blockDim.x) {
-      s.kidx[r] = bkeys[k0 + r];
-      const int4 c4 = bcodes[k0 + r];
-      s.kcode[r] = c4;
-      s.ksig[r] = (c4.x != c ? code_bit(c4.x) : 0ull) | (c4.y != c ? code_bit(c4.y) : 0ull) |
-                  (c4.z != c ? code_bit(c4.z) : 0ull) | (c4.w != c ? code_bit(c4.w) : 0ull);
+    for (int slot = threadIdx.x; slot < kTableSlots; slot += blockDim.x) {
+      s.tcode[slot] = -1;
+#pragma unroll
+      for (int w = 0; w < KW; ++w) s.tkeys[slot][w] = 0u;
     }
+    for (int r = threadIdx.x; r < kn; r += blockDim.x) s.kidx[r] = bkeys[k0 + r];
     __syncthreads();
+    // the table: each key's codes other than c (a code outside the codebook
+    // is inserted like any other value; it matches no valid query code)
+    for (int r = threadIdx.x; r < kn; r += blockDim.x) {
+      const int4 c4 = bcodes[k0 + r];
+      const int codes[4] = {c4.x, c4.y, c4.z, c4.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int x = codes[q];
+        if (x == c) continue;
+        unsigned slot = code_slot(x);
+        while (true) {                                      // fewer than half the slots are taken
+          const int prev = atomicCAS(&s.tcode[slot], -1, x);
+          if (prev == -1 || prev == x) break;
+          slot = (slot + 1) & (kTableSlots - 1);
+        }
+        atomicOr(&s.tkeys[slot][r >> 5], 1u << (r & 31));
+      }
+    }
     for (int idx = threadIdx.x; idx < kn * CH; idx += blockDim.x) {
       const int r = idx / CH, ch = idx % CH;
       s.krow[r * CH + (ch ^ (r & 7))] =
@@ -209,21 +234,8 @@ __global__ void __launch_bounds__(kScoreWarps * kWarp) bucket_score_kernel(Resco
       const bool in_group = e >= 0;
       const int qi = in_group ? e / a : 0, row_t = in_group ? e % a : 0;
       const int64_t row_u = unit_of(p, bh, qi);
-      // the row's codes before slot t (first-match rule), its A fragments,
-      // its segment and the part of it that belongs to this bucket
-      const int32_t* qcodes = p.q_codes + ((static_cast<int64_t>(bat) * p.n_q + qi) * p.h_kv + h) * a;
-      uint64_t row_sig = 0ull;
-#pragma unroll
-      for (int m = 0; m < 8; ++m) {
-        const int t = tig + 4 * m;
-        if (in_group && t < row_t) {
-          const int raw = qcodes[t];
-          s.qc[warp][gid][t] = raw;
-          row_sig |= code_bit(raw);
-        }
-      }
-      row_sig |= __shfl_xor_sync(0xffffffffu, row_sig, 1);
-      row_sig |= __shfl_xor_sync(0xffffffffu, row_sig, 2);
+      // the row's A fragments, its segment and the part of it that belongs
+      // to this bucket
       uint4 hi4[KP], lo4[KP];
       {
         const T* qr = qbar + row_u * 2 * D + 8 * tig;
@@ -245,7 +257,33 @@ __global__ void __launch_bounds__(kScoreWarps * kWarp) bucket_score_kernel(Resco
           row_dst = off + ps;
         }
       }
-      __syncwarp();                                         // s.qc rows are complete
+      // the keys of this chunk the row reaches through an earlier code: the
+      // quad looks up the row's codes before slot t, a quarter each
+      uint32_t drop[KW];
+#pragma unroll
+      for (int w = 0; w < KW; ++w) drop[w] = 0u;
+      if (row_m > k0 && row_t > 0) {
+        const int32_t* qcodes = p.q_codes + ((static_cast<int64_t>(bat) * p.n_q + qi) * p.h_kv + h) * a;
+        for (int t = tig; t < row_t; t += 4) {
+          const int x = qcodes[t];
+          unsigned slot = code_slot(x);
+          while (true) {                                    // ends at x or at an empty slot
+            const int tc = s.tcode[slot];
+            if (tc == x) {
+#pragma unroll
+              for (int w = 0; w < KW; ++w) drop[w] |= s.tkeys[slot][w];
+              break;
+            }
+            if (tc == -1) break;
+            slot = (slot + 1) & (kTableSlots - 1);
+          }
+        }
+      }
+#pragma unroll
+      for (int w = 0; w < KW; ++w) {
+        drop[w] |= __shfl_xor_sync(0xffffffffu, drop[w], 1);
+        drop[w] |= __shfl_xor_sync(0xffffffffu, drop[w], 2);
+      }
       int mmax = row_m;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) mmax = max(mmax, __shfl_xor_sync(0xffffffffu, mmax, o));
@@ -261,7 +299,6 @@ __global__ void __launch_bounds__(kScoreWarps * kWarp) bucket_score_kernel(Resco
       }
       const int kend = min(kn, mmax - k0);                  // keys of this chunk some row needs
       uint64_t* dst = p.cand + row_dst;
-      const int32_t* qcr = s.qc[warp][gid];
       for (int nt = 0; nt * 8 < kend; ++nt) {
         const int kr = nt * 8 + gid;                        // B: key row kr of the chunk
         float sc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -273,24 +310,17 @@ __global__ void __launch_bounds__(kScoreWarps * kWarp) bucket_score_kernel(Resco
         }
         if (live) {
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int col = nt * 8 + 2 * tig + e;            // key of the chunk for output column e
+          for (int e2 = 0; e2 < 2; ++e2) {
+            const int col = nt * 8 + 2 * tig + e2;          // key of the chunk for output column e2
             const int colg = k0 + col;
             if (col < kn && colg < row_m) {
-              bool keep = true;
-              if (s.ksig[col] & row_sig) {
-                const int4 c4 = s.kcode[col];
-                for (int uu = 0; uu < row_t; ++uu) {
-                  const int32_t q = qcr[uu];
-                  keep &= (q != c4.x) & (q != c4.y) & (q != c4.z) & (q != c4.w);
-                }
-              }
-              dst[colg] = keep ? rank_key(sc[e] + sc[2 + e], static_cast<uint32_t>(s.kidx[col])) : 0ull;
+              const uint32_t dw = col < 32 ? drop[0] : drop[1];
+              const bool keep = ((dw >> (col & 31)) & 1u) == 0u;
+              dst[colg] = keep ? rank_key(sc[e2] + sc[2 + e2], static_cast<uint32_t>(s.kidx[col])) : 0ull;
             }
           }
         }
       }
-      __syncwarp();                                         // qc rows are rewritten by the next group
     }
   }
 }
