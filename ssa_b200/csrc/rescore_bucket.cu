@@ -67,72 +67,86 @@ __global__ void __launch_bounds__(8 * kWarp) qbar_kernel(RescoreParams p, int64_
 }
 
 // --- 3. bucket lengths and segments -------------------------------------------
-// Lane t < a: the t-th code of the unit, the causal length of its key bucket
-// (0 for a code outside [0, n_codes) -- which also sets SSA_DEVICE_BAD_CODE --
-// and for a repeat of an earlier code, whose keys the first-match rule drops
-// anyway), part[t] = the lengths before it, part[a] = the total.
+// Lane t < a of a unit's lanes: the t-th code of the unit, the causal length of
+// its key bucket (0 for a code outside [0, n_codes) -- which also sets
+// SSA_DEVICE_BAD_CODE -- and for a repeat of an earlier code, whose keys the
+// first-match rule drops anyway), part[t] = the lengths before it, part[a] =
+// the total.  With a <= 16 (HALF) each half-warp takes a unit, so that two
+// units' index searches are in flight together.
+template <bool HALF>
 __global__ void __launch_bounds__(kLocateWarps * kWarp) locate_kernel(RescoreParams p, int64_t units) {
-  __shared__ int totals[kLocateWarps * kLocateUnits];
-  __shared__ long long bases[kLocateWarps * kLocateUnits];
+  constexpr int UPW = HALF ? 2 : 1;                              // units a warp takes at a time
+  constexpr int W = kWarp / UPW;                                 // lanes of a unit
+  constexpr int SLOTS = kLocateWarps * kLocateUnits * UPW;       // units of the CTA: one claim
+  static_assert(SLOTS <= 2 * kWarp, "the claim scans two words a lane");
+  __shared__ int totals[SLOTS];
+  __shared__ long long bases[SLOTS];
   const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+  const int sub = lane / W, sl = lane % W;
   const bool bad_index = p.index_bad && *p.index_bad != 0;
   const int a = p.a;
   for (int r = 0; r < kLocateUnits; ++r) {
-    const int slot = warp * kLocateUnits + r;
-    const int64_t u = (static_cast<int64_t>(blockIdx.x) * kLocateWarps + warp) * kLocateUnits + r;
-    int total = 0;
-    if (u < units && !bad_index) {
-      const int bh = static_cast<int>(u / p.n_q), i = static_cast<int>(u % p.n_q);
-      const int bat = bh / p.h_kv, h = bh % p.h_kv;
-      const int pos = seg_pos(p.seg, i);
-      int len = 0, raw = -1;
-      if (lane < a) raw = p.q_codes[((static_cast<int64_t>(bat) * p.n_q + i) * p.h_kv + h) * a + lane];
-      const unsigned in_a = a >= kWarp ? 0xffffffffu : ((1u << a) - 1u);
-      const unsigned same = __match_any_sync(0xffffffffu, raw) & in_a;
-      if (lane < a) {
-        const bool valid = static_cast<unsigned>(raw) < static_cast<unsigned>(p.n_codes);
-        if (!valid) set_status(p.status, SSA_DEVICE_BAD_CODE);
-        const bool first = (same & ((1u << lane) - 1u)) == 0;
-        if (valid && first) {
-          int lo, hi;
-          bucket_range(p, bh, raw, lo, hi);
-          if (p.causal) hi = first_above(bucket_base(p, bh), lo, hi, pos);
-          len = hi - lo;
-        }
+    const int slot = (warp * kLocateUnits + r) * UPW + sub;
+    const int64_t u = static_cast<int64_t>(blockIdx.x) * SLOTS + slot;
+    const bool live = u < units && !bad_index;
+    const int bh = live ? static_cast<int>(u / p.n_q) : 0, i = live ? static_cast<int>(u % p.n_q) : 0;
+    const int bat = bh / p.h_kv, h = bh % p.h_kv;
+    int len = 0, raw = -1;
+    if (live && sl < a) raw = p.q_codes[((static_cast<int64_t>(bat) * p.n_q + i) * p.h_kv + h) * a + sl];
+    // lanes of the same unit holding the same code value
+    const unsigned long long tag = (static_cast<unsigned long long>(sub) << 32) | static_cast<unsigned>(raw);
+    const unsigned same = __match_any_sync(0xffffffffu, tag);
+    if (live && sl < a) {
+      const bool valid = static_cast<unsigned>(raw) < static_cast<unsigned>(p.n_codes);
+      if (!valid) set_status(p.status, SSA_DEVICE_BAD_CODE);
+      const bool first = (same & ((1u << lane) - 1u)) == 0;     // lower lanes of the unit: slots < t
+      if (valid && first) {
+        int lo, hi;
+        bucket_range(p, bh, raw, lo, hi);
+        if (p.causal) hi = first_above(bucket_base(p, bh), lo, hi, seg_pos(p.seg, i));
+        len = hi - lo;
       }
-      int incl = len;
-#pragma unroll
-      for (int o = 1; o < kWarp; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
-      }
-      int32_t* part = p.part + u * (a + 1);
-      if (lane < a) part[lane] = incl - len;
-      total = __shfl_sync(0xffffffffu, incl, a - 1);
-      if (lane == 0) part[a] = total;
     }
-    if (lane == 0) totals[slot] = total;
+    int incl = len;
+#pragma unroll
+    for (int o = 1; o < W; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o, W);
+      if (sl >= o) incl += y;
+    }
+    const int total = __shfl_sync(0xffffffffu, incl, a - 1, W);
+    if (live) {
+      int32_t* part = p.part + u * (a + 1);
+      if (sl < a) part[sl] = incl - len;
+      if (sl == 0) part[a] = total;
+    }
+    if (sl == 0) totals[slot] = live ? total : 0;
   }
   __syncthreads();
   // one claim for the CTA's units; offsets in unit order within it
   if (warp == 0) {
-    const int v = lane < kLocateWarps * kLocateUnits ? totals[lane] : 0;
-    long long incl = v;
+    const int v0 = lane < SLOTS ? totals[lane] : 0;
+    const int v1 = kWarp + lane < SLOTS ? totals[kWarp + lane] : 0;
+    long long i0 = v0, i1 = v1;
 #pragma unroll
     for (int o = 1; o < kWarp; o <<= 1) {
-      const long long y = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += y;
+      const long long y0 = __shfl_up_sync(0xffffffffu, i0, o);
+      const long long y1 = __shfl_up_sync(0xffffffffu, i1, o);
+      if (lane >= o) {
+        i0 += y0;
+        i1 += y1;
+      }
     }
+    const long long t0 = __shfl_sync(0xffffffffu, i0, kWarp - 1);
     unsigned long long base = 0;
-    if (lane == kWarp - 1) base = atomicAdd(p.cursor, static_cast<unsigned long long>(incl));
+    if (lane == kWarp - 1) base = atomicAdd(p.cursor, static_cast<unsigned long long>(i0 + i1));
     base = __shfl_sync(0xffffffffu, base, kWarp - 1);
-    if (lane < kLocateWarps * kLocateUnits) bases[lane] = static_cast<long long>(base) + (incl - v);
+    if (lane < SLOTS) bases[lane] = static_cast<long long>(base) + (i0 - v0);
+    if (kWarp + lane < SLOTS) bases[kWarp + lane] = static_cast<long long>(base) + t0 + (i1 - v1);
   }
   __syncthreads();
-  if (threadIdx.x < kLocateWarps * kLocateUnits) {
+  if (threadIdx.x < SLOTS) {
     const int slot = threadIdx.x;
-    const int64_t u = (static_cast<int64_t>(blockIdx.x) * kLocateWarps + slot / kLocateUnits) * kLocateUnits +
-                      slot % kLocateUnits;
+    const int64_t u = static_cast<int64_t>(blockIdx.x) * SLOTS + slot;
     if (u < units) {
       const long long off = bases[slot];
       p.seg_off[u] = (!bad_index && off + totals[slot] <= p.cand_capacity) ? off : -1;
@@ -245,6 +259,17 @@ __global__ void __launch_bounds__(kScoreWarps * kWarp) bucket_score_kernel(Resco
           lo4[kp] = in_group ? __ldg(reinterpret_cast<const uint4*>(qr + D + kp * 32)) : make_uint4(0, 0, 0, 0);
         }
       }
+      // the row's codes before slot t (a quarter of them a lane), loaded in
+      // the same round trip as its segment and part
+      int early[8];
+      {
+        const int32_t* qcodes = p.q_codes + ((static_cast<int64_t>(bat) * p.n_q + qi) * p.h_kv + h) * a;
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+          const int t = tig + 4 * m;
+          early[m] = in_group && t < row_t ? qcodes[t] : -1;
+        }
+      }
       int row_m = 0;
       int64_t row_dst = 0;
       if (in_group) {
@@ -263,9 +288,10 @@ __global__ void __launch_bounds__(kScoreWarps * kWarp) bucket_score_kernel(Resco
 #pragma unroll
       for (int w = 0; w < KW; ++w) drop[w] = 0u;
       if (row_m > k0 && row_t > 0) {
-        const int32_t* qcodes = p.q_codes + ((static_cast<int64_t>(bat) * p.n_q + qi) * p.h_kv + h) * a;
-        for (int t = tig; t < row_t; t += 4) {
-          const int x = qcodes[t];
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+          if (tig + 4 * m >= row_t) break;
+          const int x = early[m];
           unsigned slot = code_slot(x);
           while (true) {                                    // ends at x or at an empty slot
             const int tc = s.tcode[slot];
@@ -436,7 +462,10 @@ cudaError_t launch_rescore_bucket(const RescoreParams& p, cudaStream_t st) {
   e = launch_build_index(ip, st);
   if (e != cudaSuccess) return e;
   constexpr int per_cta = kLocateWarps * kLocateUnits;
-  locate_kernel<<<static_cast<unsigned>(cdiv(units, per_cta)), kLocateWarps * kWarp, 0, st>>>(p, units);
+  if (p.a <= kWarp / 2)
+    locate_kernel<true><<<static_cast<unsigned>(cdiv(units, 2 * per_cta)), kLocateWarps * kWarp, 0, st>>>(p, units);
+  else
+    locate_kernel<false><<<static_cast<unsigned>(cdiv(units, per_cta)), kLocateWarps * kWarp, 0, st>>>(p, units);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const size_t smem = sizeof(BucketSmem<D>);
