@@ -176,7 +176,10 @@ __device__ __forceinline__ unsigned code_slot(int code) {
 }
 
 template <typename T, int D>
-__global__ void __launch_bounds__(kScoreWarps * kWarp) bucket_score_kernel(RescoreParams p) {
+#ifndef SSA_BUCKET_MIN_CTAS
+#define SSA_BUCKET_MIN_CTAS 1
+#endif
+__global__ void __launch_bounds__(kScoreWarps * kWarp, SSA_BUCKET_MIN_CTAS) bucket_score_kernel(RescoreParams p) {
   constexpr int CH = D / 8;            // 16-byte chunks per row
   constexpr int KP = D / 32;           // pairs of k-steps
   constexpr int KW = kKeysPerChunk / 32;
