@@ -38,20 +38,20 @@ struct __align__(128) RsMmaSmem {
 // a lane and only log2(32) of every log2(32*E) stages shuffle.  The merge
 // direction of a stage, (position & k2) == 0, depends only on e while
 // k2 < E and only on the lane from k2 = E on, so it is computed once per
-// stage (not per element) and every compare-exchange is one 64-bit compare
-// and two 64-bit selects.  The stage loops from k2 = 2E on stay rolled
-// (run-time distances): the whole network is a few hundred instructions of
-// code, so the warps of a CTA do not evict one another's instructions.
-template <int E>
-__device__ __forceinline__ void cx_desc(uint64_t (&key)[E], int e, int f, bool desc) {
-  const uint64_t x = key[e], y = key[f];
+// stage (not per element) and every compare-exchange is one compare and two
+// selects.  The stage loops from k2 = 2E on stay rolled (run-time distances):
+// the whole network is a few hundred instructions of code, so the warps of a
+// CTA do not evict one another's instructions.
+template <typename K, int E>
+__device__ __forceinline__ void cx_desc(K (&key)[E], int e, int f, bool desc) {
+  const K x = key[e], y = key[f];
   const bool sw = (x > y) != desc;           // equal keys: either order
   key[e] = sw ? y : x;
   key[f] = sw ? x : y;
 }
 
-template <int E>
-__device__ __forceinline__ void sort_desc_blocked(uint64_t (&key)[E], int lane) {
+template <typename K, int E>
+__device__ __forceinline__ void sort_desc_blocked(K (&key)[E], int lane) {
   constexpr int N = 32 * E;
   // k2 < E: within each lane, direction fixed by e
 #pragma unroll
@@ -60,7 +60,7 @@ __device__ __forceinline__ void sort_desc_blocked(uint64_t (&key)[E], int lane) 
     for (int jj = k2 >> 1; jj > 0; jj >>= 1)
 #pragma unroll
       for (int e = 0; e < E; ++e)
-        if ((e ^ jj) > e) cx_desc<E>(key, e, e ^ jj, (e & k2) == 0);
+        if ((e ^ jj) > e) cx_desc<K, E>(key, e, e ^ jj, (e & k2) == 0);
   // k2 = E: each lane's E keys in the direction of the lane's parity
   {
     const bool desc = (lane & 1) == 0;
@@ -68,7 +68,7 @@ __device__ __forceinline__ void sort_desc_blocked(uint64_t (&key)[E], int lane) 
     for (int jj = E >> 1; jj > 0; jj >>= 1)
 #pragma unroll
       for (int e = 0; e < E; ++e)
-        if ((e ^ jj) > e) cx_desc<E>(key, e, e ^ jj, desc);
+        if ((e ^ jj) > e) cx_desc<K, E>(key, e, e ^ jj, desc);
   }
   const int lk = lane * E;
 #pragma unroll 1
@@ -79,7 +79,7 @@ __device__ __forceinline__ void sort_desc_blocked(uint64_t (&key)[E], int lane) 
       const bool keep_max = desc == ((lk & j) == 0);
 #pragma unroll
       for (int e = 0; e < E; ++e) {
-        const uint64_t other = __shfl_xor_sync(0xffffffffu, key[e], j / E);
+        const K other = __shfl_xor_sync(0xffffffffu, key[e], j / E);
         key[e] = ((key[e] > other) == keep_max) ? key[e] : other;
       }
     }
@@ -87,20 +87,57 @@ __device__ __forceinline__ void sort_desc_blocked(uint64_t (&key)[E], int lane) 
     for (int jj = E >> 1; jj > 0; jj >>= 1)        // partner in the same lane
 #pragma unroll
       for (int e = 0; e < E; ++e)
-        if ((e ^ jj) > e) cx_desc<E>(key, e, e ^ jj, desc);
+        if ((e ^ jj) > e) cx_desc<K, E>(key, e, e ^ jj, desc);
   }
 }
 
+// Sort the nsel keys at src (shared memory, any order) descending and write
+// their indices in order at out[obase ..].  The network runs on 32-bit keys:
+// the top bits of each 64-bit ranking key (its score) with the key's slot in
+// src below them, so every compare-exchange is one 32-bit compare and every
+// shuffle one word.  The full keys are then fetched by slot; keys whose top
+// bits are equal form runs in arbitrary order, which an odd-even
+// transposition pass over the full keys puts in order (one or two rounds;
+// it stops when a round swaps nothing, and 32*E rounds sort any input).
 template <int E>
 __device__ __forceinline__ void sort_and_write(const uint64_t* src, int nsel, int lane, const RescoreParams& p,
                                                int64_t obase) {
-  uint64_t key[E];
+  constexpr int SB = E <= 8 ? 8 : 9;          // bits of a slot number: 32 * E <= 2^SB
+  constexpr uint32_t kSlot = (1u << SB) - 1u;
+  static_assert(32 * E <= (1 << SB) && E % 2 == 0 && E >= 4, "slot bits");
+  uint32_t k32[E];
 #pragma unroll
   for (int e = 0; e < E; ++e) {              // any input order: read conflict-free
     const int idx = e * 32 + lane;
-    key[e] = idx < nsel ? src[idx] : 0ull;
+    k32[e] = idx < nsel ? ((static_cast<uint32_t>(src[idx] >> 32) & ~kSlot) | static_cast<uint32_t>(idx)) : 0u;
   }
-  sort_desc_blocked<E>(key, lane);
+  // real keys have a nonzero high word (a float's order key), so padding sorts last
+  sort_desc_blocked<uint32_t, E>(k32, lane);
+  uint64_t key[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) key[e] = lane * E + e < nsel ? src[k32[e] & kSlot] : 0ull;
+#pragma unroll 1
+  for (int round = 0; round < 32 * E; ++round) {
+    bool sw = false;
+#pragma unroll
+    for (int e = 0; e + 1 < E; e += 2)        // pairs (2m, 2m+1): inside the lane
+      if (key[e] < key[e + 1]) {
+        const uint64_t t = key[e]; key[e] = key[e + 1]; key[e + 1] = t; sw = true;
+      }
+#pragma unroll
+    for (int e = 1; e + 1 < E; e += 2)        // pairs (2m+1, 2m+2) inside the lane ...
+      if (key[e] < key[e + 1]) {
+        const uint64_t t = key[e]; key[e] = key[e + 1]; key[e + 1] = t; sw = true;
+      }
+    // ... and across lanes: this lane's last key and the next lane's first
+    const uint64_t next = __shfl_down_sync(0xffffffffu, key[0], 1);
+    const uint64_t prev = __shfl_up_sync(0xffffffffu, key[E - 1], 1);
+    const bool give = lane < kWarp - 1 && key[E - 1] < next;
+    const bool take = lane > 0 && prev < key[0];
+    if (give) key[E - 1] = next;
+    if (take) key[0] = prev;
+    if (!__any_sync(0xffffffffu, sw || give || take)) break;
+  }
 #pragma unroll
   for (int e = 0; e < E; ++e) {
     const int idx = lane * E + e;
