@@ -353,6 +353,9 @@ def stage_rooflines(lib, rargs, q_codes, k_codes, cand, shape, ws, sptr, stream,
     units = n * hkv
     s2_bytes = (16 * c_sum + units * (g * d * 2 + 2 * d * 2 * (1 + shape.a) + shape.top_k * 4)
                 + n * hkv * shape.b * d * 2)
+    # the same stage as the per-query formulation defines its work: every
+    # candidate's key row, id and codes gathered once per query that reaches it
+    walk_bytes = c_sum * (4 + 16 + 2 * d) + units * (g * d * 2 + shape.top_k * 4)
     s1_flops = 2.0 * n * hkv * shape.n_codes * shape.d_s
 
     def timed(fn):
@@ -391,7 +394,12 @@ def stage_rooflines(lib, rargs, q_codes, k_codes, cand, shape, ws, sptr, stream,
                    "frac": dram2 / (t2 / 1e3) / 1e9 / hbm, "traffic": dram2,
                    "l2": {"achieved": s2_bytes / (t2 / 1e3) / 1e9, "peak": l2_peak,
                           "frac": s2_bytes / (t2 / 1e3) / 1e9 / l2_peak, "bytes": s2_bytes},
-                   "logical_bytes": s2_bytes, "mean_unique_candidates": c_sum / units},
+                   "logical_bytes": s2_bytes, "mean_unique_candidates": c_sum / units,
+                   "per_query_equivalent": {
+                       "bytes": walk_bytes, "achieved": walk_bytes / (t2 / 1e3) / 1e9, "unit": "GB/s",
+                       "frac_of_hbm": walk_bytes / (t2 / 1e3) / 1e9 / hbm,
+                       "note": "bytes a per-query re-score gathers (the survey's K3 work); the "
+                               "bucket-major path moves logical_bytes instead"}},
     }
 
 
