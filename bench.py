@@ -97,6 +97,8 @@ def parse():
     p.add_argument("--batch", type=int, default=4, help="config5: sequences per GPU")
     p.add_argument("--folds", type=int, default=4,
                    help="config4: zig-zag passes; each rank holds 2 * folds blocks of the sequence")
+    p.add_argument("--kv-after-qcodes", action="store_true",
+                   help="config4: issue the K and V all-gathers after the query codes")
     return p.parse_args()
 
 
@@ -669,7 +671,8 @@ def config4_timing(args, dev, world, rank, steps, warmup):
 
     def step():
         with torch.no_grad():
-            return shard.sharded_forward(router, ql, kl, vl, causal=True, folds=folds)
+            return shard.sharded_forward(router, ql, kl, vl, causal=True, folds=folds,
+                                         kv_after_query_codes=args.kv_after_qcodes)
 
     for _ in range(warmup):
         step()

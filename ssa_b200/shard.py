@@ -154,7 +154,7 @@ def sharded_forward(router, q_local: torch.Tensor, k_local: torch.Tensor, v_loca
                     group=None, causal: bool = True, scale: Optional[float] = None, folds: int = 1,
                     code_fn: Optional[Callable] = None, query_code_fn: Optional[Callable] = None,
                     index_fn: Optional[Callable] = None, route_fn: Optional[Callable] = None,
-                    attn_fn: Optional[Callable] = None) -> torch.Tensor:
+                    attn_fn: Optional[Callable] = None, kv_after_query_codes: bool = False) -> torch.Tensor:
     """SSA forward of this rank's query rows of one sequence.
 
     ``q_local [B, rows, h_q, d]``, ``k_local``/``v_local [B, rows, h_kv, d]``
@@ -208,9 +208,19 @@ def sharded_forward(router, q_local: torch.Tensor, k_local: torch.Tensor, v_loca
     # neither K nor V.  The query codes need nothing from the other ranks and
     # are computed while all three gathers are in flight; the reordering of
     # the gathered rows runs on a side stream, overlapped with routing.
+    # With kv_after_query_codes the K and V gathers are issued after the query
+    # codes: the codebook-scoring kernel keeps one CTA on every SM for its
+    # whole run, and collective kernels launched before it hold SMs it then
+    # waits for.
     codes_local = code_fn(k_local)
-    gathers = [gather_sequence(x, world, group, async_op=True, folds=folds) for x in (codes_local, k_local, v_local)]
-    q_codes = query_code_fn(q_local)
+    if kv_after_query_codes:
+        gathers = [gather_sequence(codes_local, world, group, async_op=True, folds=folds)]
+        q_codes = query_code_fn(q_local)
+        gathers += [gather_sequence(x, world, group, async_op=True, folds=folds) for x in (k_local, v_local)]
+    else:
+        gathers = [gather_sequence(x, world, group, async_op=True, folds=folds)
+                   for x in (codes_local, k_local, v_local)]
+        q_codes = query_code_fn(q_local)
     (codes, c_ready), (k_full, k_ready), (v_full, v_ready) = (_arrive(w, f, side) for w, f in gathers)
     index = index_fn(_use(codes, c_ready))
     idx = route_fn(q_local, _use(k_full, k_ready), q_codes, codes, index, blocks)

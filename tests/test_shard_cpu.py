@@ -95,7 +95,8 @@ def _worker(rank, world, port, task, result_dir, folds=1):
             code_fn, query_code_fn, route_fn, attn_fn = _oracle_fns(p)
             out = shard.sharded_forward(None, ql, kl, vl, folds=folds, code_fn=code_fn,
                                         query_code_fn=query_code_fn, index_fn=lambda c: None,
-                                        route_fn=route_fn, attn_fn=attn_fn)
+                                        route_fn=route_fn, attn_fn=attn_fn,
+                                        kv_after_query_codes=task == "forward_late_kv")
             want = shard.local_rows(torch.from_numpy(_oracle_full(p))[None], world, rank, folds=folds)
             ok = out.shape == want.shape and torch.allclose(out, want, rtol=0, atol=1e-12)
         with open(os.path.join(result_dir, f"rank{rank}"), "w") as f:
@@ -150,3 +151,8 @@ def test_gather_sequence_round_trip(world, folds, tmp_path):
 @pytest.mark.parametrize("world,folds", [(2, 1), (3, 1), (2, 2)])
 def test_sharded_forward_matches_single_process(world, folds, tmp_path):
     _run(world, "forward", tmp_path, folds)
+
+
+def test_sharded_forward_with_late_kv_gathers(tmp_path):
+    """K and V gathered after the query codes: the same output."""
+    _run(2, "forward_late_kv", tmp_path, 2)
