@@ -176,11 +176,7 @@ __device__ __forceinline__ unsigned code_slot(int code) {
 }
 
 template <typename T, int D>
-#ifdef SSA_BUCKET_MIN_CTAS
-__global__ void __launch_bounds__(kScoreWarps * kWarp, SSA_BUCKET_MIN_CTAS) bucket_score_kernel(RescoreParams p) {
-#else
 __global__ void __launch_bounds__(kScoreWarps * kWarp) bucket_score_kernel(RescoreParams p) {
-#endif
   constexpr int CH = D / 8;            // 16-byte chunks per row
   constexpr int KP = D / 32;           // pairs of k-steps
   constexpr int KW = kKeysPerChunk / 32;
