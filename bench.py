@@ -99,6 +99,8 @@ def parse():
                    help="config4: zig-zag passes; each rank holds 2 * folds blocks of the sequence")
     p.add_argument("--kv-after-qcodes", action="store_true",
                    help="config4: issue the K and V all-gathers after the query codes")
+    p.add_argument("--timeline", action="store_true",
+                   help="config4: after the timed steps, one step with CUDA events between its phases")
     return p.parse_args()
 
 
@@ -669,10 +671,10 @@ def config4_timing(args, dev, world, rank, steps, warmup):
     torch.cuda.empty_cache()
     stream = torch.cuda.current_stream(dev)
 
-    def step():
+    def step(marks=None):
         with torch.no_grad():
             return shard.sharded_forward(router, ql, kl, vl, causal=True, folds=folds,
-                                         kv_after_query_codes=args.kv_after_qcodes)
+                                         kv_after_query_codes=args.kv_after_qcodes, marks=marks)
 
     for _ in range(warmup):
         step()
@@ -695,6 +697,19 @@ def config4_timing(args, dev, world, rank, steps, warmup):
     tt = torch.tensor([e0.elapsed_time(e1)], device=dev)
     dist.all_reduce(tt, op=dist.ReduceOp.MAX)
     ms_step = float(tt.item()) / steps
+    timeline = None
+    if getattr(args, "timeline", False):
+        # one more step, outside the timed region, with events between its
+        # phases; every rank's durations, gathered on rank 0
+        marks = []
+        step(marks)
+        torch.cuda.synchronize(dev)
+        phases = [name for name, _ in marks[1:]]
+        mine = [round(marks[i][1].elapsed_time(marks[i + 1][1]), 3) for i in range(len(marks) - 1)]
+        every = [None] * world
+        dist.all_gather_object(every, mine)
+        timeline = {"phases": phases, "ms_by_rank": every,
+                    "max_ms": [max(r[i] for r in every) for i in range(len(phases))]}
     del ql, kl, vl
     torch.cuda.empty_cache()
     return {"metric": "SSA fwd tokens/s, one n=131072 sequence split over the GPUs (k=512, bf16)",
@@ -705,7 +720,7 @@ def config4_timing(args, dev, world, rank, steps, warmup):
                        "parallelism": f"query-split x{world} ({2 * folds} zig-zag blocks per rank routed and "
                                       "attended in one call each, NCCL all-gather of K, V, codes)",
                        "l2": "inputs 1.6 GB > 126 MB L2, no flush"},
-            "clocks": clk}
+            "clocks": clk, **({"timeline": timeline} if timeline else {})}
 
 
 def run_config4(args):

@@ -154,7 +154,8 @@ def sharded_forward(router, q_local: torch.Tensor, k_local: torch.Tensor, v_loca
                     group=None, causal: bool = True, scale: Optional[float] = None, folds: int = 1,
                     code_fn: Optional[Callable] = None, query_code_fn: Optional[Callable] = None,
                     index_fn: Optional[Callable] = None, route_fn: Optional[Callable] = None,
-                    attn_fn: Optional[Callable] = None, kv_after_query_codes: bool = False) -> torch.Tensor:
+                    attn_fn: Optional[Callable] = None, kv_after_query_codes: bool = False,
+                    marks: Optional[list] = None) -> torch.Tensor:
     """SSA forward of this rank's query rows of one sequence.
 
     ``q_local [B, rows, h_q, d]``, ``k_local``/``v_local [B, rows, h_kv, d]``
@@ -212,7 +213,17 @@ def sharded_forward(router, q_local: torch.Tensor, k_local: torch.Tensor, v_loca
     # codes: the codebook-scoring kernel keeps one CTA on every SM for its
     # whole run, and collective kernels launched before it hold SMs it then
     # waits for.
+    # `marks` (GPU ranks only): a list that receives (phase, CUDA event) pairs
+    # recorded on the current stream at the end of each phase.
+    def mark(name):
+        if marks is not None and side is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record(torch.cuda.current_stream(q_local.device))
+            marks.append((name, ev))
+
+    mark("start")
     codes_local = code_fn(k_local)
+    mark("key codes")
     if kv_after_query_codes:
         gathers = [gather_sequence(codes_local, world, group, async_op=True, folds=folds)]
         q_codes = query_code_fn(q_local)
@@ -221,7 +232,16 @@ def sharded_forward(router, q_local: torch.Tensor, k_local: torch.Tensor, v_loca
         gathers = [gather_sequence(x, world, group, async_op=True, folds=folds)
                    for x in (codes_local, k_local, v_local)]
         q_codes = query_code_fn(q_local)
+    mark("query codes")
     (codes, c_ready), (k_full, k_ready), (v_full, v_ready) = (_arrive(w, f, side) for w, f in gathers)
     index = index_fn(_use(codes, c_ready))
-    idx = route_fn(q_local, _use(k_full, k_ready), q_codes, codes, index, blocks)
-    return attn_fn(q_local, k_full, _use(v_full, v_ready), idx, blocks)
+    mark("codes arrive + index")
+    k_full = _use(k_full, k_ready)
+    mark("K arrives")
+    idx = route_fn(q_local, k_full, q_codes, codes, index, blocks)
+    mark("candidates")
+    v_full = _use(v_full, v_ready)
+    mark("V arrives")
+    out = attn_fn(q_local, k_full, v_full, idx, blocks)
+    mark("attention")
+    return out
