@@ -101,6 +101,9 @@ def parse():
                    help="config4: issue the K and V all-gathers after the query codes")
     p.add_argument("--timeline", action="store_true",
                    help="config4: after the timed steps, one step with CUDA events between its phases")
+    p.add_argument("--emulate", default=None, metavar="RANK/WORLD",
+                   help="config4, one GPU: time the work of rank RANK of WORLD with the gathered tensors "
+                        "already in place (no exchange), by phase and by kernel")
     return p.parse_args()
 
 
@@ -723,11 +726,115 @@ def config4_timing(args, dev, world, rank, steps, warmup):
             "clocks": clk, **({"timeline": timeline} if timeline else {})}
 
 
+def config4_emulation(args, dev):
+    """``--workload config4 --emulate R/W`` on one GPU: the compute of rank
+    ``R`` of a ``W``-rank config-4 forward, with the gathered K, V and key
+    codes already in place, so that the exchange and its interference with
+    the kernels are left out.  The phases are those of
+    ``ssa_b200.shard.sharded_forward`` without the collectives: key codes of
+    the rank's own keys, the rank's query codes, the code->key index of all
+    ``n`` keys, one candidate-selection call and one attention call over the
+    rank's blocks.  Reports the CUDA-event time per step and per phase, and
+    the device time per kernel (torch.profiler over the same steps)."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    import ssa_b200 as ssa
+    from ssa_b200 import ops, shard
+    from ssa_b200 import workloads as W
+
+    rank, world = (int(x) for x in args.emulate.split("/"))
+    shape = W.CONFIG4
+    n = shape.n
+    folds = args.folds
+    t = W.make_inputs(shape, seed=args.seed, dtype=torch.bfloat16, device=dev, planted=False,
+                      generate_on_device=True)
+    router = ssa.CodebookRouter(head_dim=shape.d, route_dim=shape.d_s, num_kv_heads=shape.h_kv,
+                                num_codebook=shape.n_codes, codes_per_key=shape.b, codes_per_query=shape.a,
+                                top_k=shape.top_k).to(dev)
+    with torch.no_grad():
+        router.W_qr.weight.copy_(t["w_qr"])
+        router.W_kr.weight.copy_(t["w_kr"])
+        router.codebook.copy_(t["codebook"])
+    k_full, v_full = t["k"], t["v"]
+    ql, kl = (shard.local_rows(t[x], world, rank, folds=folds) for x in ("q", "k"))
+    del t
+    blocks = shard.zigzag_blocks(n, world, rank, folds)
+    codes_full = router.key_codes(k_full)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(marks=None):
+        def mark(name):
+            if marks is not None:
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record(stream)
+                marks.append((name, ev))
+
+        with torch.no_grad():
+            mark("start")
+            router.key_codes(kl)
+            mark("key codes")
+            q_codes = ops.query_codes(ql, router.W_qr.weight, router.codebook, router.codes_per_query,
+                                      router.num_kv_heads, float(router.temperature))
+            mark("query codes")
+            index = router.key_index(codes_full)
+            mark("index")
+            idx = ops.select_candidates_segments(ql, k_full, q_codes, codes_full, index[0], index[1],
+                                                 router.top_k, True, blocks)
+            mark("candidates")
+            out = ops.sparse_attn_segments(ql, k_full, v_full, idx, math.sqrt(shape.d), True, blocks)
+            mark("attention")
+        return out
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    ssa.check_errors(dev)
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    marks_all = []
+    for _ in range(args.steps):
+        marks = []
+        step(marks)
+        marks_all.append(marks)
+    torch.cuda.synchronize(dev)
+    clk = clocks.stop()
+    ssa.check_errors(dev)
+    phases = [name for name, _ in marks_all[0][1:]]
+    per_phase = [sum(m[i][1].elapsed_time(m[i + 1][1]) for m in marks_all) / args.steps
+                 for i in range(len(phases))]
+    ms_step = sum(m[0][1].elapsed_time(m[-1][1]) for m in marks_all) / args.steps
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(args.steps):
+            step()
+        torch.cuda.synchronize(dev)
+    kernels = {}
+    for e in prof.key_averages():
+        us = getattr(e, "self_device_time_total", None)
+        if us is None:
+            us = e.self_cuda_time_total
+        if us > 0:
+            kernels[e.key] = round(us / 1e3 / args.steps, 3)
+    kernels = dict(sorted(kernels.items(), key=lambda kv: -kv[1]))
+    print(json.dumps({
+        "metric": "config-4 rank work emulated on one GPU (no exchange), ms per step",
+        "emulated_rank": rank, "emulated_world": world, "folds": folds, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
+        "phases": phases, "phase_ms": [round(x, 3) for x in per_phase],
+        "kernel_ms_per_step": kernels, "clocks": clk,
+        "config": {"workload": "config4", **shape.asdict(), "blocks": blocks},
+        "data": "synthetic (seeded on device: Q/K/V ~ N(0,1))"}), flush=True)
+    return 0
+
+
 def run_config4(args):
     """``--workload config4``: the config-4 record alone, as its own line."""
     import torch
     import torch.distributed as dist
 
+    if args.emulate:
+        torch.cuda.set_device(0)
+        return config4_emulation(args, torch.device("cuda", 0))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
