@@ -99,6 +99,8 @@ def parse():
                    help="config4: zig-zag passes; each rank holds 2 * folds blocks of the sequence")
     p.add_argument("--kv-after-qcodes", action="store_true",
                    help="config4: issue the K and V all-gathers after the query codes")
+    p.add_argument("--v-after-qcodes", action="store_true",
+                   help="config4: issue the V all-gather after the query codes (K with the codes)")
     p.add_argument("--timeline", action="store_true",
                    help="config4: after the timed steps, one step with CUDA events between its phases")
     p.add_argument("--emulate", default=None, metavar="RANK/WORLD",
@@ -677,7 +679,8 @@ def config4_timing(args, dev, world, rank, steps, warmup):
     def step(marks=None):
         with torch.no_grad():
             return shard.sharded_forward(router, ql, kl, vl, causal=True, folds=folds,
-                                         kv_after_query_codes=args.kv_after_qcodes, marks=marks)
+                                         kv_after_query_codes=args.kv_after_qcodes,
+                                         v_after_query_codes=args.v_after_qcodes, marks=marks)
 
     for _ in range(warmup):
         step()

@@ -155,7 +155,7 @@ def sharded_forward(router, q_local: torch.Tensor, k_local: torch.Tensor, v_loca
                     code_fn: Optional[Callable] = None, query_code_fn: Optional[Callable] = None,
                     index_fn: Optional[Callable] = None, route_fn: Optional[Callable] = None,
                     attn_fn: Optional[Callable] = None, kv_after_query_codes: bool = False,
-                    marks: Optional[list] = None) -> torch.Tensor:
+                    v_after_query_codes: bool = False, marks: Optional[list] = None) -> torch.Tensor:
     """SSA forward of this rank's query rows of one sequence.
 
     ``q_local [B, rows, h_q, d]``, ``k_local``/``v_local [B, rows, h_kv, d]``
@@ -210,9 +210,10 @@ def sharded_forward(router, q_local: torch.Tensor, k_local: torch.Tensor, v_loca
     # are computed while all three gathers are in flight; the reordering of
     # the gathered rows runs on a side stream, overlapped with routing.
     # With kv_after_query_codes the K and V gathers are issued after the query
-    # codes: the codebook-scoring kernel keeps one CTA on every SM for its
-    # whole run, and collective kernels launched before it hold SMs it then
-    # waits for.
+    # codes (with v_after_query_codes only the V gather): the codebook-scoring
+    # kernel keeps one CTA on every SM for its whole run, and collective
+    # kernels launched before it hold SMs it then waits for; V is read only by
+    # the attention, so its gather can move during the candidate selection.
     # `marks` (GPU ranks only): a list that receives (phase, CUDA event) pairs
     # recorded on the current stream at the end of each phase.
     def mark(name):
@@ -224,10 +225,12 @@ def sharded_forward(router, q_local: torch.Tensor, k_local: torch.Tensor, v_loca
     mark("start")
     codes_local = code_fn(k_local)
     mark("key codes")
-    if kv_after_query_codes:
-        gathers = [gather_sequence(codes_local, world, group, async_op=True, folds=folds)]
+    if kv_after_query_codes or v_after_query_codes:
+        early = (codes_local,) if kv_after_query_codes else (codes_local, k_local)
+        gathers = [gather_sequence(x, world, group, async_op=True, folds=folds) for x in early]
         q_codes = query_code_fn(q_local)
-        gathers += [gather_sequence(x, world, group, async_op=True, folds=folds) for x in (k_local, v_local)]
+        late = (k_local, v_local) if kv_after_query_codes else (v_local,)
+        gathers += [gather_sequence(x, world, group, async_op=True, folds=folds) for x in late]
     else:
         gathers = [gather_sequence(x, world, group, async_op=True, folds=folds)
                    for x in (codes_local, k_local, v_local)]

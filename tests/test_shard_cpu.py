@@ -96,7 +96,8 @@ def _worker(rank, world, port, task, result_dir, folds=1):
             out = shard.sharded_forward(None, ql, kl, vl, folds=folds, code_fn=code_fn,
                                         query_code_fn=query_code_fn, index_fn=lambda c: None,
                                         route_fn=route_fn, attn_fn=attn_fn,
-                                        kv_after_query_codes=task == "forward_late_kv")
+                                        kv_after_query_codes=task == "forward_late_kv",
+                                        v_after_query_codes=task == "forward_late_v")
             want = shard.local_rows(torch.from_numpy(_oracle_full(p))[None], world, rank, folds=folds)
             ok = out.shape == want.shape and torch.allclose(out, want, rtol=0, atol=1e-12)
         with open(os.path.join(result_dir, f"rank{rank}"), "w") as f:
@@ -153,6 +154,7 @@ def test_sharded_forward_matches_single_process(world, folds, tmp_path):
     _run(world, "forward", tmp_path, folds)
 
 
-def test_sharded_forward_with_late_kv_gathers(tmp_path):
-    """K and V gathered after the query codes: the same output."""
-    _run(2, "forward_late_kv", tmp_path, 2)
+@pytest.mark.parametrize("task", ["forward_late_kv", "forward_late_v"])
+def test_sharded_forward_with_late_gathers(task, tmp_path):
+    """K and V (or V alone) gathered after the query codes: the same output."""
+    _run(2, task, tmp_path, 2)
